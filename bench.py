@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark of the NVFP4 hot path on B200s; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attention|quantize]
+                    [--impl ours|reference]
+
+For N > 1 launch one rank per GPU with torch.distributed.run; ranks shard the
+work with no collective on the data path (weak scaling: every rank runs the
+full per-GPU workload) and the reported time is the max over ranks.
+
+Workloads (synthetic data with the shapes and distributions of the named
+configurations; no dataset is read):
+
+* attention -- NVFP4 attention forward, Llama-3-8B shape: B=1, 32 query /
+  8 KV heads, D=128, T=4096, causal, bf16 q/k/v ~ N(0,1) from seed 1.  A
+  step quantizes Q/K/V to NVFP4 and runs the FP4 attention kernel.  Metric:
+  TFLOP/s with the algorithmic causal count 4*B*Hq*T^2*D/2.
+* quantize -- NVFP4 quantize of one bf16 [4096,4096] tensor (N(0,1), seed
+  0, 0.1% of entries x50) with a per-tensor scale amax/(448*6).  Metric:
+  GB/s of algorithmic traffic, 2.5625 B per element (2 B read, 0.5 B codes,
+  1/16 B scales).
+
+L2 (126 MB) is defeated by rotating through input/output buffer sets larger
+than L2 in total, so every step reads HBM.
+
+--impl reference times the reference's own CPU implementation of the path
+(its torch ops, restated op for op in oracle/torch_port.py and pinned to its
+outputs) on the host cores, for the same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 2**20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["attention", "quantize"], default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampling (200 ms) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- workloads
+def quantize_input():
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(4096, 4096, generator=g)
+    idx = torch.randperm(x.numel(), generator=g)[: x.numel() // 1000]
+    x.view(-1)[idx] *= 50
+    return x.bfloat16()
+
+
+class QuantizeWorkload:
+    name = "quantize"
+    metric = "NVFP4 quantize GB/s per B200, % of HBM roofline"
+    unit = "GB/s"
+    dtype = "bf16->nvfp4 (fp32 arithmetic)"
+
+    def __init__(self, dev):
+        from fp4_attn_b200 import _lib
+        self.lib = _lib
+        self.dev = dev
+        x = quantize_input()
+        self.m, self.n = x.shape
+        self.elems = x.numel()
+        self.algo_bytes = self.elems * (2 + 0.5 + 1 / 16)
+        per_set = self.elems * (2 + 0.5 + 1 / 16)
+        self.nsets = max(2, int(2 * L2_BYTES // per_set) + 1)
+        self.x_host = x.pin_memory()
+        self.xs = [x.to(dev) for _ in range(self.nsets)]
+        self.codes = [torch.empty(self.m, self.n // 2, dtype=torch.uint8, device=dev) for _ in range(self.nsets)]
+        self.scales = [torch.empty(self.m, self.n // 16, dtype=torch.uint8, device=dev) for _ in range(self.nsets)]
+        self.g = [torch.empty(1, dtype=torch.float32, device=dev) for _ in range(self.nsets)]
+        self.codes_host = torch.empty(self.m, self.n // 2, dtype=torch.uint8).pin_memory()
+        self.scales_host = torch.empty(self.m, self.n // 16, dtype=torch.uint8).pin_memory()
+        self.stream = torch.cuda.current_stream(dev).cuda_stream
+        self.config = {"workload": "quantize bf16 [4096,4096], per-tensor scale amax/2688, block 16",
+                       "elements": self.elems, "l2": f"rotating {self.nsets} input/output sets (> L2)"}
+
+    def _global(self, i):
+        self.lib.call("fp4q_global_scale", self.xs[i].data_ptr(), 1, 1, self.m, 1, self.n, 0, self.n, 0,
+                      3, 0, 2688.0, self.g[i].data_ptr(), self.stream)
+
+    def _rows(self, i):
+        self.lib.call("fp4q_quantize", self.xs[i].data_ptr(), 1, 1, self.m, 1, self.n, 0, self.n, 0, self.m,
+                      3 | 0x10, 0, 2688.0, self.codes[i].data_ptr(), self.n // 2, self.scales[i].data_ptr(), 0,
+                      self.n // 16, self.g[i].data_ptr(), None, 0, 0, self.stream)
+
+    def step(self, i, ev=None):
+        i %= self.nsets
+        self._global(i)
+        if ev is not None:
+            ev[0].record()
+        self._rows(i)
+        if ev is not None:
+            ev[1].record()
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D input, quantize, D2H codes + scales."""
+        from fp4_attn_b200 import quant
+        i %= self.nsets
+        self.xs[i].copy_(self.x_host, non_blocking=True)
+        t = quant.quantize(self.xs[i], "tensor", 2688.0)
+        self.codes_host.copy_(t.codes, non_blocking=True)
+        self.scales_host.copy_(t.scales, non_blocking=True)
+
+    e2e_h2d = property(lambda self: self.elems * 2)
+    e2e_d2h = property(lambda self: self.elems // 2 + self.elems // 16)
+
+    def value(self, seconds_per_step, world):
+        return world * self.algo_bytes / seconds_per_step / 1e9
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        achieved = self.algo_bytes / kernel_s / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "kernel": "quant_rows_kernel", "achieved": round(achieved, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} copy bandwidth",
+                "algorithmic_bytes_per_launch": self.algo_bytes, "traffic": None}
+
+    # CPU: the reference's torch path restated (oracle/torch_port.py), full tensor.
+    def cpu_sample(self, reps=None):
+        from oracle import torch_port as tp
+        x = quantize_input()
+        one = torch.tensor(1.0)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            amax = x.abs().max().float()
+            g = amax * (one / torch.tensor(2688.0))
+            tp.fused_qdq(x.float() * (one / g), aligned=True, global_sf_max=None) * g
+            n += 1
+            el = time.perf_counter() - t0
+            if (reps and n >= reps) or (not reps and (el > 10.0 or n >= 30)):
+                break
+        return self.algo_bytes * n / el / 1e9, f"full [4096,4096] tensor x{n} (torch ops, fp32)"
+
+
+# ----------------------------------------------------------------- timing
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v, world, dev):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_ours(args, world, rank, local):
+    from fp4_attn_b200 import _lib
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    wl_name = args.workload or default_workload()
+    wl = make_workload(wl_name, dev)
+    peaks, peak_src = measured_peaks()
+    K, W = args.steps, args.warmup
+    for i in range(W):
+        wl.step(i)
+    torch.cuda.synchronize(dev)
+
+    # device-resident timed region: whole steps, plus the dominant kernel alone
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    n0 = _lib.launch_count()
+    with Clocks(local) as clk:
+        start.record()
+        for i in range(K):
+            wl.step(W + i, kev[i])
+        end.record()
+        torch.cuda.synchronize(dev)
+    launches = _lib.launch_count() - n0
+    barrier(world)
+    ms = start.elapsed_time(end)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / K
+    ms_max = max_over_ranks(ms, world, dev)
+    kernel_ms_max = max_over_ranks(kernel_ms, world, dev)
+    sec_per_step = ms_max / 1e3 / K
+
+    # end to end through the public API with host buffers
+    for i in range(2):
+        wl.e2e_step(i)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        wl.e2e_step(i)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    barrier(world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample = wl.cpu_sample()
+        cpu = {"value": round(v, 4), "unit": wl.unit, "cores": torch.get_num_threads(), "kind": "port",
+               "sample": sample}
+
+    line = {
+        "metric": wl.metric, "value": round(wl.value(sec_per_step, world), 3), "unit": wl.unit,
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "data": "synthetic (seeded; shapes/distributions of the named configuration)",
+        "config": dict(wl.config, parallelism=f"{world} independent shard(s), no data-path collective"),
+        "roofline": wl.kernel_roofline(kernel_ms_max / 1e3, peaks, peak_src),
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(wl.value(e2e_ms / 1e3 / K, world), 3), "unit": wl.unit,
+                "h2d_bytes_per_step": wl.e2e_h2d, "d2h_bytes_per_step": wl.e2e_d2h},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU path (torch ops) on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    wl_name = args.workload or default_workload()
+    wl = make_workload(wl_name, None, cpu_only=True)
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        wl.cpu_sample(reps=1)
+    vals = []
+    for _ in range(args.steps):
+        v, sample = wl.cpu_sample(reps=1)
+        vals.append(v)
+    v = statistics.median(vals)
+    line = {
+        "metric": wl.metric, "value": round(v, 5), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": wl.dtype, "data": "synthetic", "config": wl.config, "impl": "reference",
+        "cpu_baseline": {"value": round(v, 5), "unit": wl.unit, "kind": "port", "cores": torch.get_num_threads(),
+                         "sample": sample},
+        "e2e": {"value": round(v, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def default_workload():
+    try:
+        from fp4_attn_b200 import attention  # noqa: F401
+        return "attention"
+    except ImportError:
+        return "quantize"
+
+
+def make_workload(name, dev, cpu_only=False):
+    if name == "quantize":
+        if cpu_only:
+            w = QuantizeWorkload.__new__(QuantizeWorkload)
+            w.elems = 4096 * 4096
+            w.algo_bytes = w.elems * (2 + 0.5 + 1 / 16)
+            w.config = {"workload": "quantize bf16 [4096,4096], per-tensor scale amax/2688, block 16"}
+            return w
+        return QuantizeWorkload(dev)
+    return AttentionWorkload(dev, cpu_only=cpu_only)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        # CPU only: rank 0 runs and prints, other ranks exit without work.
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = init_dist()
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

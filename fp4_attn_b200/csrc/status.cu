@@ -1,0 +1,38 @@
+// status.cu -- per-thread error message storage and library identity.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "status.h"
+
+namespace fp4 {
+
+static thread_local char g_msg[512];
+
+void clear_error() { g_msg[0] = 0; }
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static unsigned long long g_launches = 0;
+
+void count_launch() { __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED); }
+
+int check_launch(const char* what) {
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FP4ATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return FP4ATTN_OK;
+}
+
+}  // namespace fp4
+
+extern "C" const char* fp4attn_last_error(void) { return fp4::g_msg; }
+
+extern "C" int fp4attn_version(void) { return 1; }
+
+extern "C" unsigned long long fp4attn_launch_count(void) { return __atomic_load_n(&fp4::g_launches, __ATOMIC_RELAXED); }

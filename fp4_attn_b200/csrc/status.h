@@ -1,0 +1,19 @@
+// status.h -- error reporting for the C ABI: every entry point returns a
+// status code and keeps a per-thread message for fp4attn_last_error().
+#pragma once
+
+#include <cuda_runtime.h>
+
+#define FP4ATTN_OK 0
+#define FP4ATTN_ERR_ARG 1
+#define FP4ATTN_ERR_CUDA 2
+#define FP4ATTN_ERR_UNSUPPORTED 3
+
+namespace fp4 {
+void clear_error();
+int set_error(int code, const char* fmt, ...);
+// cudaGetLastError() after a launch, turned into a status.
+int check_launch(const char* what);
+// Count one kernel launch of this library (read by fp4attn_launch_count()).
+void count_launch();
+}  // namespace fp4

@@ -1,0 +1,109 @@
+/*
+ * fp4attn.h -- C ABI of libfp4attn.so, the sm_100a NVFP4 quantizer and FP4
+ * attention forward.
+ *
+ * Conventions for every entry point:
+ *   - plain device pointers and sizes; `stream` is a cudaStream_t (NULL = the
+ *     legacy default stream); work is enqueued asynchronously, nothing
+ *     synchronizes;
+ *   - outputs are caller-allocated and come first where the reference put
+ *     them first; nothing is allocated on the device;
+ *   - the return value is FP4ATTN_OK (0) or an error code, with a message
+ *     for the calling thread in fp4attn_last_error().
+ *
+ * Dtype codes: 0 = float32, 1 = bfloat16, 2 = float16.
+ */
+#ifndef FP4ATTN_H
+#define FP4ATTN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FP4ATTN_OK 0
+#define FP4ATTN_ERR_ARG 1
+#define FP4ATTN_ERR_CUDA 2
+#define FP4ATTN_ERR_UNSUPPORTED 3
+
+/* Message for the last failing call on this thread ("" when none). */
+const char* fp4attn_last_error(void);
+int fp4attn_version(void);
+/* Number of kernels this library has launched in this process (all threads). */
+unsigned long long fp4attn_launch_count(void);
+
+/* ------------------------------------------------------------------------
+ * nvfp4sim module functions.  Each replaces one pybind11 binding of
+ * fast_fp4/wrapper.cpp:41-45 (host functions fast_fp4/nvfp4sim.cu:156, 463,
+ * 254, 309, 365) with the same argument order and meaning: `ngroups` groups
+ * of 16 values, ngroups even; codes are 16 E2M1 nibbles per uint64 (element
+ * i in bits 4i..4i+3), scales one E4M3 byte per group.  The reference's
+ * numerics are kept: 1e-10 amax floor, satfinite scale, round-half-away E2M1
+ * encode, and (search variants) the 16-candidate scale search.
+ * ---------------------------------------------------------------------- */
+
+/* nvfp4sim.f32_to_nvf4 (fast_fp4/wrapper.cpp:41, nvfp4sim.cu:156-192). */
+int nvfp4sim_f32_to_nvf4(uint64_t* xq_out, uint8_t* xs_out, const float* x_in, int64_t ngroups, void* stream);
+
+/* nvfp4sim.f32_to_nvf4_nosearch (fast_fp4/wrapper.cpp:42, nvfp4sim.cu:463-499). */
+int nvfp4sim_f32_to_nvf4_nosearch(uint64_t* xq_out, uint8_t* xs_out, const float* x_in, int64_t ngroups,
+                                  void* stream);
+
+/* nvfp4sim.f16_to_nvf4 (fast_fp4/wrapper.cpp:44, nvfp4sim.cu:254-289); x_in holds IEEE halves. */
+int nvfp4sim_f16_to_nvf4(uint64_t* xq_out, uint8_t* xs_out, const uint16_t* x_in, int64_t ngroups, void* stream);
+
+/* nvfp4sim.nvf4_to_f32 (fast_fp4/wrapper.cpp:43, nvfp4sim.cu:309-344). */
+int nvfp4sim_nvf4_to_f32(float* x_out, const uint64_t* xq_in, const uint8_t* xs_in, int64_t ngroups, void* stream);
+
+/* nvfp4sim.nvf4_to_f16 (fast_fp4/wrapper.cpp:45, nvfp4sim.cu:365-400). */
+int nvfp4sim_nvf4_to_f16(uint16_t* x_out, const uint64_t* xq_in, const uint8_t* xs_in, int64_t ngroups,
+                         void* stream);
+
+/* ------------------------------------------------------------------------
+ * fp4q_quantize: block-16 NVFP4 quantize and (optionally) dequantize,
+ * bit-exact to FP4Quantizer.single_nvfp4_quant_dequant_fused
+ * (fp4_quant_utils.py:112-172), which it replaces, together with the torch
+ * glue of single_nvfp4 (fp4_quant_utils.py:336-341).
+ *
+ * Input: logical matrix with row (b, t) and column c = h*D + d, element at
+ * x[b*sB + t*sT + h*sH + d] (element strides; d contiguous).  A plain 2-D
+ * [m, n] tensor is B=1, T=m, H=1, D=n, sT=n.  Columns are padded with zeros
+ * to a multiple of 16 (fp4_quant_utils.py:126-130).
+ *
+ * gmode: 0 none (global_sf_max=None), 1 row (global_scale_aligned=True:
+ *   g = rowmax|x|, not divided by global_sf_max), 2 column (aligned=False:
+ *   g = colmax|x| * recip(global_sf_max); needs H == 1), 3 tensor
+ *   (g = max|x| * recip(global_sf_max), then the row-mode formulas).
+ * arith: the dequant dtype whose arithmetic is reproduced (0/1/2).
+ *
+ * Outputs (each optional, NULL to skip), output row index o = b*T_pad + t;
+ * rows with t >= T are written as zeros:
+ *   codes  [o][codes_ld] bytes, element 2k in the low nibble of byte k;
+ *   scales E4M3 bytes; scale_layout 0: linear [o][scales_ld];
+ *          scale_layout 1: tcgen05 block-scaled MMA atoms (128 rows x 4
+ *          blocks, 512 bytes, k-fastest), scales_ld = blocks-per-row / 4
+ *          rounded up;
+ *   g      row: [B*T_pad]; column: [npad]; tensor: [1] (in/out workspace of
+ *          the reduction; required when gmode != 0);
+ *   out    dequantized values [o][out_ld] in out_dtype.
+ * gmode | 0x10 (column and tensor modes): g already holds the global
+ *   scale(s) (from fp4q_global_scale or a calibration), skip the reduction.
+ * ---------------------------------------------------------------------- */
+int fp4q_quantize(const void* x, int in_dtype, int B, int T, int H, int D, int64_t sB, int64_t sT, int64_t sH,
+                  int T_pad, int gmode, int arith, float global_sf_max, uint8_t* codes, int64_t codes_ld,
+                  uint8_t* scales, int scale_layout, int64_t scales_ld, float* g, void* out, int out_dtype,
+                  int64_t out_ld, void* stream);
+
+/* The global-scale reduction of fp4q_quantize alone (gmode 2: column, 3:
+ * tensor): g = max|x| * recip(global_sf_max) in the dequant dtype, written to
+ * g ([npad] or [1]).  Same input description as fp4q_quantize.  Replaces the
+ * torch.max/abs/get_reciprocal steps of fp4_quant_utils.py:135-139. */
+int fp4q_global_scale(const void* x, int in_dtype, int B, int T, int H, int D, int64_t sB, int64_t sT, int64_t sH,
+                      int gmode, int arith, float global_sf_max, float* g, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP4ATTN_H */

@@ -1,0 +1,62 @@
+"""The C ABI: the library loads and exports every entry point include/fp4attn.h declares.
+
+CPU-only: argument validation is checked on calls that are rejected before
+any CUDA work is issued.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "fp4attn.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^[A-Za-z_][\w \*]*?\b(\w+)\s*\(", text, flags=re.M)) - {"defined"})
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for n in ("fp4q_quantize", "nvfp4sim_f32_to_nvf4", "nvfp4sim_nvf4_to_f16", "fp4attn_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from fp4_attn_b200 import _lib
+    L = _lib.load()
+    for n in declared_functions():
+        assert hasattr(L, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_version_and_error_string():
+    from fp4_attn_b200 import _lib
+    L = _lib.load()
+    assert L.fp4attn_version() == 1
+    assert isinstance(L.fp4attn_last_error(), bytes)
+
+
+def test_argument_errors_are_codes_not_aborts():
+    """Odd group counts and null pointers come back as FP4ATTN_ERR_ARG with a message."""
+    from fp4_attn_b200 import _lib
+    L = _lib.load()
+    assert L.nvfp4sim_f32_to_nvf4(None, None, None, 3, None) == 1
+    assert b"even" in L.fp4attn_last_error()
+    assert L.nvfp4sim_nvf4_to_f32(None, None, None, 4, None) == 1
+    assert b"null" in L.fp4attn_last_error()
+    assert L.fp4q_quantize(None, 1, 1, 4, 1, 16, 0, 16, 0, 4, 1, 0, 1536.0, None, 0, None, 0, 0, None, None, 0, 0,
+                           None) == 1
+    assert L.fp4q_quantize(ctypes.c_void_p(16), 1, 1, 4, 1, 16, 0, 16, 0, 4, 1, 0, 1536.0, None, 0, None, 0, 0,
+                           None, None, 0, 0, None) == 1
+    assert b"g buffer" in L.fp4attn_last_error()
+
+
+def test_python_api_refuses_cpu_tensors():
+    import torch
+    from fp4_attn_b200 import FP4Quantizer
+    with pytest.raises(RuntimeError, match="CUDA"):
+        FP4Quantizer().single_nvfp4(torch.randn(4, 16))

@@ -66,54 +66,62 @@ def measured_peaks():
 
 # ----------------------------------------------------------------- clocks
 class Clocks:
-    """nvidia-smi sampling (200 ms) during the timed region."""
+    """SM clock and throttle reasons sampled through NVML (a polling thread,
+    ~5 ms period) while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
+    def __init__(self, dev):
+        self.dev = dev
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = False
+        self._thread = None
+
+    def _handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.dev)
+        dom, bus, dv = (getattr(props, a, None) for a in ("pci_domain_id", "pci_bus_id", "pci_device_id"))
+        if all(isinstance(v, int) for v in (dom, bus, dv)):
+            # torch reports the PCI location as integers; NVML wants "dddddddd:bb:dd.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dv:02x}.0")
+        return pynvml.nvmlDeviceGetHandleByIndex(self.dev.index or 0)
+
+    def _run(self, h):
+        import pynvml
+        while not self._stop:
+            try:
+                self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                self.reasons |= pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception:
+                pass
+            time.sleep(0.005)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            h = self._handle()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._thread = threading.Thread(target=self._run, args=(h,), daemon=True)
+            self._thread.start()
+            time.sleep(0.02)
+        except Exception:
+            self._thread = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        names = sorted(v for k, v in self.REASONS.items() if self.reasons & k)
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples), "source": "nvml"}
 
 
 # ------------------------------------------------------------- workloads
@@ -210,6 +218,99 @@ class QuantizeWorkload:
         return self.algo_bytes * n / el / 1e9, f"full [4096,4096] tensor x{n} (torch ops, fp32)"
 
 
+def attention_inputs():
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, 32, 4096, 128, generator=g).bfloat16()
+    k = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
+    v = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
+    return q, k, v
+
+
+class AttentionWorkload:
+    name = "attention"
+    metric = "NVFP4 attention forward TFLOP/s per B200, % of dense FP4 tensor peak"
+    unit = "TFLOP/s"
+    dtype = "nvfp4 QK^T (tcgen05 mxf4nvf4) + fp16-exact Phat x Vhat (tcgen05 f16), fp32 accumulate"
+    B, Hq, Hkv, T, D = 1, 32, 8, 4096, 128
+
+    def __init__(self, dev, cpu_only=False):
+        self.flops = 4 * self.B * self.Hq * self.T * self.T * self.D / 2  # causal, algorithmic
+        self.config = {"workload": "NVFP4 attention fwd, Llama-3-8B shape: B=1, Hq=32, Hkv=8, D=128, T=4096, "
+                                   "causal, single-slice Q/P quantization",
+                       "flops_per_step": self.flops}
+        if cpu_only:
+            return
+        from fp4_attn_b200 import attention as A
+        self.A = A
+        self.dev = dev
+        q, k, v = attention_inputs()
+        self.host = [t.pin_memory() for t in (q, k, v)]
+        per_set = sum(t.numel() * 2 for t in (q, k, v))
+        self.nsets = max(2, int(2 * L2_BYTES // per_set) + 1)
+        self.sets = [tuple(t.to(dev) for t in (q, k, v)) for _ in range(self.nsets)]
+        self.ws = [A.AttentionWorkspace(self.B, self.Hq, self.Hkv, self.T, self.D, dev) for _ in range(self.nsets)]
+        self.out = [torch.empty(self.B, self.T, self.Hq, self.D, device=dev) for _ in range(self.nsets)]
+        self.out_host = torch.empty(self.B, self.T, self.Hq, self.D).pin_memory()
+        self.config["l2"] = f"rotating {self.nsets} input sets (> L2)"
+
+    def step(self, i, ev=None):
+        from fp4_attn_b200 import _lib
+        i %= self.nsets
+        q, k, v = self.sets[i]
+        ws = self.ws[i]
+        A = self.A
+        A.quantize_qk(q, ws.qc, ws.qs, ws.gq, ws.Tp)
+        A.quantize_qk(k, ws.kc, ws.ks, ws.gk, ws.Tp)
+        A.prepare_v(v, ws.vhi, ws.vlo, ws.Tp)
+        if ev is not None:
+            ev[0].record()
+        _lib.call("fp4attn_fwd_packed", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), ws.kc.data_ptr(),
+                  ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), self.out[i].data_ptr(),
+                  self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, 1, self.D ** -0.5, 0, _lib.stream_of(q))
+        if ev is not None:
+            ev[1].record()
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D q/k/v, fp4_attention_fwd, D2H the output."""
+        i %= self.nsets
+        q, k, v = self.sets[i]
+        for d, h in zip((q, k, v), self.host):
+            d.copy_(h, non_blocking=True)
+        o = self.A.fp4_attention_fwd(q, k, v, causal=True, workspace=self.ws[i], out=self.out[i])
+        self.out_host.copy_(o, non_blocking=True)
+
+    e2e_h2d = property(lambda self: sum(t.numel() * 2 for t in self.host))
+    e2e_d2h = property(lambda self: self.out_host.numel() * 4)
+
+    def value(self, seconds_per_step, world):
+        return world * self.flops / seconds_per_step / 1e12
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        achieved = self.flops / kernel_s / 1e12
+        peak = 4 * peaks["bf16_tflops"]
+        return {"bound": "tensor", "kernel": "fp4_attn_kernel", "achieved": round(achieved, 1), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
+                "frac_of_nominal_fp4": round(achieved / 9000.0, 4),
+                "algorithmic_flops_per_launch": self.flops, "traffic": None}
+
+    def cpu_sample(self, reps=None):
+        """The reference's CPU path (torch ops) on one KV-head group (4 of 32 query heads)."""
+        from oracle import torch_port as tp
+        q, k, v = attention_inputs()
+        q, k, v = q[:, :4], k[:, :1], v[:, :1]
+        flops = 4 * 4 * self.T * self.T * self.D / 2
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            tp.attention(q, k, v, causal=True)
+            n += 1
+            el = time.perf_counter() - t0
+            if (reps and n >= reps) or (not reps and (el > 10.0 or n >= 5)):
+                break
+        return flops * n / el / 1e12, f"1 of 8 KV-head groups (4 query heads, all 4096 rows) x{n}, torch ops fp32"
+
+
 # ----------------------------------------------------------------- timing
 def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -254,7 +355,7 @@ def run_ours(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize(dev)
     n0 = _lib.launch_count()
-    with Clocks(local) as clk:
+    with Clocks(dev) as clk:
         start.record()
         for i in range(K):
             wl.step(W + i, kev[i])
@@ -331,11 +432,7 @@ def run_reference(args, world, rank):
 
 
 def default_workload():
-    try:
-        from fp4_attn_b200 import attention  # noqa: F401
-        return "attention"
-    except ImportError:
-        return "quantize"
+    return "attention"
 
 
 def make_workload(name, dev, cpu_only=False):

@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -22,7 +23,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
           "-I", CSRC, "-I", os.path.join(ROOT, "include")]
 # Files whose arithmetic must round exactly like the reference: no FMA contraction.
-EXACT = {"quant.cu", "nvfp4sim_compat.cu"}
+EXACT = {"quant.cu", "quant_f32.cu", "quant_bf16.cu", "quant_f16.cu", "nvfp4sim_compat.cu"}
 
 
 def _nvcc() -> str:
@@ -43,7 +44,7 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
         glob.glob(os.path.join(ROOT, "include", "*.h"))
     hdr_time = _newest(hdrs) if hdrs else 0.0
     nvcc = _nvcc()
-    objs = []
+    objs, jobs = [], []
     for s in srcs:
         o = os.path.join(OBJ, os.path.basename(s)[:-3] + ".o")
         objs.append(o)
@@ -53,9 +54,14 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
                *(extra or []), "-c", s, "-o", o]
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        jobs.append(cmd)
+    with ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
+        for r in ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), jobs):
+            if r.returncode != 0:
+                sys.stderr.write(r.stdout + r.stderr)
+                raise RuntimeError("nvcc failed: " + " ".join(r.args[-3:]))
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < _newest(objs):
-        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

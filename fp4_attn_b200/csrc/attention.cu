@@ -1,0 +1,616 @@
+// attention.cu -- NVFP4 attention forward on sm_100a (tcgen05 + TMA + TMEM).
+//
+// Computes what the reference's patched attention computes
+// (llama_patch.py:57-105 after the Q/K/V fake-quant of llama_patch.py:167-196):
+//
+//   S = (Qhat Khat^T) * scaling (+ causal mask);  P = softmax(S)
+//   Phat = NVFP4 fake-quant of P, per query row (row global scale = row max
+//          of P, blocks of 16 along keys)              (llama_patch.py:81-99)
+//   O = Phat Vhat                                       (llama_patch.py:102)
+//
+// with Qhat/Khat NVFP4 along head_dim under a per-token global scale and
+// Vhat NVFP4 along tokens under a per-token global scale
+// (single_nvfp4(v2d.T, global_scale_aligned=False), llama_patch.py:196).
+//
+// Numerics.  P's block scales depend on P relative to the row maximum, so
+// each 128-query tile runs two passes over its keys: pass 1 computes S with
+// FP4 tensor-core MMAs and keeps the exact row maximum; pass 2 recomputes S,
+// forms e = exp2((S - max) * log2 e) (the reference's P / rowmax(P)), sums
+// e for the softmax denominator, quantizes e to E2M1 codes with an E4M3
+// scale per 16 keys exactly as the reference's quantizer does, and writes
+// Phat = code * scale (exact in fp16) into TMEM.  The reference's per-token
+// V global scale varies along PV's reduction axis, so PV cannot use
+// block-scaled FP4 without changing the result; Vhat is prepared once as
+// two fp16 planes (hi + lo, 22 significant bits, fp4attn_prepare_v) and PV
+// runs as two kind::f16 MMAs with A = Phat read from TMEM.  O = acc / sum.
+//
+// Schedule.  A work unit is (batch, query head, 128-query tile); persistent
+// CTAs take units longest-first (causal cost grows with the tile index).
+// Warp 0 issues TMA, warp 1 issues tcgen05 MMAs, warps 4-7 and 8-11 are two
+// softmax warpgroups that take alternate 128-key tiles (S double-buffered in
+// TMEM), warps 2-3 are idle.  Every wait is bounded (sm100.cuh).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+#include "status.h"
+#include "tmap.h"
+
+namespace fp4 {
+
+FP4_DEFINE_STATUS_READER(attn_status)
+
+namespace attn {
+constexpr int BM = 128, BN = 128, HD = 128;
+constexpr int NK = 3, NV = 2;
+constexpr int THREADS = 384;
+// shared memory map (bytes, all pieces 1024-aligned where TMA/UMMA need it)
+constexpr int Q_BYTES = BM * HD / 2;  // 8 KB of E2M1 codes
+constexpr int OFF_Q = 0, OFF_QSF = 8192, OFF_GQ = 9216;
+constexpr int K_STAGE = 10240;  // codes 8 KB, scale atoms 1 KB, gk 512 B
+constexpr int OFF_K = 10240;
+constexpr int V_HALF = HD * 64 * 2;  // 128 rows (d) x 64 keys x fp16
+constexpr int V_STAGE = 4 * V_HALF;  // hi keys 0-63, hi 64-127, lo 0-63, lo 64-127
+constexpr int OFF_V = OFF_K + NK * K_STAGE;
+constexpr int OFF_STAT = OFF_V + NV * V_STAGE;  // m[2][128], l[2][128]
+constexpr int OFF_RCP = OFF_STAT + 4 * 128 * 4;
+constexpr int OFF_BAR = OFF_RCP + 128 * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t T_S = 0, T_O = 256, T_SFA = 384, T_SFB = 392;
+}  // namespace attn
+
+struct AttnArgs {
+  const uint8_t* qsf;  // tcgen05 atoms, nkb4q = Hq*2 groups per 128-row block
+  const float* gq;     // [B*Tp]
+  const uint8_t* ksf;
+  const float* gk;
+  float* out;  // [B, T, Hq, HD] fp32
+  int B, Hq, Hkv, T, Tp;
+  int causal;
+  float scale_log2;  // scaling * log2(e)
+  int units;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two E2M1 codes (one byte) -> their fp16 values.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(r) : "r"(byte));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+struct Unit {
+  int qt, b, h;
+};
+
+__device__ __forceinline__ Unit unit_of(int u, const AttnArgs& p) {
+  const int nqt = p.Tp / attn::BM;
+  const int bh = p.B * p.Hq;
+  Unit r;
+  r.qt = nqt - 1 - u / bh;  // longest (latest) query tiles first
+  const int x = u % bh;
+  r.b = x / p.Hq;
+  r.h = x % p.Hq;
+  return r;
+}
+
+__device__ __forceinline__ int kv_tiles(const Unit& un, const AttnArgs& p) {
+  return p.causal ? un.qt + 1 : p.Tp / attn::BN;
+}
+
+__global__ void __launch_bounds__(attn::THREADS, 1)
+    fp4_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmVhi, const __grid_constant__ CUtensorMap tmVlo,
+                    AttnArgs p) {
+  using namespace attn;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* stat_m = reinterpret_cast<float*>(sm + OFF_STAT);
+  float* stat_l = stat_m + 256;
+  float* rcp = reinterpret_cast<float*>(sm + OFF_RCP);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* q_full = bar + 0;
+  uint64_t* q_empty = bar + 1;
+  uint64_t* k_full = bar + 2;    // [NK]
+  uint64_t* k_empty = bar + 5;   // [NK]
+  uint64_t* v_full = bar + 8;    // [NV]
+  uint64_t* v_empty = bar + 10;  // [NV]
+  uint64_t* s_full = bar + 12;   // [2]
+  uint64_t* buf_free = bar + 14; // [2]
+  uint64_t* p_full = bar + 16;   // [2]
+  uint64_t* o_full = bar + 18;
+  uint64_t* o_free = bar + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 20);
+
+  const int warp = threadIdx.x / 32;
+  const int nkb4q = p.Hq * 2, nkb4k = p.Hkv * 2;
+  const int group = p.Hq / p.Hkv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < NK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 2);  // MMA commit + the softmax warpgroup that read gk
+    }
+    for (int i = 0; i < NV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&buf_free[i], 1);
+      mbar_init(&p_full[i], 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 1);
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 128) {
+    // correctly rounded 1/s for every non-negative E4M3 scale byte (0 -> 0, get_reciprocal)
+    const float s = e4m3_to_f32((uint8_t)threadIdx.x);
+    rcp[threadIdx.x] = s == 0.0f ? 0.0f : __frcp_rn(s);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmVhi);
+      tma_prefetch_desc(&tmVlo);
+      uint32_t kc = 0, vc = 0, uc = 0;
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
+        const Unit un = unit_of(u, p);
+        const int n = kv_tiles(un, p);
+        const int hk = un.h / group;
+        const int qrow = un.b * p.Tp + un.qt * BM;
+        if (uc > 0) mbar_wait(q_empty, (uc - 1) & 1, 0x201);
+        mbar_arrive_expect_tx(q_full, Q_BYTES + 1024 + 512);
+        tma_load_2d(sm + OFF_Q, &tmQ, q_full, un.h * (HD / 2), qrow);
+        bulk_load(sm + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * nkb4q + 2 * un.h) * 512, 1024, q_full);
+        bulk_load(sm + OFF_GQ, p.gq + qrow, 512, q_full);
+        for (int pass = 0; pass < 2; ++pass) {
+          for (int j = 0; j < n; ++j, ++kc) {
+            const int s = kc % NK;
+            if (kc >= NK) mbar_wait(&k_empty[s], ((kc / NK) - 1) & 1, 0x202);
+            uint8_t* ks = sm + OFF_K + s * K_STAGE;
+            const int krow = un.b * p.Tp + j * BN;
+            mbar_arrive_expect_tx(&k_full[s], 8192 + 1024 + 512);
+            tma_load_2d(ks, &tmK, &k_full[s], hk * (HD / 2), krow);
+            bulk_load(ks + 8192, p.ksf + ((int64_t)(krow / 128) * nkb4k + 2 * hk) * 512, 1024, &k_full[s]);
+            bulk_load(ks + 9216, p.gk + krow, 512, &k_full[s]);
+            if (pass == 1) {
+              const int vs = vc % NV;
+              if (vc >= NV) mbar_wait(&v_empty[vs], ((vc / NV) - 1) & 1, 0x203);
+              uint8_t* v = sm + OFF_V + vs * V_STAGE;
+              const int vrow = (un.b * p.Hkv + hk) * HD;
+              mbar_arrive_expect_tx(&v_full[vs], V_STAGE);
+              tma_load_2d(v, &tmVhi, &v_full[vs], j * BN, vrow);
+              tma_load_2d(v + V_HALF, &tmVhi, &v_full[vs], j * BN + 64, vrow);
+              tma_load_2d(v + 2 * V_HALF, &tmVlo, &v_full[vs], j * BN, vrow);
+              tma_load_2d(v + 3 * V_HALF, &tmVlo, &v_full[vs], j * BN + 64, vrow);
+              ++vc;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issue
+    if (elect_one_lane()) {
+      const uint32_t idq = idesc_nvf4(BM, BN);
+      const uint32_t idv = idesc_f16(BM, HD);
+      uint32_t kc = 0, vc = 0, uc = 0;
+      uint32_t use[2] = {0, 0}, pu[2] = {0, 0};
+      auto issue_qk = [&](int j, int kbuf) {
+        // buffer kbuf: wait until its previous use was released
+        if (use[kbuf] > 0) mbar_wait(&buf_free[kbuf], (use[kbuf] - 1) & 1, 0x211);
+        const int s = kc % NK;
+        mbar_wait(&k_full[s], (kc / NK) & 1, 0x212);
+        tc_fence_after();
+        uint8_t* ks = sm + OFF_K + s * K_STAGE;
+        const uint32_t sfb = tmem + T_SFB + 8 * s;
+        tmem_cp_sf_atom(sfb, smem_desc(smem_u32(ks + 8192), 16, 128, kSwizzleNone));
+        tmem_cp_sf_atom(sfb + 4, smem_desc(smem_u32(ks + 8192 + 512), 16, 128, kSwizzleNone));
+        const uint32_t d = tmem + T_S + 128 * kbuf;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t ad = smem_desc(smem_u32(sm + OFF_Q) + kk * 32, 16, 512, kSwizzle64B);
+          const uint64_t bd = smem_desc(smem_u32(ks) + kk * 32, 16, 512, kSwizzle64B);
+          mma_nvf4(d, ad, bd, idq, tmem + T_SFA + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&k_empty[s]);
+        tc_commit(&s_full[kbuf]);
+        ++use[kbuf];
+        ++kc;
+      };
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
+        const Unit un = unit_of(u, p);
+        const int n = kv_tiles(un, p);
+        mbar_wait(q_full, uc & 1, 0x213);
+        tc_fence_after();
+        tmem_cp_sf_atom(tmem + T_SFA, smem_desc(smem_u32(sm + OFF_QSF), 16, 128, kSwizzleNone));
+        tmem_cp_sf_atom(tmem + T_SFA + 4, smem_desc(smem_u32(sm + OFF_QSF + 512), 16, 128, kSwizzleNone));
+        // pass 1: scores only (the softmax groups release each buffer after reading it)
+        for (int j = 0; j < n; ++j) issue_qk(j, j & 1);
+        // pass 2: scores again, then PV once P is in TMEM
+        issue_qk(0, 0);
+        for (int j = 0; j < n; ++j) {
+          const int kb = j & 1;
+          if (j + 1 < n) issue_qk(j + 1, (j + 1) & 1);
+          mbar_wait(&p_full[kb], pu[kb] & 1, 0x214);
+          ++pu[kb];
+          const int vs = vc % NV;
+          mbar_wait(&v_full[vs], (vc / NV) & 1, 0x215);
+          if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
+          tc_fence_after();
+          uint8_t* v = sm + OFF_V + vs * V_STAGE;
+          const uint32_t a = tmem + T_S + 128 * kb;
+#pragma unroll
+          for (int part = 0; part < 2; ++part) {  // hi, lo
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t vb = smem_u32(v + part * 2 * V_HALF + (kk >> 2) * V_HALF) + (kk & 3) * 32;
+              mma_f16_ts(tmem + T_O, a + 8 * kk, smem_desc(vb, 16, 1024, kSwizzle128B), idv,
+                         (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit(&v_empty[vs]);
+          tc_commit(&buf_free[kb]);
+          ++vc;
+        }
+        tc_commit(o_full);
+        tc_commit(q_empty);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------- softmax warpgroups
+    const int wg = (warp - 4) >> 2;  // 0 or 1: takes key tiles j with j % 2 == wg
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + (threadIdx.x & 31);  // row of the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t sbuf = tmem + lane_base + T_S + 128 * wg;
+    const float r6 = __frcp_rn(6.0f);
+    uint32_t kc = 0, uc = 0, su = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
+      const Unit un = unit_of(u, p);
+      const int n = kv_tiles(un, p);
+      const int qpos = un.qt * BM + r;  // query index within the sequence
+      mbar_wait(q_full, uc & 1, 0x221);
+      const float uscale = reinterpret_cast<const float*>(sm + OFF_GQ)[r] * p.scale_log2;
+      // ---- pass 1: row maximum of z = acc * gk (S = z * gq * scaling)
+      float m = -INFINITY;
+      for (int j = 0; j < n; ++j, ++kc) {
+        if ((j & 1) != wg) continue;
+        const int s = kc % NK;
+        mbar_wait(&s_full[wg], su & 1, 0x222);
+        ++su;
+        tc_fence_after();
+        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216);
+        const bool diag = p.causal && j == un.qt;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t a[32];
+          tmem_ld32(sbuf + c * 32, a);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = c * 32 + i;
+            const int key = j * BN + col;
+            const bool masked = (diag && col > r) || (!p.causal && key >= p.T);
+            const float z = __uint_as_float(a[i]) * gk[col];
+            m = masked ? m : fmaxf(m, z);
+          }
+        }
+        tc_fence_before();
+        named_bar(1 + wg, 128);
+        if (threadIdx.x % 128 == 0) {
+          mbar_arrive(&buf_free[wg]);
+          mbar_arrive(&k_empty[s]);
+        }
+      }
+      stat_m[wg * 128 + r] = m;
+      named_bar(3, 256);
+      m = fmaxf(stat_m[r], stat_m[128 + r]);
+      const float mu = m == -INFINITY ? 0.0f : m * uscale;
+      // ---- pass 2: e = exp2(z*u - m*u), sum, NVFP4 fake-quant of e -> TMEM
+      float l = 0.0f;
+      for (int j = 0; j < n; ++j, ++kc) {
+        if ((j & 1) != wg) continue;
+        const int s = kc % NK;
+        mbar_wait(&s_full[wg], su & 1, 0x223);
+        ++su;
+        tc_fence_after();
+        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216);
+        const bool diag = p.causal && j == un.qt;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t a[32];
+          tmem_ld32(sbuf + c * 32, a);
+          tmem_ld_wait();
+          float e[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = c * 32 + i;
+            const int key = j * BN + col;
+            const bool masked = (diag && col > r) || (!p.causal && key >= p.T);
+            const float z = __uint_as_float(a[i]) * gk[col];
+            const float ev = ex2(fmaf(z, uscale, -mu));
+            e[i] = masked ? 0.0f : ev;
+            l += e[i];
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int blk = 0; blk < 2; ++blk) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, e[blk * 16 + i]);
+            const uint8_t sb = e4m3_satfinite(amax * r6);
+            const float rs = rcp[sb & 127];
+            const __half sh = __float2half_rn(e4m3_to_f32(sb));
+            const uint32_t sh2 = (uint32_t)__half_as_ushort(sh) * 0x10001u;
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+              const uint32_t byte = e2m1x2(e[blk * 16 + i] * rs, e[blk * 16 + i + 1] * rs);
+              pk[blk * 8 + i / 2] = hmul2_u32(e2m1x2_to_f16x2(byte), sh2);
+            }
+          }
+          // Phat for keys 32c..32c+31 -> TMEM columns 16c..16c+15 of this buffer
+          // (already read: S chunk c/2 precedes it)
+          tmem_st16(sbuf + c * 16, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        named_bar(1 + wg, 128);
+        if (threadIdx.x % 128 == 0) {
+          mbar_arrive(&p_full[wg]);
+          mbar_arrive(&k_empty[s]);
+        }
+      }
+      stat_l[wg * 128 + r] = l;
+      named_bar(3, 256);
+      l = stat_l[r] + stat_l[128 + r];
+      // ---- epilogue: O rows / l, columns 64*wg .. 64*wg+63
+      mbar_wait(o_full, uc & 1, 0x224);
+      tc_fence_after();
+      const float rl = 1.0f / l;
+      const bool store = qpos < p.T;
+      float* dst = p.out + (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + 64 * wg;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t a[32];
+        tmem_ld32(tmem + lane_base + T_O + 64 * wg + 32 * c, a);
+        tmem_ld_wait();
+        if (store) {
+          float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(__uint_as_float(a[4 * i]) * rl, __uint_as_float(a[4 * i + 1]) * rl,
+                                __uint_as_float(a[4 * i + 2]) * rl, __uint_as_float(a[4 * i + 3]) * rl);
+        }
+      }
+      tc_fence_before();
+      named_bar(3, 256);
+      if (threadIdx.x == 128) mbar_arrive(o_free);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ------------------------------------------------------------ V preparation
+// Vhat = single_nvfp4(v2d.T, global_scale_aligned=False) in fp32 arithmetic
+// (fp4_quant_utils.py:112-172 column mode on the [Hkv*D, B*T] view), written
+// as two fp16 planes hi = fp16(Vhat), lo = fp16(Vhat - hi) in the layout the
+// attention kernel loads: row (b*Hkv + h)*D + d, column t (Tp columns).
+// One CTA per 16 consecutive tokens of the flattened B*T axis (one NVFP4
+// block along tokens for every channel).
+constexpr int VP_THREADS = 256;
+constexpr int VP_MAX_HD = 2048;
+
+struct VPrepArgs {
+  const void* v;  // bf16 / f16 / f32, [B, Hkv, T, D] with element strides
+  int in_dtype;
+  int64_t sB, sH, sT;
+  int B, Hkv, T, D, Tp;
+  __half* hi;
+  __half* lo;
+  float* vhat;  // optional fp32 Vhat, same layout
+  float* g;     // optional per-token global scale [B*T]
+};
+
+template <int DT>
+__global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
+  using T = typename In<DT>::T;
+  extern __shared__ float vp_smem[];  // [16][HDn + 1] token slab, then g[16], rg[16]
+  const int HDn = p.Hkv * p.D;
+  const int ld = HDn + 1;
+  float* gtok = vp_smem + 16 * ld;
+  float* rgtok = gtok + 16;
+#define slab(tk, c) vp_smem[(tk) * ld + (c)]
+  const int64_t BT = (int64_t)p.B * p.T;
+  const int64_t j0 = (int64_t)blockIdx.x * 16;
+  // load 16 tokens x all channels (zeros past the end: the reference pads B*T to x16)
+  for (int idx = threadIdx.x; idx < 16 * HDn; idx += VP_THREADS) {
+    const int tk = idx / HDn, c = idx - tk * HDn;
+    const int64_t jj = j0 + tk;
+    float x = 0.0f;
+    if (jj < BT) {
+      const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
+      const int h = c / p.D, d = c - h * p.D;
+      x = In<DT>::f(reinterpret_cast<const T*>(p.v)[(int64_t)b * p.sB + (int64_t)h * p.sH + (int64_t)t * p.sT + d]);
+    }
+    slab(tk, c) = x;
+  }
+  __syncthreads();
+  // per-token global scale: colmax of v2d.T * recip(1536) (fp4_quant_utils.py:136,139)
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int tk = warp; tk < 16; tk += VP_THREADS / 32) {
+    float mx = 0.0f;
+    for (int c = lane; c < HDn; c += 32) mx = nanmax(mx, fabsf(slab(tk, c)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = nanmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) {
+      const float g = mul<FP4_ARITH_F32>(mx, recip<FP4_ARITH_F32>(1536.0f));
+      gtok[tk] = g;
+      rgtok[tk] = recip<FP4_ARITH_F32>(g);
+      if (p.g && j0 + tk < BT) p.g[j0 + tk] = g;
+    }
+  }
+  __syncthreads();
+  const float r6 = recip<FP4_ARITH_F32>(6.0f);
+  for (int c = threadIdx.x; c < HDn; c += VP_THREADS) {
+    float x[16];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      x[i] = mul<FP4_ARITH_F32>(slab(i, c), rgtok[i]);
+      amax = nanmax(amax, fabsf(x[i]));
+    }
+    const uint8_t sb = e4m3_torch(mul<FP4_ARITH_F32>(amax, r6));
+    const float s = e4m3_to_f32(sb);
+    const float rs = recip<FP4_ARITH_F32>(s);
+    const bool nan_block = (sb & 0x7F) == 0x7F;
+    const int h = c / p.D, d = c - h * p.D;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const float a0 = __fmaf_rn(x[i], rs, 0.0f), a1 = __fmaf_rn(x[i + 1], rs, 0.0f);
+      const uint32_t byte = nan_block ? 0u : e2m1x2(a0, a1);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t jj = j0 + i + k;
+        if (jj >= BT) continue;
+        const float vh = mul<FP4_ARITH_F32>(mul<FP4_ARITH_F32>(e2m1_value((byte >> (4 * k)) & 15u), s), gtok[i + k]);
+        const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
+        const int64_t o = ((int64_t)(b * p.Hkv + h) * p.D + d) * p.Tp + t;
+        const __half hi = __float2half_rn(vh);
+        p.hi[o] = hi;
+        p.lo[o] = __float2half_rn(vh - __half2float(hi));
+        if (p.vhat) p.vhat[o] = vh;
+      }
+    }
+  }
+#undef slab
+}
+
+template <int DT>
+static void vprep_launch(const VPrepArgs& a, unsigned blocks, size_t smem, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(vprep_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (16 * (VP_MAX_HD + 1) + 32) * (int)sizeof(float));
+    attr = true;
+  }
+  vprep_kernel<DT><<<blocks, VP_THREADS, smem, st>>>(a);
+}
+
+static int launch_vprep(const VPrepArgs& a, cudaStream_t st) {
+  const unsigned blocks = (unsigned)(((int64_t)a.B * a.T + 15) / 16);
+  const size_t smem = (16 * (size_t)(a.Hkv * a.D + 1) + 32) * sizeof(float);
+  switch (a.in_dtype) {
+    case FP4_DT_F32: vprep_launch<FP4_DT_F32>(a, blocks, smem, st); break;
+    case FP4_DT_BF16: vprep_launch<FP4_DT_BF16>(a, blocks, smem, st); break;
+    case FP4_DT_F16: vprep_launch<FP4_DT_F16>(a, blocks, smem, st); break;
+    default: return set_error(FP4ATTN_ERR_ARG, "bad dtype");
+  }
+  return check_launch("vprep_kernel");
+}
+
+}  // namespace fp4
+
+using namespace fp4;
+
+extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, int T, int D, int64_t sB, int64_t sH,
+                                 int64_t sT, int Tp, uint16_t* v_hi, uint16_t* v_lo, float* vhat, float* g,
+                                 void* stream) {
+  clear_error();
+  if (!v || !v_hi || !v_lo) return set_error(FP4ATTN_ERR_ARG, "null pointer");
+  if (B <= 0 || Hkv <= 0 || T <= 0 || D <= 0 || Tp < T) return set_error(FP4ATTN_ERR_ARG, "bad shape");
+  if (Hkv * D > VP_MAX_HD) return set_error(FP4ATTN_ERR_UNSUPPORTED, "Hkv*D > %d", VP_MAX_HD);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (Tp > T) {  // padded key columns must read as zeros
+    const size_t bytes = (size_t)B * Hkv * D * Tp * 2;
+    if (cudaMemsetAsync(v_hi, 0, bytes, st) != cudaSuccess || cudaMemsetAsync(v_lo, 0, bytes, st) != cudaSuccess)
+      return set_error(FP4ATTN_ERR_CUDA, "memset");
+  }
+  VPrepArgs a{v, in_dtype, sB, sH, sT, B, Hkv, T, D, Tp, reinterpret_cast<__half*>(v_hi),
+              reinterpret_cast<__half*>(v_lo), vhat, g};
+  return launch_vprep(a, st);
+}
+
+extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                                  const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                                  const uint16_t* v_hi, const uint16_t* v_lo, float* out, int B, int Hq, int Hkv,
+                                  int T, int Tp, int D, int causal, float scaling, int num_ctas, void* stream) {
+  using namespace attn;
+  clear_error();
+  if (D != HD) return set_error(FP4ATTN_ERR_UNSUPPORTED, "head_dim must be %d", HD);
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0 || Hq % Hkv != 0) return set_error(FP4ATTN_ERR_ARG, "bad shape");
+  if (Tp % 128 != 0 || Tp < T) return set_error(FP4ATTN_ERR_ARG, "Tp must be a multiple of 128 >= T");
+  if (!q_codes || !q_scales || !q_g || !k_codes || !k_scales || !k_g || !v_hi || !v_lo || !out)
+    return set_error(FP4ATTN_ERR_ARG, "null pointer");
+  if (((uintptr_t)q_codes | (uintptr_t)k_codes | (uintptr_t)v_hi | (uintptr_t)v_lo | (uintptr_t)q_scales |
+       (uintptr_t)k_scales | (uintptr_t)q_g | (uintptr_t)k_g | (uintptr_t)out) % 16)
+    return set_error(FP4ATTN_ERR_ARG, "buffers must be 16-byte aligned");
+  CUtensorMap mq, mk, mvh, mvl;
+  if (int e = encode_tiled_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, q_codes, (uint64_t)Hq * (HD / 2), (uint64_t)B * Tp,
+                              (uint64_t)Hq * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  if (int e = encode_tiled_2d(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_codes, (uint64_t)Hkv * (HD / 2), (uint64_t)B * Tp,
+                              (uint64_t)Hkv * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  if (int e = encode_tiled_2d(&mvh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, v_hi, (uint64_t)Tp, (uint64_t)B * Hkv * HD,
+                              (uint64_t)Tp * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  if (int e = encode_tiled_2d(&mvl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, v_lo, (uint64_t)Tp, (uint64_t)B * Hkv * HD,
+                              (uint64_t)Tp * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  AttnArgs a{};
+  a.qsf = q_scales;
+  a.gq = q_g;
+  a.ksf = k_scales;
+  a.gk = k_g;
+  a.out = out;
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.T = T;
+  a.Tp = Tp;
+  a.causal = causal ? 1 : 0;
+  a.scale_log2 = scaling * 1.4426950408889634f;
+  a.units = B * Hq * (Tp / 128);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(fp4_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr = true;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int grid = num_ctas > 0 ? num_ctas : sms;
+  if (grid > a.units) grid = a.units;
+  fp4_attn_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mvh, mvl, a);
+  return check_launch("fp4_attn_kernel");
+}

@@ -1,0 +1,9 @@
+// quant_bf16.cu -- quantizer kernels instantiated for bf16 input.
+#include "quant_impl.cuh"
+
+namespace fp4 {
+int quant_dispatch_bf16(const QuantArgs& p, int arith, int out_dtype, float* g, float gsf_max, int what,
+                        cudaStream_t st) {
+  return dispatch_arith<FP4_DT_BF16>(p, arith, out_dtype, g, gsf_max, what, st);
+}
+}  // namespace fp4

@@ -35,4 +35,13 @@ extern "C" const char* fp4attn_last_error(void) { return fp4::g_msg; }
 
 extern "C" int fp4attn_version(void) { return 1; }
 
+// Synchronizes with the device (reads device symbols).  Non-zero means a
+// bounded wait inside a kernel gave up: (site << 16) | (CTA index + 1).
+extern "C" unsigned int fp4attn_device_status(int reset) {
+  unsigned int v = fp4::gemm_status(reset != 0);
+  if (!v) v = fp4::attn_status(reset != 0);
+  else fp4::attn_status(reset != 0);
+  return v;
+}
+
 extern "C" unsigned long long fp4attn_launch_count(void) { return __atomic_load_n(&fp4::g_launches, __ATOMIC_RELAXED); }

@@ -16,4 +16,7 @@ int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 // Count one kernel launch of this library (read by fp4attn_launch_count()).
 void count_launch();
+// Device status words of the translation units with bounded waits.
+unsigned int gemm_status(bool reset);
+unsigned int attn_status(bool reset);
 }  // namespace fp4

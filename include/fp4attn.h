@@ -32,6 +32,23 @@ const char* fp4attn_last_error(void);
 int fp4attn_version(void);
 /* Number of kernels this library has launched in this process (all threads). */
 unsigned long long fp4attn_launch_count(void);
+/* Device-side status: 0, or the first bounded wait inside a kernel that gave
+ * up ((site << 16) | (CTA index + 1)); such a kernel unwinds and returns
+ * instead of hanging.  Synchronizes with the device; reset != 0 clears it. */
+unsigned int fp4attn_device_status(int reset);
+
+/* ------------------------------------------------------------------------
+ * fp4_gemm_nvf4: C[m,n] = ga[m] * gb[n] * sum_k A[m,k] * B[n,k] on NVFP4
+ * operands (tcgen05 kind::mxf4nvf4).  A and B are E2M1 codes [rows][ld]
+ * bytes (K-major, two per byte, as fp4q_quantize writes them) with UE4M3
+ * block scales in the tcgen05 atom layout (fp4q_quantize scale_layout 1);
+ * ga/gb are per-row global scales or NULL.  C is fp32 [M][ldc].
+ * K % 256 == 0.  No reference counterpart: the reference computes
+ * attention scores with a dequantize + torch.matmul (llama_patch.py:71).
+ * ---------------------------------------------------------------------- */
+int fp4_gemm_nvf4(const uint8_t* a_codes, const uint8_t* a_scales, const float* a_g, const uint8_t* b_codes,
+                  const uint8_t* b_scales, const float* b_g, float* c, int M, int N, int K, int64_t lda, int64_t ldb,
+                  int64_t ldc, void* stream);
 
 /* ------------------------------------------------------------------------
  * nvfp4sim module functions.  Each replaces one pybind11 binding of
@@ -101,6 +118,36 @@ int fp4q_quantize(const void* x, int in_dtype, int B, int T, int H, int D, int64
  * torch.max/abs/get_reciprocal steps of fp4_quant_utils.py:135-139. */
 int fp4q_global_scale(const void* x, int in_dtype, int B, int T, int H, int D, int64_t sB, int64_t sT, int64_t sH,
                       int gmode, int arith, float global_sf_max, float* g, void* stream);
+
+/* ------------------------------------------------------------------------
+ * FP4 attention forward: the native replacement for eager_attention_forward
+ * with FP4 fake-quant (llama_patch.py:57-105) fed by the Q/K/V fake-quant of
+ * llama_patch.py:167-196.  Three calls:
+ *   1. fp4q_quantize on Q and K ([B,H,T,D] viewed as [B*T, H*D], row mode,
+ *      T_pad = Tp, scale_layout 1) -> codes [B*Tp][H*D/2], scale atoms,
+ *      per-token g [B*Tp];
+ *   2. fp4attn_prepare_v on V;
+ *   3. fp4attn_fwd_packed.
+ * Tp = T rounded up to a multiple of 128.
+ * ---------------------------------------------------------------------- */
+
+/* V -> Vhat = single_nvfp4(v2d.T, global_scale_aligned=False) in fp32
+ * arithmetic (llama_patch.py:196, fp4_quant_utils.py:112-172), stored as
+ * fp16 hi/lo planes [B*Hkv*D][Tp] (row (b*Hkv+h)*D+d, column t; hi+lo keeps
+ * 22 significant bits of Vhat, |Vhat| < 65504).  v is [B,Hkv,T,D] with
+ * element strides sB, sH, sT and d contiguous.  vhat (fp32, same layout) and
+ * g ([B*T], per-token global scale) are optional outputs.  Hkv*D <= 2048. */
+int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, int T, int D, int64_t sB, int64_t sH, int64_t sT,
+                      int Tp, uint16_t* v_hi, uint16_t* v_lo, float* vhat, float* g, void* stream);
+
+/* O[b,t,hq,:] = sum_j Phat[t,j] Vhat[j,:] with S = Qhat Khat^T * scaling,
+ * causal or not, GQA (Hq % Hkv == 0), Phat = NVFP4 fake-quant of softmax(S)
+ * per row (llama_patch.py:81-99).  out is fp32 [B,T,Hq,D].  D = 128.
+ * num_ctas 0 = one persistent CTA per SM. */
+int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g, const uint8_t* k_codes,
+                       const uint8_t* k_scales, const float* k_g, const uint16_t* v_hi, const uint16_t* v_lo,
+                       float* out, int B, int Hq, int Hkv, int T, int Tp, int D, int causal, float scaling,
+                       int num_ctas, void* stream);
 
 #ifdef __cplusplus
 }

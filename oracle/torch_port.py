@@ -132,3 +132,67 @@ def attention(q, k, v, causal: bool = True, scaling: float | None = None,
         scaling = q.shape[-1] ** -0.5
     Qf, Kf, Vf = fake_quant_qkv(q, k, v, dual_q)
     return eager_attention(Qf, Kf, Vf, causal, scaling, dual_p, q_rows)
+
+
+# --------------------------------------------------------------------------
+# Decision margins of the P quantization.
+#
+# P's NVFP4 codes are a discontinuous function of S: two correct
+# implementations whose S differ in the last bits of fp32 (summation order,
+# exp implementation) can round a P element -- or a whole block's E4M3 scale
+# -- to neighbouring values, which moves that output row by far more than
+# the rounding noise.  The reference itself shows this: recomputing its S in
+# float64 instead of fp32 moves a few rows of O by up to ~0.05 x RMS(O).
+# ambiguous_rows() flags the rows where any quantization decision of P lies
+# within a relative `delta` of a rounding boundary, so a max-abs check can be
+# restricted to rows whose FP4 decisions are determined at fp32 precision.
+
+_E2M1_THRESH = (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0)
+
+
+def _e4m3_margin(v: torch.Tensor) -> torch.Tensor:
+    """Relative distance of v (>= 0) to the nearest E4M3 round-to-nearest boundary."""
+    v = v.double()
+    e = torch.floor(torch.log2(torch.clamp(v, min=1e-300))).clamp(min=-6)
+    step = torch.exp2(e - 3)
+    f = v / step
+    d = (f - torch.floor(f) - 0.5).abs() * step / torch.clamp(v, min=1e-300)
+    return torch.where(v > 0, d, torch.full_like(d, float("inf")))
+
+
+def ambiguous_rows(S: torch.Tensor, delta: float) -> torch.Tensor:
+    """S: scaled, masked scores [..., keys] (float64 preferred).  Returns bool [...]."""
+    S = S.double()
+    m = S.amax(-1, keepdim=True)
+    x = torch.exp(S - m)
+    n = x.shape[-1]
+    if n % 16:
+        x = torch.nn.functional.pad(x, (0, 16 - n % 16))
+    xb = x.reshape(*x.shape[:-1], -1, 16)
+    sc = xb.amax(-1) * (1.0 / 6.0)
+    amb = (_e4m3_margin(sc) < delta).any(-1)
+    s = sc.float().to(torch.float8_e4m3fn).double()
+    rs = torch.where(s == 0, torch.zeros_like(s), 1.0 / s)
+    y = xb * rs[..., None]
+    for t in _E2M1_THRESH:
+        amb |= ((y - t).abs() / t < delta).flatten(-2).any(-1)
+    return amb
+
+
+def attention_with_margins(q, k, v, causal: bool = True, scaling: float | None = None, delta: float = 1e-5):
+    """attention() plus, per output row [B, T, Hq], whether its P quantization is ambiguous at `delta`."""
+    if scaling is None:
+        scaling = q.shape[-1] ** -0.5
+    Qf, Kf, Vf = fake_quant_qkv(q, k, v)
+    out = eager_attention(Qf, Kf, Vf, causal, scaling)
+    B, Hq, T, D = Qf.shape
+    G = Hq // Kf.shape[1]
+    flags = torch.zeros(B, T, Hq, dtype=torch.bool)
+    mask = torch.triu(torch.full((T, T), float("-inf"), dtype=torch.float64), 1) if causal else None
+    for b in range(B):
+        for h in range(Hq):
+            S = (Qf[b, h].double() @ Kf[b, h // G].double().T) * scaling
+            if mask is not None:
+                S = S + mask
+            flags[b, :, h] = ambiguous_rows(S, delta)
+    return out, flags

@@ -1,0 +1,112 @@
+"""FP4 attention forward (tcgen05) against the simulated-FP4 attention oracle.
+
+Tolerance (stated for the attention output O, fp32):
+  * cosine(O, O_ref) >= 0.9999 over the whole output;
+  * max |O - O_ref| <= 2e-2 * RMS(O_ref) over every row whose NVFP4
+    quantization of P is decided at fp32 precision: rows with a P decision
+    within a relative DELTA of a rounding boundary are excluded from the
+    max-abs check (they stay in the cosine), because there two correct fp32
+    implementations -- including the reference against itself with another
+    summation order -- legitimately round to neighbouring FP4 values.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as oq
+from oracle import torch_port as tp
+
+pytestmark = pytest.mark.gpu
+
+DELTA = 1e-5
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def check(o_gpu, o_ref, flags=None, max_masked_frac=0.25):
+    o_gpu, o_ref = o_gpu.double(), o_ref.double()
+    rms = o_ref.pow(2).mean().sqrt()
+    cos = torch.nn.functional.cosine_similarity(o_gpu.flatten(), o_ref.flatten(), dim=0)
+    assert cos >= 0.9999, f"cosine {cos}"
+    err = (o_gpu - o_ref).abs().amax(-1)  # per (b, t, h) row
+    ok = torch.ones_like(err, dtype=torch.bool) if flags is None else ~flags
+    if flags is not None:
+        assert flags.float().mean() <= max_masked_frac, f"masked fraction {flags.float().mean()}"
+    worst = err[ok].max() / rms
+    assert worst <= 2e-2, f"max-abs / RMS on decided rows = {worst}"
+    return float(cos), float(worst)
+
+
+def _run(q, k, v, causal):
+    from fp4_attn_b200.attention import fp4_attention_fwd
+    from fp4_attn_b200.gemm import device_status
+    dev = torch.device("cuda", 0)
+    o = fp4_attention_fwd(q.to(dev), k.to(dev), v.to(dev), causal=causal).cpu()
+    assert device_status() == 0
+    return o
+
+
+def test_prepare_v_bit_exact():
+    from fp4_attn_b200.attention import prepare_v
+    dev = torch.device("cuda", 0)
+    rng = np.random.RandomState(3)
+    B, H, T, D = 2, 3, 100, 128
+    v = torch.from_numpy(rng.standard_normal((B, H, T, D)).astype(np.float32)).bfloat16()
+    Tp = 128
+    vhi = torch.empty(B * H * D, Tp, dtype=torch.float16, device=dev)
+    vlo = torch.empty_like(vhi)
+    vhat = torch.zeros(B * H * D, Tp, device=dev)
+    g = torch.empty(B * T, device=dev)
+    prepare_v(v.to(dev), vhi, vlo, Tp, vhat, g)
+    v2d = v.permute(0, 2, 1, 3).reshape(B * T, H * D).float()
+    ref, _, _, ref_g = oq.fused_qdq(np.ascontiguousarray(v2d.T.numpy()), "col", "float32", 1536.0)
+    got = vhat.cpu().reshape(B, H, D, Tp)[..., :T].permute(1, 2, 0, 3).reshape(H * D, B * T).numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+    np.testing.assert_array_equal(g.cpu().numpy().view(np.uint32), ref_g[: B * T].view(np.uint32))
+    s = (vhi.float() + vlo.float()).cpu().double().reshape(B, H, D, Tp)
+    assert (s[..., T:] == 0).all()
+    hv = vhat.cpu().double().reshape(B, H, D, Tp)
+    assert ((s - hv).abs() <= hv.abs() * 2.0 ** -21 + 1e-12).all()
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,causal", [
+    (1, 2, 1, 256, True), (2, 4, 2, 200, True), (1, 2, 2, 384, False), (1, 8, 2, 512, True),
+    (1, 4, 4, 130, False), (3, 2, 1, 64, True)])
+def test_attention_small(B, Hq, Hkv, T, causal):
+    g = torch.Generator().manual_seed(B * 1000 + Hq * 100 + T)
+    q = torch.randn(B, Hq, T, 128, generator=g).bfloat16()
+    k = torch.randn(B, Hkv, T, 128, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, T, 128, generator=g).bfloat16()
+    o = _run(q, k, v, causal)
+    ref, flags = tp.attention_with_margins(q, k, v, causal, delta=DELTA)
+    check(o, ref, flags)
+
+
+def test_attention_against_reference_goldens():
+    """The reference's own outputs (tests/golden/attention.npz), single P quantization, head_dim 128."""
+    z = np.load(os.path.join(GOLD, "attention.npz"))
+    idx = json.loads(bytes(z["index"]).decode())
+    ran = 0
+    for c in idx:
+        if c["dual_p"] or c["D"] != 128:
+            continue
+        q, k, v = (torch.from_numpy(z[c["inputs"] + s]).view(torch.bfloat16) for s in ("_q", "_k", "_v"))
+        o = _run(q, k, v, c["causal"])
+        _, flags = tp.attention_with_margins(q, k, v, c["causal"], delta=DELTA)
+        check(o, torch.from_numpy(z[c["key"] + "_o"]), flags)
+        ran += 1
+    assert ran >= 3
+
+
+def test_attention_llama3_8b_shape_full():
+    """Config 2 at full size: B=1, Hq=32, Hkv=8, T=4096, causal, q/k/v ~ N(0,1) seed 1."""
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, 32, 4096, 128, generator=g).bfloat16()
+    k = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
+    v = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
+    o = _run(q, k, v, True)
+    ref, flags = tp.attention_with_margins(q, k, v, True, delta=DELTA)
+    cos, worst = check(o, ref, flags)
+    print(f"config2: cosine {cos:.9f}, max-abs/RMS on decided rows {worst:.3e}, masked {flags.float().mean():.4f}")

@@ -91,6 +91,117 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   return r;
 }
 
+// Packed fp32 pairs (sm_100a f32x2 ALU ops, each lane rounded like the scalar op).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// E2M1 round-to-nearest-even of (x0, x1) -> fp16 code values times the block
+// scale (sh2 = the scale as two halves): code * scale is exact in fp16.
+__device__ __forceinline__ uint32_t quant_pair_f16(float x0, float x1, uint32_t sh2) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, t;\n\t"
+      "mul.rn.f16x2 %0, %0, %3;\n\t}"
+      : "=r"(r)
+      : "f"(x0), "f"(x1), "r"(sh2));
+  return r;
+}
+
+// Pass 1 on one 32-key chunk: running max of z = acc * gk (keys with
+// column > lim masked when MASK).
+template <bool MASK>
+__device__ __forceinline__ float chunk_max(const uint32_t (&a)[32], const float* gk, int col0, int lim, float m) {
+  float z[32];
+  const float4* g4 = reinterpret_cast<const float4*>(gk);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 g = g4[q];
+    upk2(mul2(pk2(__uint_as_float(a[4 * q]), __uint_as_float(a[4 * q + 1])), pk2(g.x, g.y)), z[4 * q], z[4 * q + 1]);
+    upk2(mul2(pk2(__uint_as_float(a[4 * q + 2]), __uint_as_float(a[4 * q + 3])), pk2(g.z, g.w)), z[4 * q + 2],
+         z[4 * q + 3]);
+  }
+  if constexpr (MASK) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) z[i] = (col0 + i > lim) ? -INFINITY : z[i];
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) m = max3f(m, z[i], z[i + 1]);
+  return m;
+}
+
+// Pass 2 on one 32-key chunk: e = exp2(z*u - m*u), running sum, NVFP4
+// fake-quant of e in two blocks of 16 -> 16 words of fp16 pairs.
+template <bool MASK>
+__device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
+                                        uint64_t nmu2, const float* rcp, float r6, uint64_t (&lsum2)[4],
+                                        uint32_t (&pk)[16]) {
+  float e[32];
+  const float4* g4 = reinterpret_cast<const float4*>(gk);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 g = g4[q];
+    float t0, t1, t2, t3;
+    upk2(fma2(mul2(pk2(__uint_as_float(a[4 * q]), __uint_as_float(a[4 * q + 1])), pk2(g.x, g.y)), u2, nmu2), t0, t1);
+    upk2(fma2(mul2(pk2(__uint_as_float(a[4 * q + 2]), __uint_as_float(a[4 * q + 3])), pk2(g.z, g.w)), u2, nmu2), t2,
+         t3);
+    e[4 * q] = ex2(t0);
+    e[4 * q + 1] = ex2(t1);
+    e[4 * q + 2] = ex2(t2);
+    e[4 * q + 3] = ex2(t3);
+  }
+  if constexpr (MASK) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) lsum2[(i >> 1) & 3] = add2(lsum2[(i >> 1) & 3], pk2(e[i], e[i + 1]));
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    const float* eb = e + 16 * blk;
+    const float m0 = max3f(eb[0], eb[1], eb[2]), m1 = max3f(eb[3], eb[4], eb[5]);
+    const float m2 = max3f(eb[6], eb[7], eb[8]), m3 = max3f(eb[9], eb[10], eb[11]);
+    const float m4 = max3f(eb[12], eb[13], eb[14]);
+    const float amax = fmaxf(max3f(m0, m1, m2), max3f(m3, m4, eb[15]));
+    const uint8_t sb = e4m3_satfinite(amax * r6);
+    const float rs = rcp[sb & 127];
+    const uint32_t sh2 = (uint32_t)__half_as_ushort(__float2half_rn(e4m3_to_f32(sb))) * 0x10001u;
+    const uint64_t rs2 = pk2(rs, rs);
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      float x0, x1;
+      upk2(mul2(pk2(eb[i], eb[i + 1]), rs2), x0, x1);
+      pk[8 * blk + i / 2] = quant_pair_f16(x0, x1, sh2);
+    }
+  }
+}
+
 struct Unit {
   int qt, b, h;
 };
@@ -308,20 +419,17 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         ++su;
         tc_fence_after();
         const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216);
-        const bool diag = p.causal && j == un.qt;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t a[32];
-          tmem_ld32(sbuf + c * 32, a);
-          tmem_ld_wait();
+        // keys with column > lim are masked (causal diagonal tile, or keys past T)
+        const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
+        uint32_t a[2][32];
+        tmem_ld32(sbuf, a[0]);
+        tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c * 32 + i;
-            const int key = j * BN + col;
-            const bool masked = (diag && col > r) || (!p.causal && key >= p.T);
-            const float z = __uint_as_float(a[i]) * gk[col];
-            m = masked ? m : fmaxf(m, z);
-          }
+        for (int c = 0; c < 4; ++c) {
+          if (c < 3) tmem_ld32(sbuf + (c + 1) * 32, a[(c + 1) & 1]);
+          if (lim < 127) m = chunk_max<true>(a[c & 1], gk + 32 * c, 32 * c, lim, m);
+          else m = chunk_max<false>(a[c & 1], gk + 32 * c, 32 * c, lim, m);
+          if (c < 3) tmem_ld_wait();
         }
         tc_fence_before();
         named_bar(1 + wg, 128);
@@ -334,8 +442,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       named_bar(3, 256);
       m = fmaxf(stat_m[r], stat_m[128 + r]);
       const float mu = m == -INFINITY ? 0.0f : m * uscale;
+      const uint64_t u2 = pk2(uscale, uscale), nmu2 = pk2(-mu, -mu);
       // ---- pass 2: e = exp2(z*u - m*u), sum, NVFP4 fake-quant of e -> TMEM
-      float l = 0.0f;
+      uint64_t lsum2[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
       for (int j = 0; j < n; ++j, ++kc) {
         if ((j & 1) != wg) continue;
         const int s = kc % NK;
@@ -343,42 +452,20 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         ++su;
         tc_fence_after();
         const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216);
-        const bool diag = p.causal && j == un.qt;
-#pragma unroll 1
+        const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
+        uint32_t a[2][32];
+        tmem_ld32(sbuf, a[0]);
+        tmem_ld_wait();
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t a[32];
-          tmem_ld32(sbuf + c * 32, a);
-          tmem_ld_wait();
-          float e[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c * 32 + i;
-            const int key = j * BN + col;
-            const bool masked = (diag && col > r) || (!p.causal && key >= p.T);
-            const float z = __uint_as_float(a[i]) * gk[col];
-            const float ev = ex2(fmaf(z, uscale, -mu));
-            e[i] = masked ? 0.0f : ev;
-            l += e[i];
-          }
+          if (c < 3) tmem_ld32(sbuf + (c + 1) * 32, a[(c + 1) & 1]);
           uint32_t pk[16];
-#pragma unroll
-          for (int blk = 0; blk < 2; ++blk) {
-            float amax = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, e[blk * 16 + i]);
-            const uint8_t sb = e4m3_satfinite(amax * r6);
-            const float rs = rcp[sb & 127];
-            const __half sh = __float2half_rn(e4m3_to_f32(sb));
-            const uint32_t sh2 = (uint32_t)__half_as_ushort(sh) * 0x10001u;
-#pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              const uint32_t byte = e2m1x2(e[blk * 16 + i] * rs, e[blk * 16 + i + 1] * rs);
-              pk[blk * 8 + i / 2] = hmul2_u32(e2m1x2_to_f16x2(byte), sh2);
-            }
-          }
+          if (lim < 127) chunk_p<true>(a[c & 1], gk + 32 * c, 32 * c, lim, u2, nmu2, rcp, r6, lsum2, pk);
+          else chunk_p<false>(a[c & 1], gk + 32 * c, 32 * c, lim, u2, nmu2, rcp, r6, lsum2, pk);
           // Phat for keys 32c..32c+31 -> TMEM columns 16c..16c+15 of this buffer
-          // (already read: S chunk c/2 precedes it)
+          // (S chunk c/2, already read)
           tmem_st16(sbuf + c * 16, pk);
+          if (c < 3) tmem_ld_wait();
         }
         tmem_st_wait();
         tc_fence_before();
@@ -388,26 +475,29 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           mbar_arrive(&k_empty[s]);
         }
       }
-      stat_l[wg * 128 + r] = l;
+      float l0, l1;
+      upk2(add2(add2(lsum2[0], lsum2[1]), add2(lsum2[2], lsum2[3])), l0, l1);
+      stat_l[wg * 128 + r] = l0 + l1;
       named_bar(3, 256);
-      l = stat_l[r] + stat_l[128 + r];
+      const float l = stat_l[r] + stat_l[128 + r];
       // ---- epilogue: O rows / l, columns 64*wg .. 64*wg+63
       mbar_wait(o_full, uc & 1, 0x224);
       tc_fence_after();
       const float rl = 1.0f / l;
       const bool store = qpos < p.T;
       float* dst = p.out + (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + 64 * wg;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t a[32];
-        tmem_ld32(tmem + lane_base + T_O + 64 * wg + 32 * c, a);
-        tmem_ld_wait();
-        if (store) {
+      uint32_t a[2][32];
+      tmem_ld32(tmem + lane_base + T_O + 64 * wg, a[0]);
+      tmem_ld32(tmem + lane_base + T_O + 64 * wg + 32, a[1]);
+      tmem_ld_wait();
+      if (store) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
           float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(__uint_as_float(a[4 * i]) * rl, __uint_as_float(a[4 * i + 1]) * rl,
-                                __uint_as_float(a[4 * i + 2]) * rl, __uint_as_float(a[4 * i + 3]) * rl);
+            d4[i] = make_float4(__uint_as_float(a[c][4 * i]) * rl, __uint_as_float(a[c][4 * i + 1]) * rl,
+                                __uint_as_float(a[c][4 * i + 2]) * rl, __uint_as_float(a[c][4 * i + 3]) * rl);
         }
       }
       tc_fence_before();
@@ -439,6 +529,7 @@ struct VPrepArgs {
   __half* lo;
   float* vhat;  // optional fp32 Vhat, same layout
   float* g;     // optional per-token global scale [B*T]
+  int vec;      // 16-byte aligned rows of 8 channels: vector loads
 };
 
 template <int DT>
@@ -452,17 +543,42 @@ __global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
 #define slab(tk, c) vp_smem[(tk) * ld + (c)]
   const int64_t BT = (int64_t)p.B * p.T;
   const int64_t j0 = (int64_t)blockIdx.x * 16;
-  // load 16 tokens x all channels (zeros past the end: the reference pads B*T to x16)
-  for (int idx = threadIdx.x; idx < 16 * HDn; idx += VP_THREADS) {
-    const int tk = idx / HDn, c = idx - tk * HDn;
-    const int64_t jj = j0 + tk;
-    float x = 0.0f;
-    if (jj < BT) {
-      const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
-      const int h = c / p.D, d = c - h * p.D;
-      x = In<DT>::f(reinterpret_cast<const T*>(p.v)[(int64_t)b * p.sB + (int64_t)h * p.sH + (int64_t)t * p.sT + d]);
+  // load 16 tokens x all channels (zeros past the end: the reference pads B*T to x16);
+  // 8 consecutive channels of one head per 16-byte load when D % 8 == 0
+  const int dv = p.D / 8;
+  if (p.vec && DT != FP4_DT_F32) {
+    for (int idx = threadIdx.x; idx < 16 * p.Hkv * dv; idx += VP_THREADS) {
+      const int tk = idx / (p.Hkv * dv);
+      const int rem = idx - tk * (p.Hkv * dv);
+      const int h = rem / dv, d0 = (rem - h * dv) * 8;
+      const int64_t jj = j0 + tk;
+      float x[8];
+      if (jj < BT) {
+        const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + (int64_t)b * p.sB +
+                                                              (int64_t)h * p.sH + (int64_t)t * p.sT + d0));
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = In<DT>::f(e[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) slab(tk, h * p.D + d0 + k) = x[k];
     }
-    slab(tk, c) = x;
+  } else {
+    for (int idx = threadIdx.x; idx < 16 * HDn; idx += VP_THREADS) {
+      const int tk = idx / HDn, c = idx - tk * HDn;
+      const int64_t jj = j0 + tk;
+      float x = 0.0f;
+      if (jj < BT) {
+        const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
+        const int h = c / p.D, d = c - h * p.D;
+        x = In<DT>::f(reinterpret_cast<const T*>(p.v)[(int64_t)b * p.sB + (int64_t)h * p.sH + (int64_t)t * p.sT + d]);
+      }
+      slab(tk, c) = x;
+    }
   }
   __syncthreads();
   // per-token global scale: colmax of v2d.T * recip(1536) (fp4_quant_utils.py:136,139)
@@ -494,21 +610,44 @@ __global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
     const float rs = recip<FP4_ARITH_F32>(s);
     const bool nan_block = (sb & 0x7F) == 0x7F;
     const int h = c / p.D, d = c - h * p.D;
+    float vh[16];
 #pragma unroll
     for (int i = 0; i < 16; i += 2) {
       const float a0 = __fmaf_rn(x[i], rs, 0.0f), a1 = __fmaf_rn(x[i + 1], rs, 0.0f);
       const uint32_t byte = nan_block ? 0u : e2m1x2(a0, a1);
+      vh[i] = mul<FP4_ARITH_F32>(mul<FP4_ARITH_F32>(e2m1_value(byte & 15u), s), gtok[i]);
+      vh[i + 1] = mul<FP4_ARITH_F32>(mul<FP4_ARITH_F32>(e2m1_value(byte >> 4), s), gtok[i + 1]);
+    }
+    __half hi[16], lo[16];
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int64_t jj = j0 + i + k;
+    for (int i = 0; i < 16; ++i) {
+      hi[i] = __float2half_rn(vh[i]);
+      lo[i] = __float2half_rn(vh[i] - __half2float(hi[i]));
+    }
+    const int b0 = (int)(j0 / p.T), t0 = (int)(j0 - (int64_t)b0 * p.T);
+    if (j0 + 16 <= BT && t0 + 16 <= p.T && t0 % 8 == 0 && p.Tp % 8 == 0) {
+      // 16 tokens of one batch, contiguous in the output row: 16-byte stores
+      const int64_t o = ((int64_t)(b0 * p.Hkv + h) * p.D + d) * p.Tp + t0;
+      uint4* h4 = reinterpret_cast<uint4*>(p.hi + o);
+      uint4* l4 = reinterpret_cast<uint4*>(p.lo + o);
+      h4[0] = *reinterpret_cast<const uint4*>(&hi[0]);
+      h4[1] = *reinterpret_cast<const uint4*>(&hi[8]);
+      l4[0] = *reinterpret_cast<const uint4*>(&lo[0]);
+      l4[1] = *reinterpret_cast<const uint4*>(&lo[8]);
+      if (p.vhat) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) p.vhat[o + i] = vh[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int64_t jj = j0 + i;
         if (jj >= BT) continue;
-        const float vh = mul<FP4_ARITH_F32>(mul<FP4_ARITH_F32>(e2m1_value((byte >> (4 * k)) & 15u), s), gtok[i + k]);
         const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
         const int64_t o = ((int64_t)(b * p.Hkv + h) * p.D + d) * p.Tp + t;
-        const __half hi = __float2half_rn(vh);
-        p.hi[o] = hi;
-        p.lo[o] = __float2half_rn(vh - __half2float(hi));
-        if (p.vhat) p.vhat[o] = vh;
+        p.hi[o] = hi[i];
+        p.lo[o] = lo[i];
+        if (p.vhat) p.vhat[o] = vh[i];
       }
     }
   }
@@ -555,8 +694,11 @@ extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, in
     if (cudaMemsetAsync(v_hi, 0, bytes, st) != cudaSuccess || cudaMemsetAsync(v_lo, 0, bytes, st) != cudaSuccess)
       return set_error(FP4ATTN_ERR_CUDA, "memset");
   }
+  const int esz = in_dtype == FP4_DT_F32 ? 4 : 2;
+  const int vec = (D % 8 == 0) && ((uintptr_t)v % 16 == 0) && ((sB * esz) % 16 == 0) && ((sH * esz) % 16 == 0) &&
+                  ((sT * esz) % 16 == 0);
   VPrepArgs a{v, in_dtype, sB, sH, sT, B, Hkv, T, D, Tp, reinterpret_cast<__half*>(v_hi),
-              reinterpret_cast<__half*>(v_lo), vhat, g};
+              reinterpret_cast<__half*>(v_lo), vhat, g, vec};
   return launch_vprep(a, st);
 }
 

@@ -32,7 +32,7 @@
 namespace fp4 {
 
 constexpr int kThreads = 128;
-constexpr int MAXB = 4;
+constexpr int MAXB = 2;  // 16-element blocks a thread keeps in registers
 
 struct QuantArgs {
   const void* x;
@@ -144,12 +144,27 @@ __device__ __forceinline__ void mulz2(float& a, float& b, float s) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(z));
 }
 
+// Eight floats -> one word of E2M1 codes (element k in nibble k), RNE, satfinite.
+__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return r;
+}
+
 // Quantize one block of 16 (values already in the dequant dtype, before the
 // global scale) and write its codes / scale byte / dequantized values.
 // COLG: per-column global scale (column mode), else the scalar g / rg
 // (row and tensor modes; none mode runs with g = rg = 1, which is exact).
 template <int A, int ODT, bool COLG, bool OUT>
-__device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int64_t orow, int kb, float g, float rg) {
+__device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int64_t orow, int kb, float g, float rg,
+                                            const float* rcp_tab) {
   const float r6 = recip<A>(6.0f);
   if constexpr (COLG) {
 #pragma unroll
@@ -164,7 +179,7 @@ __device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int
   const float amax = block_absmax(v);
   const uint8_t sb = e4m3_torch(mul<A>(amax, r6));
   const float s = e4m3_to_f32(sb);
-  const float rs = recip<A>(s);
+  const float rs = rcp_tab[sb & 0x7F];  // recip<A>(s); sb < 0x80 (amax >= 0)
   const bool nan_block = (sb & 0x7F) == 0x7F;
   if constexpr (A == FP4_ARITH_F32) {
 #pragma unroll
@@ -174,14 +189,8 @@ __device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int
     for (int j = 0; j < 16; ++j) v[j] = rnd<A>(__fmaf_rn(v[j], rs, 0.0f));
   }
   uint32_t w[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint32_t b0 = e2m1x2(v[8 * h + 0], v[8 * h + 1]);
-    const uint32_t b1 = e2m1x2(v[8 * h + 2], v[8 * h + 3]);
-    const uint32_t b2 = e2m1x2(v[8 * h + 4], v[8 * h + 5]);
-    const uint32_t b3 = e2m1x2(v[8 * h + 6], v[8 * h + 7]);
-    w[h] = nan_block ? 0u : (b0 | (b1 << 8) | (b2 << 16) | (b3 << 24));
-  }
+  w[0] = nan_block ? 0u : e2m1x8(v);
+  w[1] = nan_block ? 0u : e2m1x8(v + 8);
   if (p.codes) {
     *reinterpret_cast<uint2*>(p.codes + orow * p.codes_ld + (int64_t)kb * 8) = make_uint2(w[0], w[1]);
   }
@@ -205,10 +214,16 @@ __device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int
 }
 
 template <int DT, int A, int ODT, int TPR, bool COLG, bool OUT>
-__global__ void __launch_bounds__(kThreads) quant_rows_kernel(QuantArgs p) {
+__global__ void __launch_bounds__(kThreads, 8) quant_rows_kernel(QuantArgs p) {
   constexpr int ROWS = kThreads / TPR;
   constexpr int WPR = TPR / 32;  // warps per row
   __shared__ float red[kThreads / 32];
+  __shared__ float rcp_tab[128];  // recip<A> of every non-negative E4M3 scale byte
+  {
+    const float sv = e4m3_to_f32((uint8_t)threadIdx.x);
+    rcp_tab[threadIdx.x] = recip<A>(sv);
+  }
+  __syncthreads();
   const int rloc = threadIdx.x / TPR;
   const int lane = threadIdx.x % TPR;
   const int64_t orow = (int64_t)blockIdx.x * ROWS + rloc;
@@ -266,11 +281,11 @@ __global__ void __launch_bounds__(kThreads) quant_rows_kernel(QuantArgs p) {
   const float rg = p.gmode == 0 ? 1.0f : recip<A>(g);
 #pragma unroll
   for (int i = 0; i < MAXB; ++i)
-    if (i < nmine) quant_block<A, ODT, COLG, OUT>(cache[i], p, orow, lane + i * TPR, g, rg);
+    if (i < nmine) quant_block<A, ODT, COLG, OUT>(cache[i], p, orow, lane + i * TPR, g, rg, rcp_tab);
   for (int i = MAXB; i < nmine; ++i) {
     float v[16];
     load_block<DT, A>(v, p, b, t, lane + i * TPR);
-    quant_block<A, ODT, COLG, OUT>(v, p, orow, lane + i * TPR, g, rg);
+    quant_block<A, ODT, COLG, OUT>(v, p, orow, lane + i * TPR, g, rg, rcp_tab);
   }
 }
 
@@ -341,8 +356,11 @@ static int launch_rows(const QuantArgs& p, cudaStream_t st) {
   const int64_t n = (int64_t)p.H * p.D;
   const int64_t nblk = (n + 15) / 16;
   const int64_t nrows = (int64_t)p.B * p.T_pad;
-  if (nblk <= 64) {
+  // threads per row: enough that each thread owns at most MAXB blocks when possible
+  if (nblk <= 32 * MAXB) {
     quant_rows_kernel<DT, A, ODT, 32, COLG, OUT><<<(unsigned)((nrows + 3) / 4), kThreads, 0, st>>>(p);
+  } else if (nblk <= 64 * MAXB) {
+    quant_rows_kernel<DT, A, ODT, 64, COLG, OUT><<<(unsigned)((nrows + 1) / 2), kThreads, 0, st>>>(p);
   } else {
     quant_rows_kernel<DT, A, ODT, 128, COLG, OUT><<<(unsigned)nrows, kThreads, 0, st>>>(p);
   }

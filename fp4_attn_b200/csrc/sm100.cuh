@@ -79,16 +79,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase with `parity` has completed.  Bounded: after kWaitNs
-// (or once another wait in the grid failed) it records `site` and returns false.
+// (or once another wait in the grid failed) it records `site` and returns
+// false.  The global failure flag and the timer are polled only every 64
+// spins so the common hand-off stays a tight try_wait loop.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (dev_failed()) return false;
-    if (globaltimer() - t0 > kWaitNs) {
-      dev_fail(site);
-      return false;
+    if ((i & 63) == 0) {
+      if (dev_failed()) return false;
+      if (globaltimer() - t0 > kWaitNs) {
+        dev_fail(site);
+        return false;
+      }
     }
   }
 }

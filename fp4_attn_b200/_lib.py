@@ -28,6 +28,7 @@ SIGNATURES = {
     "fp4attn_launch_count": ([], ctypes.c_ulonglong),
     "fp4attn_device_status": ([_I], ctypes.c_uint),
     "fp4_gemm_nvf4": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _P], _I),
+    "fp4attn_set_trace": ([_P], None),
     "fp4attn_prepare_v": ([_P, _I, _I, _I, _I, _I, _L, _L, _L, _I, _P, _P, _P, _P, _P], _I),
     "fp4attn_fwd_packed": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P], _I),
     "nvfp4sim_f32_to_nvf4": ([_P, _P, _P, _L, _P], _I),

@@ -42,22 +42,26 @@ FP4_DEFINE_STATUS_READER(attn_status)
 
 namespace attn {
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int NK = 3, NV = 2;
-constexpr int THREADS = 384;
+constexpr int NK = 4;   // K stages (codes + scale atoms + g)
+constexpr int NVH = 4;  // V half-tile stages (64 keys x hi/lo planes)
+constexpr int NWG = 4;  // softmax warpgroups; warpgroup q owns key columns 32q .. 32q+31
+constexpr int THREADS = 128 + NWG * 128;
 // shared memory map (bytes, all pieces 1024-aligned where TMA/UMMA need it)
 constexpr int Q_BYTES = BM * HD / 2;  // 8 KB of E2M1 codes
 constexpr int OFF_Q = 0, OFF_QSF = 8192, OFF_GQ = 9216;
 constexpr int K_STAGE = 10240;  // codes 8 KB, scale atoms 1 KB, gk 512 B
 constexpr int OFF_K = 10240;
-constexpr int V_HALF = HD * 64 * 2;  // 128 rows (d) x 64 keys x fp16
-constexpr int V_STAGE = 4 * V_HALF;  // hi keys 0-63, hi 64-127, lo 0-63, lo 64-127
+constexpr int V_HALF = HD * 64 * 2;  // 128 rows (d) x 64 keys x fp16 = one plane of a half tile
+constexpr int V_STAGE = 2 * V_HALF;  // hi plane, lo plane of 64 keys
 constexpr int OFF_V = OFF_K + NK * K_STAGE;
-constexpr int OFF_STAT = OFF_V + NV * V_STAGE;  // m[2][128], l[2][128]
-constexpr int OFF_RCP = OFF_STAT + 4 * 128 * 4;
+constexpr int OFF_STAT = OFF_V + NVH * V_STAGE;  // m[NWG][128], l[NWG][128]
+constexpr int OFF_RCP = OFF_STAT + 2 * NWG * 128 * 4;
 constexpr int OFF_BAR = OFF_RCP + 128 * 4;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t T_S = 0, T_O = 256, T_SFA = 384, T_SFB = 392;
+// TMEM columns: S0, S1 (fp32 scores), P (fp16 Phat, NWG quarters of 16 columns),
+// O (fp32 accumulator), Q scales, K scales per stage.
+constexpr uint32_t T_S = 0, T_P = 256, T_O = 320, T_SFA = 448, T_SFB = 456;
 }  // namespace attn
 
 struct AttnArgs {
@@ -70,7 +74,32 @@ struct AttnArgs {
   int causal;
   float scale_log2;  // scaling * log2(e)
   int units;
+  long long* trace;  // optional event timeline (fp4attn_set_trace), [grid][kTraceSlots]
 };
+
+// Timeline slots recorded for each CTA's first work unit when tracing is on.
+constexpr int kTraceSlots = 512;
+enum TraceSlot {
+  TR_QK = 0,        // + pass*32 + j : MMA issued QK (after its waits)
+  TR_PV = 64,       // + j : MMA issued PV
+  TR_PWAIT = 96,    // + j : MMA starts waiting for P
+  TR_SFULL = 128,   // + pass*32 + j : softmax saw S ready
+  TR_PDONE = 192,   // + j : softmax finished P (pass 2)
+  TR_MDONE = 224,   // + j : softmax finished the tile (pass 1)
+  TR_UNIT = 256,    // MMA saw Q ready
+  TR_OFULL = 257,   // epilogue saw O ready
+  TR_OFREE = 258,   // epilogue released O
+  TR_UEND = 259,    // MMA committed the unit
+  TR_START = 260,   // kernel start (after setup)
+  TR_LDDONE = 288,  // + j : pass-2 scores in registers (warpgroup 0)
+  TR_COMP = 320,    // + j : pass-2 Phat computed (warpgroup 0)
+  TR_PFREE = 352,   // + j : pass-2 P quarter free (warpgroup 0)
+};
+
+__device__ __forceinline__ void trace(const AttnArgs& p, uint32_t uc, int slot, int j) {
+  if (p.trace && uc == 0 && j < 32 && slot + j < kTraceSlots)
+    p.trace[(int64_t)blockIdx.x * kTraceSlots + slot + j] = (long long)globaltimer();
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -229,21 +258,22 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* stat_m = reinterpret_cast<float*>(sm + OFF_STAT);
-  float* stat_l = stat_m + 256;
+  float* stat_l = stat_m + NWG * 128;
   float* rcp = reinterpret_cast<float*>(sm + OFF_RCP);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bar + 0;
   uint64_t* q_empty = bar + 1;
   uint64_t* k_full = bar + 2;    // [NK]
-  uint64_t* k_empty = bar + 5;   // [NK]
-  uint64_t* v_full = bar + 8;    // [NV]
-  uint64_t* v_empty = bar + 10;  // [NV]
-  uint64_t* s_full = bar + 12;   // [2]
-  uint64_t* buf_free = bar + 14; // [2]
-  uint64_t* p_full = bar + 16;   // [2]
-  uint64_t* o_full = bar + 18;
-  uint64_t* o_free = bar + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 20);
+  uint64_t* k_empty = bar + 6;   // [NK]
+  uint64_t* v_full = bar + 10;   // [NVH]
+  uint64_t* v_empty = bar + 14;  // [NVH]
+  uint64_t* s_full = bar + 18;   // [2] S buffer written (MMA commit)
+  uint64_t* s_free = bar + 20;   // [2] S buffer read by every softmax warpgroup
+  uint64_t* p_full = bar + 22;   // [NWG] P quarter q written by warpgroup q
+  uint64_t* p_free = bar + 26;   // [NWG] PV of P quarter q done (MMA commit)
+  uint64_t* o_full = bar + 30;
+  uint64_t* o_free = bar + 31;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 32);
 
   const int warp = threadIdx.x / 32;
   const int nkb4q = p.Hq * 2, nkb4k = p.Hkv * 2;
@@ -254,16 +284,19 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     mbar_init(q_empty, 1);
     for (int i = 0; i < NK; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 2);  // MMA commit + the softmax warpgroup that read gk
+      mbar_init(&k_empty[i], 1 + NWG);  // MMA commit + every softmax warpgroup (they read gk)
     }
-    for (int i = 0; i < NV; ++i) {
+    for (int i = 0; i < NVH; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&buf_free[i], 1);
+      mbar_init(&s_free[i], NWG);
+    }
+    for (int i = 0; i < NWG; ++i) {
       mbar_init(&p_full[i], 1);
+      mbar_init(&p_free[i], 1);
     }
     mbar_init(o_full, 1);
     mbar_init(o_free, 1);
@@ -282,15 +315,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) trace(p, 0, TR_START, 0);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------- producer: Q and K
     if (elect_one_lane()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmVhi);
-      tma_prefetch_desc(&tmVlo);
-      uint32_t kc = 0, vc = 0, uc = 0;
+      uint32_t kc = 0, uc = 0;
       for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
@@ -311,18 +343,28 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             tma_load_2d(ks, &tmK, &k_full[s], hk * (HD / 2), krow);
             bulk_load(ks + 8192, p.ksf + ((int64_t)(krow / 128) * nkb4k + 2 * hk) * 512, 1024, &k_full[s]);
             bulk_load(ks + 9216, p.gk + krow, 512, &k_full[s]);
-            if (pass == 1) {
-              const int vs = vc % NV;
-              if (vc >= NV) mbar_wait(&v_empty[vs], ((vc / NV) - 1) & 1, 0x203);
-              uint8_t* v = sm + OFF_V + vs * V_STAGE;
-              const int vrow = (un.b * p.Hkv + hk) * HD;
-              mbar_arrive_expect_tx(&v_full[vs], V_STAGE);
-              tma_load_2d(v, &tmVhi, &v_full[vs], j * BN, vrow);
-              tma_load_2d(v + V_HALF, &tmVhi, &v_full[vs], j * BN + 64, vrow);
-              tma_load_2d(v + 2 * V_HALF, &tmVlo, &v_full[vs], j * BN, vrow);
-              tma_load_2d(v + 3 * V_HALF, &tmVlo, &v_full[vs], j * BN + 64, vrow);
-              ++vc;
-            }
+          }
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------ producer: V half tiles (pass 2)
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmVhi);
+      tma_prefetch_desc(&tmVlo);
+      uint32_t vc = 0;
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const Unit un = unit_of(u, p);
+        const int n = kv_tiles(un, p);
+        const int vrow = (un.b * p.Hkv + un.h / group) * HD;
+        for (int j = 0; j < n; ++j) {
+          for (int half = 0; half < 2; ++half, ++vc) {
+            const int vs = vc % NVH;
+            if (vc >= NVH) mbar_wait(&v_empty[vs], ((vc / NVH) - 1) & 1, 0x203);
+            uint8_t* v = sm + OFF_V + vs * V_STAGE;
+            mbar_arrive_expect_tx(&v_full[vs], V_STAGE);
+            tma_load_2d(v, &tmVhi, &v_full[vs], j * BN + 64 * half, vrow);
+            tma_load_2d(v + V_HALF, &tmVlo, &v_full[vs], j * BN + 64 * half, vrow);
           }
         }
       }
@@ -333,18 +375,19 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const uint32_t idq = idesc_nvf4(BM, BN);
       const uint32_t idv = idesc_f16(BM, HD);
       uint32_t kc = 0, vc = 0, uc = 0;
-      uint32_t use[2] = {0, 0}, pu[2] = {0, 0};
-      auto issue_qk = [&](int j, int kbuf) {
-        // buffer kbuf: wait until its previous use was released
-        if (use[kbuf] > 0) mbar_wait(&buf_free[kbuf], (use[kbuf] - 1) & 1, 0x211);
+      uint32_t suse[2] = {0, 0}, pu[NWG] = {0, 0, 0, 0};
+      auto issue_qk = [&](int j, int kb, int pass) {
+        // S buffer kb: its previous scores must have been read by every warpgroup
+        if (suse[kb] > 0) mbar_wait(&s_free[kb], (suse[kb] - 1) & 1, 0x211);
         const int s = kc % NK;
         mbar_wait(&k_full[s], (kc / NK) & 1, 0x212);
         tc_fence_after();
+        trace(p, uc, TR_QK + 32 * pass, j);
         uint8_t* ks = sm + OFF_K + s * K_STAGE;
         const uint32_t sfb = tmem + T_SFB + 8 * s;
         tmem_cp_sf_atom(sfb, smem_desc(smem_u32(ks + 8192), 16, 128, kSwizzleNone));
         tmem_cp_sf_atom(sfb + 4, smem_desc(smem_u32(ks + 8192 + 512), 16, 128, kSwizzleNone));
-        const uint32_t d = tmem + T_S + 128 * kbuf;
+        const uint32_t d = tmem + T_S + 128 * kb;
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
           const uint64_t ad = smem_desc(smem_u32(sm + OFF_Q) + kk * 32, 16, 512, kSwizzle64B);
@@ -352,157 +395,173 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           mma_nvf4(d, ad, bd, idq, tmem + T_SFA + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
         }
         tc_commit(&k_empty[s]);
-        tc_commit(&s_full[kbuf]);
-        ++use[kbuf];
+        tc_commit(&s_full[kb]);
+        ++suse[kb];
         ++kc;
       };
       for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         mbar_wait(q_full, uc & 1, 0x213);
+        trace(p, uc, TR_UNIT, 0);
         tc_fence_after();
         tmem_cp_sf_atom(tmem + T_SFA, smem_desc(smem_u32(sm + OFF_QSF), 16, 128, kSwizzleNone));
         tmem_cp_sf_atom(tmem + T_SFA + 4, smem_desc(smem_u32(sm + OFF_QSF + 512), 16, 128, kSwizzleNone));
-        // pass 1: scores only (the softmax groups release each buffer after reading it)
-        for (int j = 0; j < n; ++j) issue_qk(j, j & 1);
-        // pass 2: scores again, then PV once P is in TMEM
-        issue_qk(0, 0);
+        // pass 1: scores only
+        for (int j = 0; j < n; ++j) issue_qk(j, j & 1, 0);
+        // pass 2: scores again, then PV one key quarter at a time as each P quarter lands
+        issue_qk(0, 0, 1);
         for (int j = 0; j < n; ++j) {
-          const int kb = j & 1;
-          if (j + 1 < n) issue_qk(j + 1, (j + 1) & 1);
-          mbar_wait(&p_full[kb], pu[kb] & 1, 0x214);
-          ++pu[kb];
-          const int vs = vc % NV;
-          mbar_wait(&v_full[vs], (vc / NV) & 1, 0x215);
-          if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
-          tc_fence_after();
-          uint8_t* v = sm + OFF_V + vs * V_STAGE;
-          const uint32_t a = tmem + T_S + 128 * kb;
+          if (j + 1 < n) issue_qk(j + 1, (j + 1) & 1, 1);
 #pragma unroll
-          for (int part = 0; part < 2; ++part) {  // hi, lo
+          for (int q = 0; q < NWG; ++q) {
+            const int vs = vc % NVH;  // half tile q/2 of this key tile
+            if ((q & 1) == 0) mbar_wait(&v_full[vs], (vc / NVH) & 1, 0x215);
+            if (q == 0) trace(p, uc, TR_PWAIT, j);
+            mbar_wait(&p_full[q], pu[q] & 1, 0x214);
+            ++pu[q];
+            if (j == 0 && q == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
+            tc_fence_after();
+            if (q == 0) trace(p, uc, TR_PV, j);
+            uint8_t* v = sm + OFF_V + vs * V_STAGE;
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint32_t vb = smem_u32(v + part * 2 * V_HALF + (kk >> 2) * V_HALF) + (kk & 3) * 32;
-              mma_f16_ts(tmem + T_O, a + 8 * kk, smem_desc(vb, 16, 1024, kSwizzle128B), idv,
-                         (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+            for (int part = 0; part < 2; ++part) {  // hi, lo planes
+#pragma unroll
+              for (int kk = 2 * q; kk < 2 * q + 2; ++kk) {  // keys 16kk .. 16kk+15
+                const uint32_t vb = smem_u32(v + part * V_HALF) + (kk & 3) * 32;
+                mma_f16_ts(tmem + T_O, tmem + T_P + 8 * kk, smem_desc(vb, 16, 1024, kSwizzle128B), idv,
+                           (j > 0 || q > 0 || part > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            tc_commit(&p_free[q]);
+            if (q & 1) {
+              tc_commit(&v_empty[vs]);
+              ++vc;
             }
           }
-          tc_commit(&v_empty[vs]);
-          tc_commit(&buf_free[kb]);
-          ++vc;
         }
         tc_commit(o_full);
         tc_commit(q_empty);
+        trace(p, uc, TR_UEND, 0);
       }
     }
   } else if (warp >= 4) {
     // ------------------------------------------------- softmax warpgroups
-    const int wg = (warp - 4) >> 2;  // 0 or 1: takes key tiles j with j % 2 == wg
+    // Every warpgroup works on every key tile: warpgroup q owns key columns
+    // 32q .. 32q+31 (its quarter of S, its quarter of P).
+    const int q = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + (threadIdx.x & 31);  // row of the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t sbuf = tmem + lane_base + T_S + 128 * wg;
     const float r6 = __frcp_rn(6.0f);
-    uint32_t kc = 0, uc = 0, su = 0;
+    const bool leader = threadIdx.x % 128 == 0;
+    const int col0 = 32 * q;
+    uint32_t kc = 0, uc = 0, pt = 0;
+    uint32_t sfu[2] = {0, 0};
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
       const Unit un = unit_of(u, p);
       const int n = kv_tiles(un, p);
       const int qpos = un.qt * BM + r;  // query index within the sequence
       mbar_wait(q_full, uc & 1, 0x221);
       const float uscale = reinterpret_cast<const float*>(sm + OFF_GQ)[r] * p.scale_log2;
-      // ---- pass 1: row maximum of z = acc * gk (S = z * gq * scaling)
+      // ---- pass 1: row maximum of z = acc * gk over this quarter's keys
       float m = -INFINITY;
       for (int j = 0; j < n; ++j, ++kc) {
-        if ((j & 1) != wg) continue;
-        const int s = kc % NK;
-        mbar_wait(&s_full[wg], su & 1, 0x222);
-        ++su;
+        const int kb = j & 1, s = kc % NK;
+        mbar_wait(&s_full[kb], sfu[kb] & 1, 0x222);
+        ++sfu[kb];
+        if (leader && q == 0) trace(p, uc, TR_SFULL, j);
         tc_fence_after();
-        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216);
+        uint32_t a[32];
+        tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
+        tmem_ld_wait();
+        tc_fence_before();
+        named_bar(1 + q, 128);
+        if (leader) mbar_arrive(&s_free[kb]);
+        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
         // keys with column > lim are masked (causal diagonal tile, or keys past T)
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
-        uint32_t a[2][32];
-        tmem_ld32(sbuf, a[0]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(sbuf + (c + 1) * 32, a[(c + 1) & 1]);
-          if (lim < 127) m = chunk_max<true>(a[c & 1], gk + 32 * c, 32 * c, lim, m);
-          else m = chunk_max<false>(a[c & 1], gk + 32 * c, 32 * c, lim, m);
-          if (c < 3) tmem_ld_wait();
-        }
-        tc_fence_before();
-        named_bar(1 + wg, 128);
-        if (threadIdx.x % 128 == 0) {
-          mbar_arrive(&buf_free[wg]);
+        if (lim < col0 + 31) m = chunk_max<true>(a, gk, col0, lim, m);
+        else m = chunk_max<false>(a, gk, col0, lim, m);
+        named_bar(1 + q, 128);
+        if (leader) {
           mbar_arrive(&k_empty[s]);
+          if (q == 0) trace(p, uc, TR_MDONE, j);
         }
       }
-      stat_m[wg * 128 + r] = m;
-      named_bar(3, 256);
-      m = fmaxf(stat_m[r], stat_m[128 + r]);
+      stat_m[q * 128 + r] = m;
+      named_bar(1 + NWG, NWG * 128);
+#pragma unroll
+      for (int w = 0; w < NWG; ++w) m = fmaxf(m, stat_m[w * 128 + r]);
       const float mu = m == -INFINITY ? 0.0f : m * uscale;
       const uint64_t u2 = pk2(uscale, uscale), nmu2 = pk2(-mu, -mu);
-      // ---- pass 2: e = exp2(z*u - m*u), sum, NVFP4 fake-quant of e -> TMEM
+      // ---- pass 2: e = exp2(z*u - m*u), sum, NVFP4 fake-quant of e -> P quarter q
       uint64_t lsum2[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
       for (int j = 0; j < n; ++j, ++kc) {
-        if ((j & 1) != wg) continue;
-        const int s = kc % NK;
-        mbar_wait(&s_full[wg], su & 1, 0x223);
-        ++su;
+        const int kb = j & 1, s = kc % NK;
+        mbar_wait(&s_full[kb], sfu[kb] & 1, 0x223);
+        ++sfu[kb];
+        if (leader && q == 0) trace(p, uc, TR_SFULL + 32, j);
         tc_fence_after();
-        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216);
-        const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
-        uint32_t a[2][32];
-        tmem_ld32(sbuf, a[0]);
+        uint32_t a[32];
+        tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
         tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(sbuf + (c + 1) * 32, a[(c + 1) & 1]);
-          uint32_t pk[16];
-          if (lim < 127) chunk_p<true>(a[c & 1], gk + 32 * c, 32 * c, lim, u2, nmu2, rcp, r6, lsum2, pk);
-          else chunk_p<false>(a[c & 1], gk + 32 * c, 32 * c, lim, u2, nmu2, rcp, r6, lsum2, pk);
-          // Phat for keys 32c..32c+31 -> TMEM columns 16c..16c+15 of this buffer
-          // (S chunk c/2, already read)
-          tmem_st16(sbuf + c * 16, pk);
-          if (c < 3) tmem_ld_wait();
+        // this quarter's scores are in registers: release the S buffer now
+        tc_fence_before();
+        named_bar(1 + q, 128);
+        if (leader) {
+          mbar_arrive(&s_free[kb]);
+          if (q == 0) trace(p, uc, TR_LDDONE, j);
         }
+        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
+        const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
+        uint32_t pk[16];
+        if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
+        else chunk_p<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
+        if (leader && q == 0) trace(p, uc, TR_COMP, j);
+        // P quarter q may be overwritten once the previous tile's PV on it is done
+        if (pt > 0) mbar_wait(&p_free[q], (pt - 1) & 1, 0x225);
+        if (leader && q == 0) trace(p, uc, TR_PFREE, j);
+        tc_fence_after();
+        tmem_st16(tmem + lane_base + T_P + 16 * q, pk);
         tmem_st_wait();
         tc_fence_before();
-        named_bar(1 + wg, 128);
-        if (threadIdx.x % 128 == 0) {
-          mbar_arrive(&p_full[wg]);
+        named_bar(1 + q, 128);
+        if (leader) {
+          mbar_arrive(&p_full[q]);
           mbar_arrive(&k_empty[s]);
+          if (q == 0) trace(p, uc, TR_PDONE, j);
         }
+        ++pt;
       }
       float l0, l1;
       upk2(add2(add2(lsum2[0], lsum2[1]), add2(lsum2[2], lsum2[3])), l0, l1);
-      stat_l[wg * 128 + r] = l0 + l1;
-      named_bar(3, 256);
-      const float l = stat_l[r] + stat_l[128 + r];
-      // ---- epilogue: O rows / l, columns 64*wg .. 64*wg+63
+      stat_l[q * 128 + r] = l0 + l1;
+      named_bar(1 + NWG, NWG * 128);
+      float l = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NWG; ++w) l += stat_l[w * 128 + r];
+      // ---- epilogue: O rows / l, columns 32q .. 32q+31
       mbar_wait(o_full, uc & 1, 0x224);
+      if (threadIdx.x == 128) trace(p, uc, TR_OFULL, 0);
       tc_fence_after();
       const float rl = 1.0f / l;
-      const bool store = qpos < p.T;
-      float* dst = p.out + (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + 64 * wg;
-      uint32_t a[2][32];
-      tmem_ld32(tmem + lane_base + T_O + 64 * wg, a[0]);
-      tmem_ld32(tmem + lane_base + T_O + 64 * wg + 32, a[1]);
+      uint32_t a[32];
+      tmem_ld32(tmem + lane_base + T_O + col0, a);
       tmem_ld_wait();
-      if (store) {
+      if (qpos < p.T) {
+        float4* d4 = reinterpret_cast<float4*>(p.out + (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + col0);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(__uint_as_float(a[c][4 * i]) * rl, __uint_as_float(a[c][4 * i + 1]) * rl,
-                                __uint_as_float(a[c][4 * i + 2]) * rl, __uint_as_float(a[c][4 * i + 3]) * rl);
-        }
+        for (int i = 0; i < 8; ++i)
+          d4[i] = make_float4(__uint_as_float(a[4 * i]) * rl, __uint_as_float(a[4 * i + 1]) * rl,
+                              __uint_as_float(a[4 * i + 2]) * rl, __uint_as_float(a[4 * i + 3]) * rl);
       }
       tc_fence_before();
-      named_bar(3, 256);
-      if (threadIdx.x == 128) mbar_arrive(o_free);
+      named_bar(1 + NWG, NWG * 128);
+      if (threadIdx.x == 128) {
+        mbar_arrive(o_free);
+        trace(p, uc, TR_OFREE, 0);
+      }
     }
   }
   tc_fence_before();
@@ -681,6 +740,13 @@ static int launch_vprep(const VPrepArgs& a, cudaStream_t st) {
 
 using namespace fp4;
 
+static long long* g_trace = nullptr;
+
+// Profiling aid: when buf is non-null, the next fp4attn_fwd_packed calls
+// write an event timeline (globaltimer ns) of each CTA's first work unit into
+// buf[cta * 512 + slot]; buf needs grid * 512 int64 entries.
+extern "C" void fp4attn_set_trace(long long* buf) { g_trace = buf; }
+
 extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, int T, int D, int64_t sB, int64_t sH,
                                  int64_t sT, int Tp, uint16_t* v_hi, uint16_t* v_lo, float* vhat, float* g,
                                  void* stream) {
@@ -743,6 +809,7 @@ extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scale
   a.causal = causal ? 1 : 0;
   a.scale_log2 = scaling * 1.4426950408889634f;
   a.units = B * Hq * (Tp / 128);
+  a.trace = g_trace;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(fp4_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);

@@ -26,12 +26,17 @@
 //
 // Schedule.  A work unit is (batch, query head, 128-query tile); persistent
 // CTAs take units longest-first (causal cost grows with the tile index).
-// Warp 0 issues TMA, warp 1 issues tcgen05 MMAs, warps 4-7 and 8-11 are two
-// softmax warpgroups that take alternate 128-key tiles (S double-buffered in
-// TMEM), warps 2-3 are idle.  Every wait is bounded (sm100.cuh).
+// Warp 0 loads Q and K by TMA (codes, scale atoms, global scales), warp 2
+// loads V-hat half tiles, warp 1 issues the tcgen05 MMAs, and warps 4-19 are
+// four softmax warpgroups: warpgroup q owns key columns 32q..32q+31 of every
+// tile.  S is double-buffered in TMEM; each warpgroup writes its quarter of
+// P-hat over the S columns it has already loaded, so PV(j) reads P from S(j)'s
+// buffer and QK(j+2) reuses the buffer after it (in-order tensor pipe).  Every
+// wait is bounded (sm100.cuh).
 #include <cuda.h>
 
 #include "common.cuh"
+#include "attn_softmax.cuh"
 #include "sm100.cuh"
 #include "status.h"
 #include "tmap.h"
@@ -43,7 +48,7 @@ FP4_DEFINE_STATUS_READER(attn_status)
 namespace attn {
 constexpr int BM = 128, BN = 128, HD = 128;
 constexpr int NK = 4;   // K stages (codes + scale atoms + g)
-constexpr int NVH = 4;  // V half-tile stages (64 keys x hi/lo planes)
+constexpr int NV = 2;   // V-hat stages, one 128-key tile each (hi and lo planes)
 constexpr int NWG = 4;  // softmax warpgroups; warpgroup q owns key columns 32q .. 32q+31
 constexpr int THREADS = 128 + NWG * 128;
 // shared memory map (bytes, all pieces 1024-aligned where TMA/UMMA need it)
@@ -51,17 +56,17 @@ constexpr int Q_BYTES = BM * HD / 2;  // 8 KB of E2M1 codes
 constexpr int OFF_Q = 0, OFF_QSF = 8192, OFF_GQ = 9216;
 constexpr int K_STAGE = 10240;  // codes 8 KB, scale atoms 1 KB, gk 512 B
 constexpr int OFF_K = 10240;
-constexpr int V_HALF = HD * 64 * 2;  // 128 rows (d) x 64 keys x fp16 = one plane of a half tile
-constexpr int V_STAGE = 2 * V_HALF;  // hi plane, lo plane of 64 keys
+constexpr int V_HALF = HD * 64 * 2;  // 128 rows (d) x 64 keys x fp16 = one plane of a half tile (one TMA box)
+constexpr int V_STAGE = 4 * V_HALF;  // keys 0-63 hi, lo; keys 64-127 hi, lo
 constexpr int OFF_V = OFF_K + NK * K_STAGE;
-constexpr int OFF_STAT = OFF_V + NVH * V_STAGE;  // m[NWG][128], l[NWG][128]
+constexpr int OFF_STAT = OFF_V + NV * V_STAGE;  // m[NWG][128], l[NWG][128]
 constexpr int OFF_RCP = OFF_STAT + 2 * NWG * 128 * 4;
 constexpr int OFF_BAR = OFF_RCP + 128 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
-// TMEM columns: S0, S1 (fp32 scores), P (fp16 Phat, NWG quarters of 16 columns),
-// O (fp32 accumulator), Q scales, K scales per stage.
-constexpr uint32_t T_S = 0, T_P = 256, T_O = 320, T_SFA = 448, T_SFB = 456;
+// TMEM columns: S0, S1 (P of a tile is written over the first half of each warpgroup's S
+// columns once they are in registers), O, Q scale atoms, K scale atoms per stage.
+constexpr uint32_t T_S = 0, T_O = 256, T_SFA = 384, T_SFB = 392;
 }  // namespace attn
 
 struct AttnArgs {
@@ -93,142 +98,12 @@ enum TraceSlot {
   TR_START = 260,   // kernel start (after setup)
   TR_LDDONE = 288,  // + j : pass-2 scores in registers (warpgroup 0)
   TR_COMP = 320,    // + j : pass-2 Phat computed (warpgroup 0)
-  TR_PFREE = 352,   // + j : pass-2 P quarter free (warpgroup 0)
+  TR_PDONE3 = 384,  // + j : softmax warpgroup 3 finished P (pass 2)
 };
 
 __device__ __forceinline__ void trace(const AttnArgs& p, uint32_t uc, int slot, int j) {
   if (p.trace && uc == 0 && j < 32 && slot + j < kTraceSlots)
     p.trace[(int64_t)blockIdx.x * kTraceSlots + slot + j] = (long long)globaltimer();
-}
-
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// Two E2M1 codes (one byte) -> their fp16 values.
-__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
-  uint32_t r;
-  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(r) : "r"(byte));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-// Packed fp32 pairs (sm_100a f32x2 ALU ops, each lane rounded like the scalar op).
-__device__ __forceinline__ uint64_t pk2(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
-// E2M1 round-to-nearest-even of (x0, x1) -> fp16 code values times the block
-// scale (sh2 = the scale as two halves): code * scale is exact in fp16.
-__device__ __forceinline__ uint32_t quant_pair_f16(float x0, float x1, uint32_t sh2) {
-  uint32_t r;
-  asm("{\n\t.reg .b8 t;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, t;\n\t"
-      "mul.rn.f16x2 %0, %0, %3;\n\t}"
-      : "=r"(r)
-      : "f"(x0), "f"(x1), "r"(sh2));
-  return r;
-}
-
-// Pass 1 on one 32-key chunk: running max of z = acc * gk (keys with
-// column > lim masked when MASK).
-template <bool MASK>
-__device__ __forceinline__ float chunk_max(const uint32_t (&a)[32], const float* gk, int col0, int lim, float m) {
-  float z[32];
-  const float4* g4 = reinterpret_cast<const float4*>(gk);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float4 g = g4[q];
-    upk2(mul2(pk2(__uint_as_float(a[4 * q]), __uint_as_float(a[4 * q + 1])), pk2(g.x, g.y)), z[4 * q], z[4 * q + 1]);
-    upk2(mul2(pk2(__uint_as_float(a[4 * q + 2]), __uint_as_float(a[4 * q + 3])), pk2(g.z, g.w)), z[4 * q + 2],
-         z[4 * q + 3]);
-  }
-  if constexpr (MASK) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) z[i] = (col0 + i > lim) ? -INFINITY : z[i];
-  }
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) m = max3f(m, z[i], z[i + 1]);
-  return m;
-}
-
-// Pass 2 on one 32-key chunk: e = exp2(z*u - m*u), running sum, NVFP4
-// fake-quant of e in two blocks of 16 -> 16 words of fp16 pairs.
-template <bool MASK>
-__device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
-                                        uint64_t nmu2, const float* rcp, float r6, uint64_t (&lsum2)[4],
-                                        uint32_t (&pk)[16]) {
-  float e[32];
-  const float4* g4 = reinterpret_cast<const float4*>(gk);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float4 g = g4[q];
-    float t0, t1, t2, t3;
-    upk2(fma2(mul2(pk2(__uint_as_float(a[4 * q]), __uint_as_float(a[4 * q + 1])), pk2(g.x, g.y)), u2, nmu2), t0, t1);
-    upk2(fma2(mul2(pk2(__uint_as_float(a[4 * q + 2]), __uint_as_float(a[4 * q + 3])), pk2(g.z, g.w)), u2, nmu2), t2,
-         t3);
-    e[4 * q] = ex2(t0);
-    e[4 * q + 1] = ex2(t1);
-    e[4 * q + 2] = ex2(t2);
-    e[4 * q + 3] = ex2(t3);
-  }
-  if constexpr (MASK) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
-  }
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) lsum2[(i >> 1) & 3] = add2(lsum2[(i >> 1) & 3], pk2(e[i], e[i + 1]));
-#pragma unroll
-  for (int blk = 0; blk < 2; ++blk) {
-    const float* eb = e + 16 * blk;
-    const float m0 = max3f(eb[0], eb[1], eb[2]), m1 = max3f(eb[3], eb[4], eb[5]);
-    const float m2 = max3f(eb[6], eb[7], eb[8]), m3 = max3f(eb[9], eb[10], eb[11]);
-    const float m4 = max3f(eb[12], eb[13], eb[14]);
-    const float amax = fmaxf(max3f(m0, m1, m2), max3f(m3, m4, eb[15]));
-    const uint8_t sb = e4m3_satfinite(amax * r6);
-    const float rs = rcp[sb & 127];
-    const uint32_t sh2 = (uint32_t)__half_as_ushort(__float2half_rn(e4m3_to_f32(sb))) * 0x10001u;
-    const uint64_t rs2 = pk2(rs, rs);
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      float x0, x1;
-      upk2(mul2(pk2(eb[i], eb[i + 1]), rs2), x0, x1);
-      pk[8 * blk + i / 2] = quant_pair_f16(x0, x1, sh2);
-    }
-  }
 }
 
 struct Unit {
@@ -265,12 +140,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint64_t* q_empty = bar + 1;
   uint64_t* k_full = bar + 2;    // [NK]
   uint64_t* k_empty = bar + 6;   // [NK]
-  uint64_t* v_full = bar + 10;   // [NVH]
-  uint64_t* v_empty = bar + 14;  // [NVH]
+  uint64_t* v_full = bar + 10;   // [NV]
+  uint64_t* v_empty = bar + 14;  // [NV]
   uint64_t* s_full = bar + 18;   // [2] S buffer written (MMA commit)
   uint64_t* s_free = bar + 20;   // [2] S buffer read by every softmax warpgroup
-  uint64_t* p_full = bar + 22;   // [NWG] P quarter q written by warpgroup q
-  uint64_t* p_free = bar + 26;   // [NWG] PV of P quarter q done (MMA commit)
+  uint64_t* p_full = bar + 22;   // [2] P of the tile in S/P buffer kb written by every warpgroup
   uint64_t* o_full = bar + 30;
   uint64_t* o_free = bar + 31;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 32);
@@ -286,7 +160,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1 + NWG);  // MMA commit + every softmax warpgroup (they read gk)
     }
-    for (int i = 0; i < NVH; ++i) {
+    for (int i = 0; i < NV; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
@@ -294,9 +168,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], NWG);
     }
-    for (int i = 0; i < NWG; ++i) {
-      mbar_init(&p_full[i], 1);
-      mbar_init(&p_free[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], NWG);
     }
     mbar_init(o_full, 1);
     mbar_init(o_free, 1);
@@ -348,7 +221,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       }
     }
   } else if (warp == 2) {
-    // ------------------------------------ producer: V half tiles (pass 2)
+    // ------------------------------------------- producer: V-hat tiles (pass 2)
     if (elect_one_lane()) {
       tma_prefetch_desc(&tmVhi);
       tma_prefetch_desc(&tmVlo);
@@ -357,14 +230,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         const int vrow = (un.b * p.Hkv + un.h / group) * HD;
-        for (int j = 0; j < n; ++j) {
-          for (int half = 0; half < 2; ++half, ++vc) {
-            const int vs = vc % NVH;
-            if (vc >= NVH) mbar_wait(&v_empty[vs], ((vc / NVH) - 1) & 1, 0x203);
-            uint8_t* v = sm + OFF_V + vs * V_STAGE;
-            mbar_arrive_expect_tx(&v_full[vs], V_STAGE);
-            tma_load_2d(v, &tmVhi, &v_full[vs], j * BN + 64 * half, vrow);
-            tma_load_2d(v + V_HALF, &tmVlo, &v_full[vs], j * BN + 64 * half, vrow);
+        for (int j = 0; j < n; ++j, ++vc) {
+          const int vs = vc % NV;
+          if (vc >= NV) mbar_wait(&v_empty[vs], ((vc / NV) - 1) & 1, 0x203);
+          uint8_t* v = sm + OFF_V + vs * V_STAGE;
+          mbar_arrive_expect_tx(&v_full[vs], V_STAGE);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            tma_load_2d(v + 2 * half * V_HALF, &tmVhi, &v_full[vs], j * BN + 64 * half, vrow);
+            tma_load_2d(v + (2 * half + 1) * V_HALF, &tmVlo, &v_full[vs], j * BN + 64 * half, vrow);
           }
         }
       }
@@ -375,10 +249,13 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const uint32_t idq = idesc_nvf4(BM, BN);
       const uint32_t idv = idesc_f16(BM, HD);
       uint32_t kc = 0, vc = 0, uc = 0;
-      uint32_t suse[2] = {0, 0}, pu[NWG] = {0, 0, 0, 0};
+      // uses of each S buffer and pass-2 tiles per buffer (kept in registers:
+      // two scalars selected by the buffer index, not a dynamically indexed array)
+      uint32_t suse0 = 0, suse1 = 0, pu0 = 0, pu1 = 0;
       auto issue_qk = [&](int j, int kb, int pass) {
         // S buffer kb: its previous scores must have been read by every warpgroup
-        if (suse[kb] > 0) mbar_wait(&s_free[kb], (suse[kb] - 1) & 1, 0x211);
+        const uint32_t su = kb ? suse1 : suse0;
+        if (su > 0) mbar_wait(&s_free[kb], (su - 1) & 1, 0x211);
         const int s = kc % NK;
         mbar_wait(&k_full[s], (kc / NK) & 1, 0x212);
         tc_fence_after();
@@ -396,7 +273,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         }
         tc_commit(&k_empty[s]);
         tc_commit(&s_full[kb]);
-        ++suse[kb];
+        if (kb) ++suse1;
+        else ++suse0;
         ++kc;
       };
       for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
@@ -409,36 +287,36 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tmem_cp_sf_atom(tmem + T_SFA + 4, smem_desc(smem_u32(sm + OFF_QSF + 512), 16, 128, kSwizzleNone));
         // pass 1: scores only
         for (int j = 0; j < n; ++j) issue_qk(j, j & 1, 0);
-        // pass 2: scores again, then PV one key quarter at a time as each P quarter lands
+        // pass 2: scores again, then PV over the whole tile once every warpgroup
+        // has written its quarter of P.  P(j) lives in S(j)'s TMEM buffer, so
+        // QK(j+2) is issued after PV(j): the tensor pipe runs a thread's MMAs in
+        // order, so PV(j) has read P(j) before QK(j+2) overwrites the buffer.
         issue_qk(0, 0, 1);
-        for (int j = 0; j < n; ++j) {
-          if (j + 1 < n) issue_qk(j + 1, (j + 1) & 1, 1);
+        if (n > 1) issue_qk(1, 1, 1);
+        for (int j = 0; j < n; ++j, ++vc) {
+          const int kb = j & 1, vs = vc % NV;
+          const uint32_t pbuf = tmem + T_S + 128 * kb;
+          mbar_wait(&v_full[vs], (vc / NV) & 1, 0x215);
+          trace(p, uc, TR_PWAIT, j);
+          mbar_wait(&p_full[kb], (kb ? pu1 : pu0) & 1, 0x214);
+          if (kb) ++pu1;
+          else ++pu0;
+          if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
+          tc_fence_after();
+          trace(p, uc, TR_PV, j);
+          const uint32_t v = smem_u32(sm + OFF_V + vs * V_STAGE);
 #pragma unroll
-          for (int q = 0; q < NWG; ++q) {
-            const int vs = vc % NVH;  // half tile q/2 of this key tile
-            if ((q & 1) == 0) mbar_wait(&v_full[vs], (vc / NVH) & 1, 0x215);
-            if (q == 0) trace(p, uc, TR_PWAIT, j);
-            mbar_wait(&p_full[q], pu[q] & 1, 0x214);
-            ++pu[q];
-            if (j == 0 && q == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
-            tc_fence_after();
-            if (q == 0) trace(p, uc, TR_PV, j);
-            uint8_t* v = sm + OFF_V + vs * V_STAGE;
+          for (int kk = 0; kk < BN / 16; ++kk) {  // keys 16kk .. 16kk+15
+            // warpgroup kk/2 wrote these keys' P over its S columns 32(kk/2) .. 32(kk/2)+15
+            const uint32_t a = pbuf + 32 * (kk >> 1) + 8 * (kk & 1);
 #pragma unroll
             for (int part = 0; part < 2; ++part) {  // hi, lo planes
-#pragma unroll
-              for (int kk = 2 * q; kk < 2 * q + 2; ++kk) {  // keys 16kk .. 16kk+15
-                const uint32_t vb = smem_u32(v + part * V_HALF) + (kk & 3) * 32;
-                mma_f16_ts(tmem + T_O, tmem + T_P + 8 * kk, smem_desc(vb, 16, 1024, kSwizzle128B), idv,
-                           (j > 0 || q > 0 || part > 0 || kk > 0) ? 1u : 0u);
-              }
-            }
-            tc_commit(&p_free[q]);
-            if (q & 1) {
-              tc_commit(&v_empty[vs]);
-              ++vc;
+              const uint32_t vb = v + ((kk >> 2) * 2 + part) * V_HALF + (kk & 3) * 32;
+              mma_f16_ts(tmem + T_O, a, smem_desc(vb, 16, 1024, kSwizzle128B), idv, (j > 0 || kk > 0 || part > 0) ? 1u : 0u);
             }
           }
+          tc_commit(&v_empty[vs]);
+          if (j + 2 < n) issue_qk(j + 2, kb, 1);
         }
         tc_commit(o_full);
         tc_commit(q_empty);
@@ -456,8 +334,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     const float r6 = __frcp_rn(6.0f);
     const bool leader = threadIdx.x % 128 == 0;
     const int col0 = 32 * q;
-    uint32_t kc = 0, uc = 0, pt = 0;
-    uint32_t sfu[2] = {0, 0};
+    uint32_t kc = 0, uc = 0;
+    uint32_t sfu0 = 0, sfu1 = 0;  // completions seen per S buffer
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
       const Unit un = unit_of(u, p);
       const int n = kv_tiles(un, p);
@@ -468,8 +346,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       float m = -INFINITY;
       for (int j = 0; j < n; ++j, ++kc) {
         const int kb = j & 1, s = kc % NK;
-        mbar_wait(&s_full[kb], sfu[kb] & 1, 0x222);
-        ++sfu[kb];
+        mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x222);
+        if (kb) ++sfu1;
+        else ++sfu0;
         if (leader && q == 0) trace(p, uc, TR_SFULL, j);
         tc_fence_after();
         uint32_t a[32];
@@ -499,8 +378,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       uint64_t lsum2[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
       for (int j = 0; j < n; ++j, ++kc) {
         const int kb = j & 1, s = kc % NK;
-        mbar_wait(&s_full[kb], sfu[kb] & 1, 0x223);
-        ++sfu[kb];
+        mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x223);
+        if (kb) ++sfu1;
+        else ++sfu0;
         if (leader && q == 0) trace(p, uc, TR_SFULL + 32, j);
         tc_fence_after();
         uint32_t a[32];
@@ -519,20 +399,17 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
         else chunk_p<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
         if (leader && q == 0) trace(p, uc, TR_COMP, j);
-        // P quarter q may be overwritten once the previous tile's PV on it is done
-        if (pt > 0) mbar_wait(&p_free[q], (pt - 1) & 1, 0x225);
-        if (leader && q == 0) trace(p, uc, TR_PFREE, j);
-        tc_fence_after();
-        tmem_st16(tmem + lane_base + T_P + 16 * q, pk);
+        // P quarter q goes over the first 16 of this warpgroup's S columns
+        tmem_st16(tmem + lane_base + T_S + 128 * kb + col0, pk);
         tmem_st_wait();
         tc_fence_before();
         named_bar(1 + q, 128);
         if (leader) {
-          mbar_arrive(&p_full[q]);
+          mbar_arrive(&p_full[kb]);
           mbar_arrive(&k_empty[s]);
           if (q == 0) trace(p, uc, TR_PDONE, j);
+          if (q == 3) trace(p, uc, TR_PDONE3, j);
         }
-        ++pt;
       }
       float l0, l1;
       upk2(add2(add2(lsum2[0], lsum2[1]), add2(lsum2[2], lsum2[3])), l0, l1);

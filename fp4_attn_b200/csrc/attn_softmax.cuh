@@ -1,0 +1,162 @@
+// attn_softmax.cuh -- per-thread softmax and P requantization arithmetic of
+// the attention kernel (one TMEM lane = one query row, 32 key columns per
+// call), kept apart from the kernel's pipeline so it can be exercised alone.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace fp4 {
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Packed fp32 pairs (sm_100a f32x2 ALU ops, each lane rounded like the scalar op).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// E2M1 round-to-nearest-even of (x0, x1) (satfinite: |x| > 6 -> 6) -> the two
+// fp16 values code * scale, with s14 = the block scale * 2^14 as two halves.
+// The code byte is widened without the conversion pipe: for a 3-bit magnitude
+// c, the fp16 bit pattern c << 9 is c's E2M1 value * 2^-14 (c = 1 lands on the
+// fp16 subnormal 2^-15, c >= 2 on normals), so one multiply places both codes
+// (low nibble -> bits 9..11, high nibble -> bits 25..27) and one mask cleans
+// them.  P is non-negative, so the sign bits are dropped.  The products are
+// exact in fp16: P's block scales lie in [2^-9, 0.171875] or are 0.
+__device__ __forceinline__ uint32_t quant_pair_f16(float x0, float x1, uint32_t s14) {
+  uint32_t c;
+  asm("{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\t"
+      "cvt.u32.u8 %0, t;\n\t}"
+      : "=r"(c)
+      : "f"(x0), "f"(x1));
+  return hmul2_u32((c * 0x00200200u) & 0x0E000E00u, s14);
+}
+
+// Pass 1 on one 32-key chunk: running max of z = acc * gk (keys with
+// column > lim masked when MASK).
+template <bool MASK>
+__device__ __forceinline__ float chunk_max(const uint32_t (&a)[32], const float* gk, int col0, int lim, float m) {
+  float z[32];
+  const float4* g4 = reinterpret_cast<const float4*>(gk);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 g = g4[q];
+    upk2(mul2(pk2(__uint_as_float(a[4 * q]), __uint_as_float(a[4 * q + 1])), pk2(g.x, g.y)), z[4 * q], z[4 * q + 1]);
+    upk2(mul2(pk2(__uint_as_float(a[4 * q + 2]), __uint_as_float(a[4 * q + 3])), pk2(g.z, g.w)), z[4 * q + 2],
+         z[4 * q + 3]);
+  }
+  if constexpr (MASK) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) z[i] = (col0 + i > lim) ? -INFINITY : z[i];
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) m = max3f(m, z[i], z[i + 1]);
+  return m;
+}
+
+// exp2 of four scores: e = exp2(acc * gk * u - m * u).
+__device__ __forceinline__ void exp4(const uint32_t* a, float4 g, uint64_t u2, uint64_t nmu2, float* e) {
+  float t0, t1, t2, t3;
+  upk2(fma2(mul2(pk2(__uint_as_float(a[0]), __uint_as_float(a[1])), pk2(g.x, g.y)), u2, nmu2), t0, t1);
+  upk2(fma2(mul2(pk2(__uint_as_float(a[2]), __uint_as_float(a[3])), pk2(g.z, g.w)), u2, nmu2), t2, t3);
+  e[0] = ex2(t0);
+  e[1] = ex2(t1);
+  e[2] = ex2(t2);
+  e[3] = ex2(t3);
+}
+
+// Block scale of 16 values of e: the E4M3 scale byte's reciprocal (rs) and
+// the scale * 2^14 as two fp16 halves (s14).
+__device__ __forceinline__ void block_scale(const float* eb, const float* rcp, float r6, uint64_t& rs2,
+                                            uint32_t& s14) {
+  const float m0 = max3f(eb[0], eb[1], eb[2]), m1 = max3f(eb[3], eb[4], eb[5]);
+  const float m2 = max3f(eb[6], eb[7], eb[8]), m3 = max3f(eb[9], eb[10], eb[11]);
+  const float m4 = max3f(eb[12], eb[13], eb[14]);
+  const float amax = fmaxf(max3f(m0, m1, m2), max3f(m3, m4, eb[15]));
+  const uint8_t sb = e4m3_satfinite(amax * r6);
+  const float rs = rcp[sb & 127];
+  rs2 = pk2(rs, rs);
+  s14 = (uint32_t)__half_as_ushort(__float2half_rn(e4m3_to_f32(sb) * 16384.0f)) * 0x10001u;
+}
+
+// Pass 2 on one 32-key chunk: e = exp2(z*u - m*u), running sum, NVFP4
+// fake-quant of e in two blocks of 16 -> 16 words of fp16 pairs.  The exp2 of
+// the second block is interleaved with the quantization of the first, so the
+// MUFU and the conversion pipe work at the same time.
+template <bool MASK>
+__device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
+                                        uint64_t nmu2, const float* rcp, float r6, uint64_t (&lsum2)[4],
+                                        uint32_t (&pk)[16]) {
+  float e[32];
+  const float4* g4 = reinterpret_cast<const float4*>(gk);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) exp4(a + 4 * q, g4[q], u2, nmu2, e + 4 * q);
+  if constexpr (MASK) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
+  }
+  uint64_t rs2;
+  uint32_t s14;
+  block_scale(e, rcp, r6, rs2, s14);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    exp4(a + 16 + 4 * q, g4[4 + q], u2, nmu2, e + 16 + 4 * q);
+#pragma unroll
+    for (int i = 4 * q; i < 4 * q + 4; i += 2) {
+      float x0, x1;
+      upk2(mul2(pk2(e[i], e[i + 1]), rs2), x0, x1);
+      pk[i / 2] = quant_pair_f16(x0, x1, s14);
+    }
+  }
+  if constexpr (MASK) {
+#pragma unroll
+    for (int i = 16; i < 32; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
+  }
+  block_scale(e + 16, rcp, r6, rs2, s14);
+#pragma unroll
+  for (int i = 16; i < 32; i += 2) {
+    float x0, x1;
+    upk2(mul2(pk2(e[i], e[i + 1]), rs2), x0, x1);
+    pk[i / 2] = quant_pair_f16(x0, x1, s14);
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) lsum2[(i >> 1) & 3] = add2(lsum2[(i >> 1) & 3], pk2(e[i], e[i + 1]));
+}
+
+}  // namespace fp4

@@ -125,8 +125,8 @@ class Clocks:
 
 
 # ------------------------------------------------------------- workloads
-def quantize_input():
-    g = torch.Generator().manual_seed(0)
+def quantize_input(rank=0):
+    g = torch.Generator().manual_seed(rank)
     x = torch.randn(4096, 4096, generator=g)
     idx = torch.randperm(x.numel(), generator=g)[: x.numel() // 1000]
     x.view(-1)[idx] *= 50
@@ -139,11 +139,11 @@ class QuantizeWorkload:
     unit = "GB/s"
     dtype = "bf16->nvfp4 (fp32 arithmetic)"
 
-    def __init__(self, dev):
+    def __init__(self, dev, rank=0, world=1):
         from fp4_attn_b200 import _lib
         self.lib = _lib
         self.dev = dev
-        x = quantize_input()
+        x = quantize_input(rank)  # weak scaling: one [4096,4096] tensor per rank, seed r
         self.m, self.n = x.shape
         self.elems = x.numel()
         self.algo_bytes = self.elems * (2 + 0.5 + 1 / 16)
@@ -158,7 +158,8 @@ class QuantizeWorkload:
         self.scales_host = torch.empty(self.m, self.n // 16, dtype=torch.uint8).pin_memory()
         self.stream = torch.cuda.current_stream(dev).cuda_stream
         self.config = {"workload": "quantize bf16 [4096,4096], per-tensor scale amax/2688, block 16",
-                       "elements": self.elems, "l2": f"rotating {self.nsets} input/output sets (> L2)"}
+                       "elements": self.elems, "l2": f"rotating {self.nsets} input/output sets (> L2)",
+                       "global_batch": world, "shard": "tensor r on rank r (seed r)"}
 
     def _global(self, i):
         self.lib.call("fp4q_global_scale", self.xs[i].data_ptr(), 1, 1, self.m, 1, self.n, 0, self.n, 0,
@@ -218,8 +219,8 @@ class QuantizeWorkload:
         return self.algo_bytes * n / el / 1e9, f"full [4096,4096] tensor x{n} (torch ops, fp32)"
 
 
-def attention_inputs():
-    g = torch.Generator().manual_seed(1)
+def attention_inputs(rank=0):
+    g = torch.Generator().manual_seed(1 + rank)
     q = torch.randn(1, 32, 4096, 128, generator=g).bfloat16()
     k = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
     v = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
@@ -233,17 +234,23 @@ class AttentionWorkload:
     dtype = "nvfp4 QK^T (tcgen05 mxf4nvf4) + fp16-exact Phat x Vhat (tcgen05 f16), fp32 accumulate"
     B, Hq, Hkv, T, D = 1, 32, 8, 4096, 128
 
-    def __init__(self, dev, cpu_only=False):
-        self.flops = 4 * self.B * self.Hq * self.T * self.T * self.D / 2  # causal, algorithmic
+    def __init__(self, dev, cpu_only=False, rank=0, world=1):
+        from fp4_attn_b200 import shard
+        self.flops = 4 * self.B * self.Hq * self.T * self.T * self.D / 2  # causal, algorithmic, per rank
+        # weak scaling: the job is a batch of `world` such problems; rank r owns batch row r,
+        # i.e. its 8 (batch, kv-head) units (fp4_attn_b200.shard), with inputs from seed 1 + r
+        units = shard.attention_shard(world, self.Hq, self.Hkv, world, rank)
+        assert all(u.b == rank for u in units) and len(units) == self.Hkv
         self.config = {"workload": "NVFP4 attention fwd, Llama-3-8B shape: B=1, Hq=32, Hkv=8, D=128, T=4096, "
                                    "causal, single-slice Q/P quantization",
-                       "flops_per_step": self.flops}
+                       "flops_per_step": self.flops, "global_batch": world,
+                       "shard": "batch row r (its 8 (batch, kv-head) units) on rank r, seed 1 + r"}
         if cpu_only:
             return
         from fp4_attn_b200 import attention as A
         self.A = A
         self.dev = dev
-        q, k, v = attention_inputs()
+        q, k, v = attention_inputs(rank)
         self.host = [t.pin_memory() for t in (q, k, v)]
         per_set = sum(t.numel() * 2 for t in (q, k, v))
         self.nsets = max(2, int(2 * L2_BYTES // per_set) + 1)
@@ -342,7 +349,7 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     wl_name = args.workload or default_workload()
-    wl = make_workload(wl_name, dev)
+    wl = make_workload(wl_name, dev, rank=rank, world=world)
     peaks, peak_src = measured_peaks()
     K, W = args.steps, args.warmup
     for i in range(W):
@@ -435,7 +442,7 @@ def default_workload():
     return "attention"
 
 
-def make_workload(name, dev, cpu_only=False):
+def make_workload(name, dev, cpu_only=False, rank=0, world=1):
     if name == "quantize":
         if cpu_only:
             w = QuantizeWorkload.__new__(QuantizeWorkload)
@@ -443,8 +450,8 @@ def make_workload(name, dev, cpu_only=False):
             w.algo_bytes = w.elems * (2 + 0.5 + 1 / 16)
             w.config = {"workload": "quantize bf16 [4096,4096], per-tensor scale amax/2688, block 16"}
             return w
-        return QuantizeWorkload(dev)
-    return AttentionWorkload(dev, cpu_only=cpu_only)
+        return QuantizeWorkload(dev, rank, world)
+    return AttentionWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
 
 
 def main():

@@ -103,7 +103,7 @@ enum TraceSlot {
 
 __device__ __forceinline__ void trace(const AttnArgs& p, uint32_t uc, int slot, int j) {
   if (p.trace && uc == 0 && j < 32 && slot + j < kTraceSlots)
-    p.trace[(int64_t)blockIdx.x * kTraceSlots + slot + j] = (long long)globaltimer();
+    p.trace[(int64_t)blockIdx.x * kTraceSlots + slot + j] = (long long)clock64();
 }
 
 struct Unit {
@@ -620,7 +620,7 @@ using namespace fp4;
 static long long* g_trace = nullptr;
 
 // Profiling aid: when buf is non-null, the next fp4attn_fwd_packed calls
-// write an event timeline (globaltimer ns) of each CTA's first work unit into
+// write an event timeline (SM clock cycles, clock64) of each CTA's first work unit into
 // buf[cta * 512 + slot]; buf needs grid * 512 int64 entries.
 extern "C" void fp4attn_set_trace(long long* buf) { g_trace = buf; }
 

@@ -1,5 +1,7 @@
 // quant.cu -- C ABI entry points of the NVFP4 quantizer (fp4q_quantize,
 // fp4q_global_scale).  The kernels live in quant_impl.cuh.
+#include <stdint.h>
+
 #include "quant_impl.cuh"
 
 using namespace fp4;
@@ -11,6 +13,9 @@ static int quantize_entry(const void* x, int in_dtype, int B, int T, int H, int 
   clear_error();
   if (!x) return set_error(FP4ATTN_ERR_ARG, "x is null");
   if (B <= 0 || T < 0 || H <= 0 || D <= 0 || T_pad < T) return set_error(FP4ATTN_ERR_ARG, "bad shape");
+  // rows and columns are indexed in 32 bits inside the kernels
+  if ((int64_t)H * D > INT32_MAX || (int64_t)B * T_pad > INT32_MAX)
+    return set_error(FP4ATTN_ERR_ARG, "rows (B*T_pad) and columns (H*D) must each be below 2^31");
   if (H > 1 && D % 16 != 0) return set_error(FP4ATTN_ERR_ARG, "D must be a multiple of 16 when H > 1");
   if (gmode < 0 || gmode > 3) return set_error(FP4ATTN_ERR_ARG, "bad gmode");
   if (gmode != 0 && !g) return set_error(FP4ATTN_ERR_ARG, "g buffer required for a global-scale mode");

@@ -32,6 +32,7 @@
 namespace fp4 {
 
 constexpr int kThreads = 128;
+constexpr int kVecThreads = 256;  // quant_rows_vec_kernel
 constexpr int MAXB = 2;  // 16-element blocks a thread keeps in registers
 
 struct QuantArgs {
@@ -59,8 +60,8 @@ __device__ __forceinline__ void load_block(float v[16], const QuantArgs& p, int 
   const int64_t c0 = (int64_t)kb * 16;
   const T* base = reinterpret_cast<const T*>(p.x) + (int64_t)b * p.sB + (int64_t)t * p.sT;
   if (p.vec && c0 + 16 <= n) {
-    const int h = (int)(c0 / p.D);
-    const int d = (int)(c0 - (int64_t)h * p.D);
+    const int h = (int)c0 / p.D;
+    const int d = (int)c0 - h * p.D;
     const T* q = base + (int64_t)h * p.sH + d;
     if constexpr (DT == FP4_DT_F32) {
       const float4* q4 = reinterpret_cast<const float4*>(q);
@@ -306,12 +307,12 @@ __global__ void __launch_bounds__(256) absmax_kernel(QuantArgs p, unsigned int* 
   for (int j = 0; j < 8; ++j) m[j] = 0.0f;
   const bool vec = p.vec && c0 + 8 <= n && (p.H == 1 || (c0 % p.D) + 8 <= p.D) && (sizeof(T) == 2);
   for (int64_t r = r0; r < r1; ++r) {
-    const int b = (int)(r / p.T);
-    const int t = (int)(r - (int64_t)b * p.T);
+    const int b = (int)r / p.T;
+    const int t = (int)r - b * p.T;
     const T* row = reinterpret_cast<const T*>(p.x) + (int64_t)b * p.sB + (int64_t)t * p.sT;
     if (vec) {
-      const int h = (int)(c0 / p.D);
-      const int d = (int)(c0 - (int64_t)h * p.D);
+      const int h = (int)c0 / p.D;
+      const int d = (int)c0 - h * p.D;
       const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + (int64_t)h * p.sH + d));
       const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
@@ -341,7 +342,55 @@ __global__ void __launch_bounds__(256) absmax_kernel(QuantArgs p, unsigned int* 
   for (int j = 1; j < 8; ++j) mm = nanmax(mm, m[j]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mm = nanmax(mm, __shfl_xor_sync(0xffffffffu, mm, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(bits, __float_as_uint(mm));
+  __shared__ float wmax[8];
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = mm;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mm = nanmax(mm, wmax[w]);
+    atomicMax(bits, __float_as_uint(mm));
+  }
+}
+
+// Tensor maximum of |x| for a contiguous input (the whole tensor is one run
+// of nelem elements starting 16-byte aligned): grid-stride over 16-byte
+// chunks, eight independent loads in flight per thread, one atomicMax per block
+// (256 threads).
+template <int DT, int A>
+__global__ void __launch_bounds__(256) absmax_flat_kernel(const void* x, int64_t nelem, unsigned int* bits) {
+  using T = typename In<DT>::T;
+  constexpr int PER = 16 / sizeof(T);  // elements per 16-byte chunk
+  const int64_t nchunk = nelem / PER;
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  float m = 0.0f;
+  auto fold = [&](const uint4& u) {
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) m = nanmax(m, fabsf(rnd<A>(In<DT>::f(e[j]))));
+  };
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nchunk; i += 8 * stride) {
+    uint4 u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] = i + k * stride < nchunk ? __ldg(src + i + k * stride) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) fold(u[k]);
+  }
+  // the ragged tail (fewer than PER elements) goes to the first thread
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    for (int64_t k = nchunk * PER; k < nelem; ++k)
+      m = nanmax(m, fabsf(rnd<A>(In<DT>::f(reinterpret_cast<const T*>(x)[k]))));
+  // one atomic per block: same-address atomics serialise in L2
+  __shared__ float wmax[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = nanmax(m, wmax[w]);
+    atomicMax(bits, __float_as_uint(m));
+  }
 }
 
 // g = max * recip(global_sf_max) in the dequant dtype (fp4_quant_utils.py:139).
@@ -351,11 +400,179 @@ __global__ void finalize_g_kernel(float* g, int64_t count, float gsf_max) {
   if (i < count) g[i] = mul<A>(g[i], recip<A>(rnd<A>(gsf_max)));
 }
 
+// Raw 16-byte vectors of one 16-element block (2 for 16-bit inputs, 4 for fp32).
+template <int DT>
+struct RawBlock {
+  static constexpr int NV = DT == FP4_DT_F32 ? 4 : 2;
+  uint4 u[NV];
+};
+
+// Element offset of block kb within a row: h * sH + d for c0 = 16 kb.
+__device__ __forceinline__ int64_t block_col_offset(const QuantArgs& p, int kb) {
+  const int c0 = kb * 16;
+  const int h = c0 / p.D;
+  return (int64_t)h * p.sH + (c0 - h * p.D);
+}
+
+template <int DT>
+__device__ __forceinline__ void load_raw(RawBlock<DT>& r, const QuantArgs& p, int b, int t, int64_t col) {
+  using T = typename In<DT>::T;
+  const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.x) + (int64_t)b * p.sB +
+                                                  (int64_t)t * p.sT + col);
+#pragma unroll
+  for (int j = 0; j < RawBlock<DT>::NV; ++j) r.u[j] = __ldg(q + j);
+}
+
+template <int DT, int A>
+__device__ __forceinline__ void unpack_raw(float v[16], const RawBlock<DT>& r) {
+#pragma unroll
+  for (int j = 0; j < RawBlock<DT>::NV; ++j) {
+    const uint32_t w[4] = {r.u[j].x, r.u[j].y, r.u[j].z, r.u[j].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if constexpr (DT == FP4_DT_F32) {
+        v[4 * j + k] = rnd<A>(__uint_as_float(w[k]));
+      } else if constexpr (DT == FP4_DT_BF16) {
+        v[8 * j + 2 * k] = rnd<A>(__uint_as_float(w[k] << 16));
+        v[8 * j + 2 * k + 1] = rnd<A>(__uint_as_float(w[k] & 0xFFFF0000u));
+      } else {
+        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+        v[8 * j + 2 * k] = rnd<A>(f2.x);
+        v[8 * j + 2 * k + 1] = rnd<A>(f2.y);
+      }
+    }
+  }
+}
+
+// Persistent row quantizer for aligned rows of whole 16-element blocks
+// (n % 16 == 0, every block 16-byte aligned) with at most 2 blocks per
+// thread: each CTA walks row groups with a grid stride and loads the next
+// group's raw vectors before it quantizes the current one, so a thread keeps
+// one row's bytes in flight while it computes.  Same arithmetic as
+// quant_rows_kernel (quant_block).
+template <int DT, int A, int ODT, int TPR, bool OUT>
+__global__ void __launch_bounds__(kVecThreads, 3) quant_rows_vec_kernel(QuantArgs p) {
+  constexpr int ROWS = kVecThreads / TPR;
+  constexpr int WPR = TPR / 32;
+  __shared__ float red[2][kVecThreads / 32];
+  __shared__ float rcp_tab[128];
+  if (threadIdx.x < 128) rcp_tab[threadIdx.x] = recip<A>(e4m3_to_f32((uint8_t)threadIdx.x));
+  __syncthreads();
+  const int rloc = threadIdx.x / TPR;
+  const int lane = threadIdx.x % TPR;
+  const int64_t nrows = (int64_t)p.B * p.T_pad;
+  const int nblk = p.H * p.D / 16;
+  const int nmine = lane < nblk ? (nblk - lane + TPR - 1) / TPR : 0;  // 0, 1 or 2
+  const int64_t step = (int64_t)gridDim.x * ROWS;
+  // a thread's blocks sit at the same columns of every row
+  const int64_t col0 = block_col_offset(p, lane), col1 = block_col_offset(p, lane + TPR);
+  const uint32_t tpad = (uint32_t)p.T_pad;
+  auto row_bt = [&](int64_t orow, int& b, int& t) {
+    if (p.B == 1) {
+      b = 0;
+      t = (int)orow;
+    } else {
+      b = (int)((uint32_t)orow / tpad);
+      t = (int)((uint32_t)orow - (uint32_t)b * tpad);
+    }
+  };
+  RawBlock<DT> cur[2], nxt[2];
+  int64_t base = (int64_t)blockIdx.x * ROWS;
+  {
+    const int64_t orow = base + rloc;
+    int b, t;
+    row_bt(orow, b, t);
+    if (orow < nrows && t < p.T) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        if (i < nmine) load_raw<DT>(cur[i], p, b, t, i ? col1 : col0);
+    }
+  }
+  for (int it = 0; base < nrows; base += step, ++it) {
+    const int64_t orow = base + rloc;
+    const bool live = orow < nrows;
+    int b = 0, t = 0;
+    if (live) row_bt(orow, b, t);
+    const bool pad_row = !live || t >= p.T;
+    {  // the next row group's bytes go in flight now
+      const int64_t nrow = orow + step;
+      int nb, nt;
+      row_bt(nrow, nb, nt);
+      if (nrow < nrows && nt < p.T) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (i < nmine) load_raw<DT>(nxt[i], p, nb, nt, i ? col1 : col0);
+      }
+    }
+    float g = 1.0f;
+    if (p.gmode == 1) {
+      float m = 0.0f;
+      if (!pad_row) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (i < nmine) {
+            float v[16];
+            unpack_raw<DT, A>(v, cur[i]);
+            m = nanmax(m, block_absmax(v));
+          }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (WPR > 1) {
+        if ((threadIdx.x & 31) == 0) red[it & 1][threadIdx.x / 32] = m;
+        __syncthreads();
+        m = red[it & 1][rloc * WPR];
+#pragma unroll
+        for (int w = 1; w < WPR; ++w) m = nanmax(m, red[it & 1][rloc * WPR + w]);
+      }
+      g = m;  // rowmax, no division by global_sf_max (fp4_quant_utils.py:134,139)
+      if (p.g_row && lane == 0 && live) p.g_row[orow] = pad_row ? 0.0f : g;
+    } else if (p.gmode == 3) {
+      g = p.g_in[0];
+    }
+    if (live) {
+      if (pad_row) {
+        for (int kb = lane; kb < nblk; kb += TPR) {
+          if (p.codes) *reinterpret_cast<uint2*>(p.codes + orow * p.codes_ld + (int64_t)kb * 8) = make_uint2(0u, 0u);
+          if (p.scales)
+            p.scales[p.scale_layout ? sf_tcgen05_offset(orow, kb, p.scales_ld) : orow * p.scales_ld + kb] = 0;
+        }
+      } else {
+        const float rg = p.gmode == 0 ? 1.0f : recip<A>(g);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (i < nmine) {
+            float v[16];
+            unpack_raw<DT, A>(v, cur[i]);
+            quant_block<A, ODT, false, OUT>(v, p, orow, lane + i * TPR, g, rg, rcp_tab);
+          }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) cur[i] = nxt[i];
+  }
+}
+
 template <int DT, int A, int ODT, bool COLG, bool OUT>
 static int launch_rows(const QuantArgs& p, cudaStream_t st) {
   const int64_t n = (int64_t)p.H * p.D;
   const int64_t nblk = (n + 15) / 16;
   const int64_t nrows = (int64_t)p.B * p.T_pad;
+  if constexpr (!COLG) {
+    if (p.vec && n % 16 == 0 && nblk <= 256 * 2 && (p.H == 1 || p.D % 16 == 0)) {
+      // persistent: a few CTAs per SM, each walking row groups
+      int tpr = nblk <= 64 ? 32 : nblk <= 128 ? 64 : nblk <= 256 ? 128 : 256;
+      const int64_t groups = (nrows + (kVecThreads / tpr) - 1) / (kVecThreads / tpr);
+      const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(groups, 148 * 3));
+      switch (tpr) {
+        case 32: quant_rows_vec_kernel<DT, A, ODT, 32, OUT><<<grid, kVecThreads, 0, st>>>(p); break;
+        case 64: quant_rows_vec_kernel<DT, A, ODT, 64, OUT><<<grid, kVecThreads, 0, st>>>(p); break;
+        case 128: quant_rows_vec_kernel<DT, A, ODT, 128, OUT><<<grid, kVecThreads, 0, st>>>(p); break;
+        default: quant_rows_vec_kernel<DT, A, ODT, 256, OUT><<<grid, kVecThreads, 0, st>>>(p); break;
+      }
+      return check_launch("quant_rows_vec_kernel");
+    }
+  }
   // threads per row: enough that each thread owns at most MAXB blocks when possible
   if (nblk <= 32 * MAXB) {
     quant_rows_kernel<DT, A, ODT, 32, COLG, OUT><<<(unsigned)((nrows + 3) / 4), kThreads, 0, st>>>(p);
@@ -375,6 +592,18 @@ static int launch_prepass(const QuantArgs& p, float* g, float gsf_max, cudaStrea
   const int64_t count = per_col ? npad : 1;
   if (cudaMemsetAsync(g, 0, count * sizeof(float), st) != cudaSuccess) return set_error(FP4ATTN_ERR_CUDA, "memset g");
   const int64_t nrows = (int64_t)p.B * p.T;
+  // A contiguous tensor in tensor mode is one flat run of elements.
+  const bool flat = !per_col && p.vec && (p.H == 1 || p.sH == p.D) && p.sT == n && (p.B == 1 || p.sB == (int64_t)p.T * n);
+  if (flat) {
+    const int64_t nelem = nrows * n;
+    const int64_t chunks = nelem / (16 / (int64_t)sizeof(typename In<DT>::T));
+    // about eight chunks per thread: one batch of loads each
+    const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(148 * 8, (chunks + 2047) / 2048));
+    absmax_flat_kernel<DT, A><<<blocks, 256, 0, st>>>(p.x, nelem, reinterpret_cast<unsigned int*>(g));
+    if (int e = check_launch("absmax_flat_kernel")) return e;
+    finalize_g_kernel<A><<<1, 32, 0, st>>>(g, count, gsf_max);
+    return check_launch("finalize_g_kernel");
+  }
   const unsigned gx = (unsigned)((n + 8 * 256 - 1) / (8 * 256));
   // Enough row slices to fill the GPU several times over.
   unsigned gy = (unsigned)std::max<int64_t>(1, std::min<int64_t>(nrows, (148 * 16 + gx - 1) / gx));

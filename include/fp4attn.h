@@ -150,7 +150,7 @@ int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const fl
                        int num_ctas, void* stream);
 
 /* Profiling aid: a non-NULL buf makes later fp4attn_fwd_packed calls record
- * an event timeline (globaltimer, ns) of each CTA's first work unit into
+ * an event timeline (SM clock cycles from clock64) of each CTA's first work unit into
  * buf[cta * 512 + slot] (grid * 512 int64 entries); NULL turns it off. */
 void fp4attn_set_trace(long long* buf);
 

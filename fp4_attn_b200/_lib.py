@@ -31,6 +31,9 @@ SIGNATURES = {
     "fp4attn_set_trace": ([_P], None),
     "fp4attn_prepare_v": ([_P, _I, _I, _I, _I, _I, _L, _L, _L, _I, _P, _P, _P, _P, _P], _I),
     "fp4attn_fwd_packed": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P], _I),
+    "fp4attn_workspace_layout": ([_I, _I, _I, _I, _I, _P], _L),
+    "fp4attn_forward": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _P, _P, _L,
+                         _P], _I),
     "nvfp4sim_f32_to_nvf4": ([_P, _P, _P, _L, _P], _I),
     "nvfp4sim_f32_to_nvf4_nosearch": ([_P, _P, _P, _L, _P], _I),
     "nvfp4sim_f16_to_nvf4": ([_P, _P, _P, _L, _P], _I),

@@ -6,7 +6,7 @@ plus the Q/K/V fake-quant of llama_patch.py:167-196): it takes post-RoPE
 query/key/value in the HF layout [B, H, T, D] and returns the attention
 output in the layout the reference returns, [B, T, Hq, D], in fp32.
 
-Steps (all on the GPU, no CPU path):
+Steps (all on the GPU, no CPU path), one C ABI call (fp4attn_forward):
   1. Q and K -> NVFP4 codes + E4M3 scales (tcgen05 layout) + per-token global
      scale, on their [B*T, H*D] views (fp4q_quantize, row mode);
   2. V -> Vhat (NVFP4 along tokens, per-token global scale) as fp16 hi/lo
@@ -23,21 +23,47 @@ HEAD_DIM = 128
 
 
 class AttentionWorkspace:
-    """Packed operands of one attention call (reusable across calls of the same shape)."""
+    """Packed operands of one attention call (reusable across calls of the same shape).
+
+    One device buffer laid out by fp4attn_workspace_layout, with a tensor
+    view per piece: qc/kc codes [B*Tp, H*D/2], qs/ks tcgen05 scale atoms,
+    gq/gk per-token global scales [B*Tp], vhi/vlo V-hat planes [B*Hkv*D, Tp].
+    """
 
     def __init__(self, B, Hq, Hkv, T, D, device):
+        import ctypes
         self.shape = (B, Hq, Hkv, T, D)
         self.Tp = (T + 127) // 128 * 128
         Tp = self.Tp
-        u8 = torch.uint8
-        self.qc = torch.empty(B * Tp, Hq * D // 2, dtype=u8, device=device)
-        self.qs = torch.empty(B * Tp // 128 * Hq * (D // 64) * 512, dtype=u8, device=device)
-        self.gq = torch.empty(B * Tp, dtype=torch.float32, device=device)
-        self.kc = torch.empty(B * Tp, Hkv * D // 2, dtype=u8, device=device)
-        self.ks = torch.empty(B * Tp // 128 * Hkv * (D // 64) * 512, dtype=u8, device=device)
-        self.gk = torch.empty(B * Tp, dtype=torch.float32, device=device)
-        self.vhi = torch.empty(B * Hkv * D, Tp, dtype=torch.float16, device=device)
-        self.vlo = torch.empty(B * Hkv * D, Tp, dtype=torch.float16, device=device)
+        offs = (ctypes.c_int64 * 8)()
+        size = _lib.load().fp4attn_workspace_layout(B, Hq, Hkv, T, D, offs)
+        if size < 0:
+            raise ValueError(f"unsupported attention shape B={B} Hq={Hq} Hkv={Hkv} T={T} D={D}")
+        self.nbytes = int(size)
+        self.buf = torch.empty(self.nbytes + 256, dtype=torch.uint8, device=device)
+        base = (-self.buf.data_ptr()) % 256  # 256-byte aligned start
+        self.base = base
+        o = [int(x) + base for x in offs]
+        u8, f32, f16 = torch.uint8, torch.float32, torch.float16
+
+        def view(i, dtype, shape):
+            n = 1
+            for d in shape:
+                n *= d
+            esz = torch.empty((), dtype=dtype).element_size()
+            return self.buf[o[i]:o[i] + n * esz].view(dtype).view(*shape)
+
+        self.qc = view(0, u8, (B * Tp, Hq * D // 2))
+        self.qs = view(1, u8, (B * Tp // 128 * Hq * (D // 64) * 512,))
+        self.gq = view(2, f32, (B * Tp,))
+        self.kc = view(3, u8, (B * Tp, Hkv * D // 2))
+        self.ks = view(4, u8, (B * Tp // 128 * Hkv * (D // 64) * 512,))
+        self.gk = view(5, f32, (B * Tp,))
+        self.vhi = view(6, f16, (B * Hkv * D, Tp))
+        self.vlo = view(7, f16, (B * Hkv * D, Tp))
+
+    def ptr(self) -> int:
+        return self.buf.data_ptr() + self.base
 
 
 def _bhtd(x: torch.Tensor) -> torch.Tensor:
@@ -66,9 +92,16 @@ def prepare_v(v: torch.Tensor, vhi, vlo, Tp: int, vhat=None, g=None) -> None:
 def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
                       scaling: float | None = None, out: torch.Tensor | None = None,
                       workspace: AttentionWorkspace | None = None, num_ctas: int = 0) -> torch.Tensor:
-    """NVFP4 attention forward.  q [B,Hq,T,D], k/v [B,Hkv,T,D] (CUDA) -> fp32 [B,T,Hq,D]."""
+    """NVFP4 attention forward.  q [B,Hq,T,D], k/v [B,Hkv,T,D] (CUDA) -> fp32 [B,T,Hq,D].
+
+    One call of the C ABI's fp4attn_forward (quantize Q/K, prepare V-hat,
+    attention) with the packed operands in ``workspace``.
+    """
     _lib.require_cuda(q, k, v)
     q, k, v = _bhtd(q), _bhtd(k), _bhtd(v)
+    if not (q.dtype == k.dtype == v.dtype):
+        dt = torch.float32
+        q, k, v = q.to(dt), k.to(dt), v.to(dt)
     B, Hq, T, D = q.shape
     Hkv = k.shape[1]
     if D != HEAD_DIM:
@@ -78,13 +111,22 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
     if scaling is None:
         scaling = D ** -0.5
     ws = workspace or AttentionWorkspace(B, Hq, Hkv, T, D, q.device)
-    Tp = ws.Tp
-    quantize_qk(q, ws.qc, ws.qs, ws.gq, Tp)
-    quantize_qk(k, ws.kc, ws.ks, ws.gk, Tp)
-    prepare_v(v, ws.vhi, ws.vlo, Tp)
+    if ws.shape != (B, Hq, Hkv, T, D):
+        raise ValueError(f"workspace made for {ws.shape}, called with {(B, Hq, Hkv, T, D)}")
     if out is None:
         out = torch.empty(B, T, Hq, D, dtype=torch.float32, device=q.device)
-    _lib.call("fp4attn_fwd_packed", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), ws.kc.data_ptr(),
-              ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), out.data_ptr(), B, Hq, Hkv,
-              T, Tp, D, 1 if causal else 0, float(scaling), int(num_ctas), _lib.stream_of(q))
+    elif out.shape != (B, T, Hq, D) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous fp32 [B, T, Hq, D] tensor")
+    if num_ctas:
+        quantize_qk(q, ws.qc, ws.qs, ws.gq, ws.Tp)
+        quantize_qk(k, ws.kc, ws.ks, ws.gk, ws.Tp)
+        prepare_v(v, ws.vhi, ws.vlo, ws.Tp)
+        _lib.call("fp4attn_fwd_packed", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), ws.kc.data_ptr(),
+                  ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), out.data_ptr(), B, Hq,
+                  Hkv, T, ws.Tp, D, 1 if causal else 0, float(scaling), int(num_ctas), _lib.stream_of(q))
+        return out
+    _lib.call("fp4attn_forward", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], B, Hq, Hkv, T, D,
+              q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
+              v.stride(2), 1 if causal else 0, float(scaling), out.data_ptr(), ws.ptr(), ws.nbytes,
+              _lib.stream_of(q))
     return out

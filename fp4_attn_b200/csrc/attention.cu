@@ -452,9 +452,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 // as two fp16 planes hi = fp16(Vhat), lo = fp16(Vhat - hi) in the layout the
 // attention kernel loads: row (b*Hkv + h)*D + d, column t (Tp columns).
 // One CTA per 16 consecutive tokens of the flattened B*T axis (one NVFP4
-// block along tokens for every channel).
+// block along tokens for every channel); the 16 x Hkv*D slab stays in
+// shared memory in the input's own type (exact), so Hkv*D is limited by it.
 constexpr int VP_THREADS = 256;
-constexpr int VP_MAX_HD = 2048;
+constexpr int VP_MAX_HD_16 = 6144;  // bf16 / fp16 inputs
+constexpr int VP_MAX_HD_32 = 3072;  // fp32 inputs
+__host__ __device__ constexpr int vp_ld(int hdn, int esz) { return hdn + (esz == 2 ? 2 : 1); }
+__host__ __device__ constexpr size_t vp_smem_bytes(int hdn, int esz) {
+  return (size_t)16 * vp_ld(hdn, esz) * esz + 32 * sizeof(float);
+}
 
 struct VPrepArgs {
   const void* v;  // bf16 / f16 / f32, [B, Hkv, T, D] with element strides
@@ -471,12 +477,14 @@ struct VPrepArgs {
 template <int DT>
 __global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
   using T = typename In<DT>::T;
-  extern __shared__ float vp_smem[];  // [16][HDn + 1] token slab, then g[16], rg[16]
+  extern __shared__ __align__(16) unsigned char vp_raw[];  // [16][ld] token slab in T, then g[16], rg[16]
+  T* vp_smem = reinterpret_cast<T*>(vp_raw);
   const int HDn = p.Hkv * p.D;
-  const int ld = HDn + 1;
-  float* gtok = vp_smem + 16 * ld;
+  const int ld = vp_ld(HDn, (int)sizeof(T));
+  float* gtok = reinterpret_cast<float*>(vp_raw + (size_t)16 * ld * sizeof(T));
   float* rgtok = gtok + 16;
 #define slab(tk, c) vp_smem[(tk) * ld + (c)]
+#define slabf(tk, c) In<DT>::f(vp_smem[(tk) * ld + (c)])
   const int64_t BT = (int64_t)p.B * p.T;
   const int64_t j0 = (int64_t)blockIdx.x * 16;
   // load 16 tokens x all channels (zeros past the end: the reference pads B*T to x16);
@@ -488,30 +496,25 @@ __global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
       const int rem = idx - tk * (p.Hkv * dv);
       const int h = rem / dv, d0 = (rem - h * dv) * 8;
       const int64_t jj = j0 + tk;
-      float x[8];
+      uint4 u = make_uint4(0u, 0u, 0u, 0u);  // zeros are +0 in every input type
       if (jj < BT) {
         const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + (int64_t)b * p.sB +
-                                                              (int64_t)h * p.sH + (int64_t)t * p.sT + d0));
-        const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = In<DT>::f(e[k]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = 0.0f;
+        u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + (int64_t)b * p.sB +
+                                                 (int64_t)h * p.sH + (int64_t)t * p.sT + d0));
       }
+      const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) slab(tk, h * p.D + d0 + k) = x[k];
+      for (int k = 0; k < 8; ++k) slab(tk, h * p.D + d0 + k) = e[k];
     }
   } else {
     for (int idx = threadIdx.x; idx < 16 * HDn; idx += VP_THREADS) {
       const int tk = idx / HDn, c = idx - tk * HDn;
       const int64_t jj = j0 + tk;
-      float x = 0.0f;
+      T x{};
       if (jj < BT) {
         const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
         const int h = c / p.D, d = c - h * p.D;
-        x = In<DT>::f(reinterpret_cast<const T*>(p.v)[(int64_t)b * p.sB + (int64_t)h * p.sH + (int64_t)t * p.sT + d]);
+        x = reinterpret_cast<const T*>(p.v)[(int64_t)b * p.sB + (int64_t)h * p.sH + (int64_t)t * p.sT + d];
       }
       slab(tk, c) = x;
     }
@@ -521,7 +524,7 @@ __global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   for (int tk = warp; tk < 16; tk += VP_THREADS / 32) {
     float mx = 0.0f;
-    for (int c = lane; c < HDn; c += 32) mx = nanmax(mx, fabsf(slab(tk, c)));
+    for (int c = lane; c < HDn; c += 32) mx = nanmax(mx, fabsf(slabf(tk, c)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = nanmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) {
@@ -538,7 +541,7 @@ __global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      x[i] = mul<FP4_ARITH_F32>(slab(i, c), rgtok[i]);
+      x[i] = mul<FP4_ARITH_F32>(slabf(i, c), rgtok[i]);
       amax = nanmax(amax, fabsf(x[i]));
     }
     const uint8_t sb = e4m3_torch(mul<FP4_ARITH_F32>(amax, r6));
@@ -588,6 +591,7 @@ __global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
     }
   }
 #undef slab
+#undef slabf
 }
 
 template <int DT>
@@ -595,7 +599,8 @@ static void vprep_launch(const VPrepArgs& a, unsigned blocks, size_t smem, cudaS
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(vprep_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (16 * (VP_MAX_HD + 1) + 32) * (int)sizeof(float));
+                         (int)vp_smem_bytes(DT == FP4_DT_F32 ? VP_MAX_HD_32 : VP_MAX_HD_16,
+                                            DT == FP4_DT_F32 ? 4 : 2));
     attr = true;
   }
   vprep_kernel<DT><<<blocks, VP_THREADS, smem, st>>>(a);
@@ -603,7 +608,7 @@ static void vprep_launch(const VPrepArgs& a, unsigned blocks, size_t smem, cudaS
 
 static int launch_vprep(const VPrepArgs& a, cudaStream_t st) {
   const unsigned blocks = (unsigned)(((int64_t)a.B * a.T + 15) / 16);
-  const size_t smem = (16 * (size_t)(a.Hkv * a.D + 1) + 32) * sizeof(float);
+  const size_t smem = vp_smem_bytes(a.Hkv * a.D, a.in_dtype == FP4_DT_F32 ? 4 : 2);
   switch (a.in_dtype) {
     case FP4_DT_F32: vprep_launch<FP4_DT_F32>(a, blocks, smem, st); break;
     case FP4_DT_BF16: vprep_launch<FP4_DT_BF16>(a, blocks, smem, st); break;
@@ -630,7 +635,8 @@ extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, in
   clear_error();
   if (!v || !v_hi || !v_lo) return set_error(FP4ATTN_ERR_ARG, "null pointer");
   if (B <= 0 || Hkv <= 0 || T <= 0 || D <= 0 || Tp < T) return set_error(FP4ATTN_ERR_ARG, "bad shape");
-  if (Hkv * D > VP_MAX_HD) return set_error(FP4ATTN_ERR_UNSUPPORTED, "Hkv*D > %d", VP_MAX_HD);
+  const int max_hd = in_dtype == FP4_DT_F32 ? VP_MAX_HD_32 : VP_MAX_HD_16;
+  if (Hkv * D > max_hd) return set_error(FP4ATTN_ERR_UNSUPPORTED, "Hkv*D > %d", max_hd);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (Tp > T) {  // padded key columns must read as zeros
     const size_t bytes = (size_t)B * Hkv * D * Tp * 2;

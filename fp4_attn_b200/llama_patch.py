@@ -1,0 +1,125 @@
+"""FP4 attention inside the Hugging Face Llama attention module.
+
+Mirror of the reference's patch (llama_patch.py:108-250, installed by
+eval.py:176-179 over transformers' LlamaAttention.forward) on the B200
+kernels:
+
+* ``fp4_eager_attention(module, query, key, value, attention_mask, scaling,
+  dropout=0.0, **kw) -> (out [B, T, Hq, D], None)`` is the attention
+  interface of llama_patch.eager_attention_forward (llama_patch.py:57-105)
+  with the Q/K/V and P fake-quant: the tcgen05 FP4 attention kernel.  P is
+  never materialised, so the weights slot is None.
+* ``llama_fp4_attention_forward`` is a drop-in LlamaAttention.forward
+  (transformers 5.x signature): projections, RoPE, the KV-cache update,
+  ``fp4_eager_attention``, o_proj.
+* ``install()`` / ``uninstall()`` swap it in and out like eval.py does.
+
+Semantics that differ from the reference, by design:
+
+* Q/K/V are quantized after RoPE.  The reference quantizes before RoPE
+  (llama_patch.py:167-210) and applies RoPE to the dequantized values, which
+  leaves them off the FP4 grid; QK^T on FP4 tensor cores needs FP4
+  operands, so the native path quantizes the rotated Q and K.
+* Single-slice Q and P.  The reference reads FP4_USE_DUAL_QUANT_Q and
+  FP4_USE_DUAL_QUANT_ATTN (default true, llama_patch.py:84,183); here an
+  unset variable means single, and "true" raises NotImplementedError.
+* The quantizer arithmetic is fp32 (the FP4Quantizer default) whatever the
+  model dtype; the reference uses the weight dtype (llama_patch.py:126-134).
+* Prefill only: query and key lengths must match (a non-empty KV cache,
+  i.e. decode, raises).  The attention mask must be causal without padding.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .attention import fp4_attention_fwd
+
+_ORIGINAL = None
+
+
+def _dual_requested(name: str) -> bool:
+    v = os.getenv(name)
+    if v is None:
+        return False
+    return v.strip().lower() == "true"
+
+
+def _check_mask(mask: torch.Tensor | None, T: int, S: int) -> None:
+    if mask is None:
+        return
+    if mask.dim() != 4 or mask.shape[-2] != T or mask.shape[-1] < S:
+        raise ValueError(f"attention mask of shape {tuple(mask.shape)} does not match T={T}, S={S}")
+    m = mask[..., :S]
+    if m.dtype == torch.bool:
+        allowed = m
+    else:
+        allowed = m > torch.finfo(m.dtype).min / 2
+    causal = torch.ones(T, S, dtype=torch.bool, device=m.device).tril()
+    if not bool((allowed == causal).all()):
+        raise NotImplementedError("the FP4 attention kernel supports a plain causal mask (no padding)")
+
+
+def fp4_eager_attention(module, query, key, value, attention_mask, scaling, dropout=0.0, **kwargs):
+    """eager_attention_forward (llama_patch.py:57-105) on the FP4 kernel: ([B, T, Hq, D], None)."""
+    if _dual_requested("FP4_USE_DUAL_QUANT_ATTN"):
+        raise NotImplementedError("dual-slice P quantization is not implemented by the FP4 kernel")
+    if dropout and getattr(module, "training", False):
+        raise NotImplementedError("attention dropout is not supported")
+    B, Hq, T, D = query.shape
+    S = key.shape[2]
+    if S != T:
+        raise NotImplementedError(f"prefill only: query length {T} != key length {S}")
+    _check_mask(attention_mask, T, S)
+    out = fp4_attention_fwd(query, key, value, causal=True, scaling=float(scaling))
+    return out.to(query.dtype), None
+
+
+# the attention call used by llama_fp4_attention_forward (tests may wrap it)
+attention_interface = fp4_eager_attention
+
+
+def llama_fp4_attention_forward(self, hidden_states, position_embeddings=None, attention_mask=None,
+                                past_key_values=None, **kwargs):
+    """LlamaAttention.forward with FP4 attention (llama_patch.py:108-250, post-RoPE quantization)."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+
+    if _dual_requested("FP4_USE_DUAL_QUANT_Q"):
+        raise NotImplementedError("dual-slice Q quantization is not implemented by the FP4 kernel")
+    if "past_key_value" in kwargs and past_key_values is None:  # older transformers keyword
+        past_key_values = kwargs.pop("past_key_value")
+    input_shape = hidden_states.shape[:-1]
+    hidden_shape = (*input_shape, -1, self.head_dim)
+    q = self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+    k = self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+    v = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+    cos, sin = position_embeddings
+    q, k = apply_rotary_pos_emb(q, k, cos, sin)
+    if past_key_values is not None:
+        k, v = past_key_values.update(k, v, self.layer_idx)
+    if torch.isnan(q).any() or torch.isnan(k).any() or torch.isnan(v).any():  # llama_patch.py:228-232
+        raise FloatingPointError("NaN in the attention inputs")
+    out, weights = attention_interface(self, q, k, v, attention_mask, scaling=self.scaling,
+                                       dropout=0.0 if not self.training else self.attention_dropout)
+    out = out.reshape(*input_shape, -1).contiguous()
+    return self.o_proj(out), weights
+
+
+def install() -> None:
+    """Route transformers' LlamaAttention.forward to the FP4 path (eval.py:176-179)."""
+    global _ORIGINAL
+    from transformers.models.llama import modeling_llama
+
+    if _ORIGINAL is None:
+        _ORIGINAL = modeling_llama.LlamaAttention.forward
+    modeling_llama.LlamaAttention.forward = llama_fp4_attention_forward
+
+
+def uninstall() -> None:
+    global _ORIGINAL
+    from transformers.models.llama import modeling_llama
+
+    if _ORIGINAL is not None:
+        modeling_llama.LlamaAttention.forward = _ORIGINAL
+        _ORIGINAL = None

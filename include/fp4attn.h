@@ -136,7 +136,8 @@ int fp4q_global_scale(const void* x, int in_dtype, int B, int T, int H, int D, i
  * fp16 hi/lo planes [B*Hkv*D][Tp] (row (b*Hkv+h)*D+d, column t; hi+lo keeps
  * 22 significant bits of Vhat, |Vhat| < 65504).  v is [B,Hkv,T,D] with
  * element strides sB, sH, sT and d contiguous.  vhat (fp32, same layout) and
- * g ([B*T], per-token global scale) are optional outputs.  Hkv*D <= 2048. */
+ * g ([B*T], per-token global scale) are optional outputs.  Hkv*D <= 6144
+ * (bf16 / fp16 input) or 3072 (fp32 input). */
 int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, int T, int D, int64_t sB, int64_t sH, int64_t sT,
                       int Tp, uint16_t* v_hi, uint16_t* v_lo, float* vhat, float* g, void* stream);
 
@@ -148,6 +149,25 @@ int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const fl
                        const uint8_t* k_scales, const float* k_g, const uint16_t* v_hi, const uint16_t* v_lo,
                        float* out, int B, int Hq, int Hkv, int T, int Tp, int D, int causal, float scaling,
                        int num_ctas, void* stream);
+
+/* Workspace of fp4attn_forward for a shape: writes the byte offsets of its
+ * eight pieces -- Q codes, Q scale atoms, Q g, K codes, K scale atoms, K g,
+ * V-hat hi plane, V-hat lo plane, each 256-byte aligned, laid out as steps 1
+ * and 2 above describe -- to offsets[0..7] (may be NULL) and returns the
+ * total size in bytes; -1 for a bad shape.  No reference counterpart: the
+ * reference materialises the fake-quantized tensors in torch instead. */
+int64_t fp4attn_workspace_layout(int B, int Hq, int Hkv, int T, int D, int64_t* offsets);
+
+/* Steps 1-3 as one call: q [B,Hq,T,D], k and v [B,Hkv,T,D] in in_dtype
+ * (FP4_DT_F32 / BF16 / F16) with element strides (sB, sH, sT) each and d
+ * contiguous; out fp32 [B,T,Hq,D]; the packed operands go to workspace
+ * (256-byte aligned, at least fp4attn_workspace_layout bytes).  Replaces the
+ * Q/K/V fake-quant of llama_patch.py:167-196 plus eager_attention_forward
+ * with P fake-quant (llama_patch.py:57-105). */
+int fp4attn_forward(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv, int T, int D,
+                    int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH, int64_t k_sT, int64_t v_sB,
+                    int64_t v_sH, int64_t v_sT, int causal, float scaling, float* out, void* workspace,
+                    int64_t workspace_bytes, void* stream);
 
 /* Profiling aid: a non-NULL buf makes later fp4attn_fwd_packed calls record
  * an event timeline (SM clock cycles from clock64) of each CTA's first work unit into

@@ -21,22 +21,9 @@ from oracle import torch_port as tp
 
 pytestmark = pytest.mark.gpu
 
-DELTA = 1e-5
+from attn_check import DELTA, check  # noqa: E402
+
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
-
-
-def check(o_gpu, o_ref, flags=None, max_masked_frac=0.25):
-    o_gpu, o_ref = o_gpu.double(), o_ref.double()
-    rms = o_ref.pow(2).mean().sqrt()
-    cos = torch.nn.functional.cosine_similarity(o_gpu.flatten(), o_ref.flatten(), dim=0)
-    assert cos >= 0.9999, f"cosine {cos}"
-    err = (o_gpu - o_ref).abs().amax(-1)  # per (b, t, h) row
-    ok = torch.ones_like(err, dtype=torch.bool) if flags is None else ~flags
-    if flags is not None:
-        assert flags.float().mean() <= max_masked_frac, f"masked fraction {flags.float().mean()}"
-    worst = err[ok].max() / rms
-    assert worst <= 2e-2, f"max-abs / RMS on decided rows = {worst}"
-    return float(cos), float(worst)
 
 
 def _run(q, k, v, causal):

@@ -60,3 +60,33 @@ def test_python_api_refuses_cpu_tensors():
     from fp4_attn_b200 import FP4Quantizer
     with pytest.raises(RuntimeError, match="CUDA"):
         FP4Quantizer().single_nvfp4(torch.randn(4, 16))
+
+
+def test_attention_workspace_layout():
+    """Pieces of the fp4attn_forward workspace: 256-byte aligned, in order, sized for the Llama-3-8B shape."""
+    from fp4_attn_b200 import _lib
+    L = _lib.load()
+    offs = (ctypes.c_int64 * 8)()
+    B, Hq, Hkv, T, D = 1, 32, 8, 4096, 128
+    total = L.fp4attn_workspace_layout(B, Hq, Hkv, T, D, offs)
+    sizes = [T * Hq * D // 2, T // 128 * Hq * 2 * 512, T * 4, T * Hkv * D // 2, T // 128 * Hkv * 2 * 512, T * 4,
+             Hkv * D * T * 2, Hkv * D * T * 2]
+    o = list(offs)
+    assert o[0] == 0 and all(x % 256 == 0 for x in o)
+    for i in range(7):
+        assert o[i + 1] >= o[i] + sizes[i]
+    assert total >= o[7] + sizes[7] and total % 256 == 0
+    assert L.fp4attn_workspace_layout(1, 3, 2, 128, 128, None) == -1  # Hq % Hkv != 0
+    assert L.fp4attn_workspace_layout(1, 2, 1, 0, 128, None) == -1
+
+
+def test_attention_forward_argument_errors():
+    from fp4_attn_b200 import _lib
+    L = _lib.load()
+    args = [None, None, None, 1, 1, 2, 1, 128, 128] + [0] * 9 + [1, 0.1, None, None, 0, None]
+    assert L.fp4attn_forward(*args) == 1
+    assert b"null" in L.fp4attn_last_error()
+    p = ctypes.c_void_p(256)
+    args = [p, p, p, 1, 1, 2, 1, 128, 128] + [0] * 9 + [1, 0.1, p, p, 16, None]
+    assert L.fp4attn_forward(*args) == 1
+    assert b"workspace" in L.fp4attn_last_error()

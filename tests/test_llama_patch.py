@@ -1,0 +1,70 @@
+"""Host logic of fp4_attn_b200.llama_patch on CPU: patching, refusals, masks.
+
+No kernel runs here: every case stops at a check before the GPU (and the
+kernel path itself refuses CPU tensors -- there is no CPU fallback).
+"""
+import pytest
+import torch
+
+from fp4_attn_b200 import llama_patch as lp
+
+
+def _tiny_model():
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=1, num_attention_heads=2,
+                      num_key_value_heads=1, head_dim=128, vocab_size=64, max_position_embeddings=64,
+                      attn_implementation="eager")
+    torch.manual_seed(0)
+    return LlamaForCausalLM(cfg).eval()
+
+
+def test_install_uninstall_restores_forward():
+    from transformers.models.llama import modeling_llama as M
+    orig = M.LlamaAttention.forward
+    lp.install()
+    try:
+        assert M.LlamaAttention.forward is lp.llama_fp4_attention_forward
+        lp.install()  # idempotent
+    finally:
+        lp.uninstall()
+    assert M.LlamaAttention.forward is orig
+
+
+def test_dual_quant_request_is_refused(monkeypatch):
+    model = _tiny_model()
+    ids = torch.randint(0, 64, (1, 8))
+    monkeypatch.setenv("FP4_USE_DUAL_QUANT_Q", "true")
+    lp.install()
+    try:
+        with pytest.raises(NotImplementedError):
+            model(ids)
+    finally:
+        lp.uninstall()
+
+
+def test_cpu_tensors_are_refused():
+    q = torch.randn(1, 2, 16, 128).bfloat16()
+    k = torch.randn(1, 1, 16, 128).bfloat16()
+    with pytest.raises(RuntimeError):
+        lp.fp4_eager_attention(torch.nn.Module(), q, k, k, None, scaling=128 ** -0.5)
+
+
+def test_decode_shape_is_refused():
+    q = torch.randn(1, 2, 1, 128)
+    k = torch.randn(1, 1, 16, 128)
+    with pytest.raises(NotImplementedError):
+        lp.fp4_eager_attention(torch.nn.Module(), q, k, k, None, scaling=1.0)
+
+
+def test_mask_check():
+    T = 8
+    causal = torch.full((T, T), torch.finfo(torch.float32).min).triu(1)[None, None]
+    lp._check_mask(causal, T, T)
+    lp._check_mask(None, T, T)
+    lp._check_mask(torch.ones(T, T, dtype=torch.bool).tril()[None, None], T, T)
+    padded = causal.clone()
+    padded[..., :, 0] = torch.finfo(torch.float32).min  # a padded first key
+    with pytest.raises(NotImplementedError):
+        lp._check_mask(padded, T, T)
+    with pytest.raises(ValueError):
+        lp._check_mask(causal[..., :4, :], T, T)

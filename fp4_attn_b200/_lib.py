@@ -34,6 +34,8 @@ SIGNATURES = {
     "fp4attn_workspace_layout": ([_I, _I, _I, _I, _I, _P], _L),
     "fp4attn_forward": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _P, _P, _L,
                          _P], _I),
+    "fp4attn_forward_noalloc": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _P,
+                                 _P], _I),
     "nvfp4sim_f32_to_nvf4": ([_P, _P, _P, _L, _P], _I),
     "nvfp4sim_f32_to_nvf4_nosearch": ([_P, _P, _P, _L, _P], _I),
     "nvfp4sim_f16_to_nvf4": ([_P, _P, _P, _L, _P], _I),

@@ -169,6 +169,22 @@ int fp4attn_forward(const void* q, const void* k, const void* v, int in_dtype, i
                     int64_t v_sH, int64_t v_sT, int causal, float scaling, float* out, void* workspace,
                     int64_t workspace_bytes, void* stream);
 
+/* fp4attn_forward without a caller workspace; allocates no device memory.
+ * No counterpart in the reference.  For callers that cannot hand the library
+ * device memory: a C/FFI binding without a device allocator of its own, or a
+ * serving loop that must not call cudaMalloc per request (it can synchronize
+ * the device and fail under memory pressure).  The packed operands live in a
+ * fixed library-owned device array of 32 MiB (33554432 bytes); shapes whose
+ * fp4attn_workspace_layout size exceeds it are rejected with
+ * FP4ATTN_ERR_UNSUPPORTED.  The array's address is looked up on the first
+ * call per device, so make that call before any stream capture.  All calls
+ * share the array: calls whose GPU work overlaps race; issue them on one
+ * stream or order them with events.  Nothing has to start zeroed. */
+int fp4attn_forward_noalloc(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv, int T,
+                            int D, int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH, int64_t k_sT,
+                            int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling, float* out,
+                            void* stream);
+
 /* Profiling aid: a non-NULL buf makes later fp4attn_fwd_packed calls record
  * an event timeline (SM clock cycles from clock64) of each CTA's first work unit into
  * buf[cta * 512 + slot] (grid * 512 int64 entries); NULL turns it off. */

@@ -25,7 +25,7 @@
 // runs as two kind::f16 MMAs with A = Phat read from TMEM.  O = acc / sum.
 //
 // Schedule.  A work unit is (batch, query head, 128-query tile); persistent
-// CTAs take units longest-first (causal cost grows with the tile index).
+// CTAs take units longest-first in snake order (causal cost grows with the tile index).
 // Warp 0 loads Q and K by TMA (codes, scale atoms, global scales), warp 2
 // loads V-hat half tiles, warp 1 issues the tcgen05 MMAs, and warps 4-19 are
 // four softmax warpgroups: warpgroup q owns key columns 32q..32q+31 of every
@@ -121,6 +121,16 @@ __device__ __forceinline__ Unit unit_of(int u, const AttnArgs& p) {
   return r;
 }
 
+// The i-th unit of this CTA, or -1 past its last.  Units are numbered longest
+// first; round r hands them to CTAs 0..G-1 on even rounds and G-1..0 on odd
+// rounds ("snake"), which evens out the causal cost across CTAs (only the
+// last round is partial, so a CTA's units are rounds 0, 1, ... without gaps).
+__device__ __forceinline__ int cta_unit(int i, int units) {
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  const int u = i * G + ((i & 1) ? G - 1 - c : c);
+  return u < units ? u : -1;
+}
+
 __device__ __forceinline__ int kv_tiles(const Unit& un, const AttnArgs& p) {
   return p.causal ? un.qt + 1 : p.Tp / attn::BN;
 }
@@ -143,8 +153,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint64_t* v_full = bar + 10;   // [NV]
   uint64_t* v_empty = bar + 14;  // [NV]
   uint64_t* s_full = bar + 18;   // [2] S buffer written (MMA commit)
-  uint64_t* s_free = bar + 20;   // [2] S buffer read by every softmax warpgroup
-  uint64_t* p_full = bar + 22;   // [2] P of the tile in S/P buffer kb written by every warpgroup
+  uint64_t* s_free = bar + 20;   // [2] S buffer read by every softmax warp
+  uint64_t* p_full = bar + 22;   // [2] P of the tile in S/P buffer kb written by every softmax warp
   uint64_t* o_full = bar + 30;
   uint64_t* o_free = bar + 31;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 32);
@@ -158,7 +168,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     mbar_init(q_empty, 1);
     for (int i = 0; i < NK; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1 + NWG);  // MMA commit + every softmax warpgroup (they read gk)
+      mbar_init(&k_empty[i], 1 + 4 * NWG);  // MMA commit + every softmax warp (they read gk)
     }
     for (int i = 0; i < NV; ++i) {
       mbar_init(&v_full[i], 1);
@@ -166,10 +176,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], NWG);
+      mbar_init(&s_free[i], 4 * NWG);  // every softmax warp has loaded its rows
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], NWG);
+      mbar_init(&p_full[i], 4 * NWG);  // every softmax warp has stored its P
     }
     mbar_init(o_full, 1);
     mbar_init(o_free, 1);
@@ -196,7 +206,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       uint32_t kc = 0, uc = 0;
-      for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
+      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         const int hk = un.h / group;
@@ -226,7 +236,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       tma_prefetch_desc(&tmVhi);
       tma_prefetch_desc(&tmVlo);
       uint32_t vc = 0;
-      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units)) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         const int vrow = (un.b * p.Hkv + un.h / group) * HD;
@@ -277,7 +287,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         else ++suse0;
         ++kc;
       };
-      for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
+      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         mbar_wait(q_full, uc & 1, 0x213);
@@ -333,10 +343,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float r6 = __frcp_rn(6.0f);
     const bool leader = threadIdx.x % 128 == 0;
+    const bool wlead = (threadIdx.x & 31) == 0;  // lane 0 arrives on behalf of its warp
     const int col0 = 32 * q;
     uint32_t kc = 0, uc = 0;
     uint32_t sfu0 = 0, sfu1 = 0;  // completions seen per S buffer
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
+    for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
       const Unit un = unit_of(u, p);
       const int n = kv_tiles(un, p);
       const int qpos = un.qt * BM + r;  // query index within the sequence
@@ -354,19 +365,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         uint32_t a[32];
         tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
         tmem_ld_wait();
+        // every warp releases what it has read on its own (no warpgroup barrier)
         tc_fence_before();
-        named_bar(1 + q, 128);
-        if (leader) mbar_arrive(&s_free[kb]);
+        __syncwarp();
+        if (wlead) mbar_arrive(&s_free[kb]);
         const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
         // keys with column > lim are masked (causal diagonal tile, or keys past T)
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         if (lim < col0 + 31) m = chunk_max<true>(a, gk, col0, lim, m);
         else m = chunk_max<false>(a, gk, col0, lim, m);
-        named_bar(1 + q, 128);
-        if (leader) {
-          mbar_arrive(&k_empty[s]);
-          if (q == 0) trace(p, uc, TR_MDONE, j);
-        }
+        __syncwarp();
+        if (wlead) mbar_arrive(&k_empty[s]);
+        if (leader && q == 0) trace(p, uc, TR_MDONE, j);
       }
       stat_m[q * 128 + r] = m;
       named_bar(1 + NWG, NWG * 128);
@@ -386,13 +396,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         uint32_t a[32];
         tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
         tmem_ld_wait();
-        // this quarter's scores are in registers: release the S buffer now
+        // this warp's scores are in registers: release its share of the S buffer now
         tc_fence_before();
-        named_bar(1 + q, 128);
-        if (leader) {
-          mbar_arrive(&s_free[kb]);
-          if (q == 0) trace(p, uc, TR_LDDONE, j);
-        }
+        __syncwarp();
+        if (wlead) mbar_arrive(&s_free[kb]);
+        if (leader && q == 0) trace(p, uc, TR_LDDONE, j);
         const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         uint32_t pk[16];
@@ -403,13 +411,13 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tmem_st16(tmem + lane_base + T_S + 128 * kb + col0, pk);
         tmem_st_wait();
         tc_fence_before();
-        named_bar(1 + q, 128);
-        if (leader) {
+        __syncwarp();
+        if (wlead) {
           mbar_arrive(&p_full[kb]);
           mbar_arrive(&k_empty[s]);
-          if (q == 0) trace(p, uc, TR_PDONE, j);
-          if (q == 3) trace(p, uc, TR_PDONE3, j);
         }
+        if (leader && q == 0) trace(p, uc, TR_PDONE, j);
+        if (leader && q == 3) trace(p, uc, TR_PDONE3, j);
       }
       float l0, l1;
       upk2(add2(add2(lsum2[0], lsum2[1]), add2(lsum2[2], lsum2[3])), l0, l1);

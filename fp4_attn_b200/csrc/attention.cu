@@ -27,11 +27,11 @@
 // Schedule.  A work unit is (batch, query head, 128-query tile); persistent
 // CTAs take units longest-first in snake order (causal cost grows with the tile index).
 // Warp 0 loads Q and K by TMA (codes, scale atoms, global scales), warp 2
-// loads V-hat half tiles, warp 1 issues the tcgen05 MMAs, and warps 4-19 are
-// four softmax warpgroups: warpgroup q owns key columns 32q..32q+31 of every
+// loads V-hat tiles, warp 1 issues the QK^T MMAs, warp 3 the PV MMAs, and
+// warps 4-19 are four softmax warpgroups: warpgroup q owns key columns 32q..32q+31 of every
 // tile.  S is double-buffered in TMEM; each warpgroup writes its quarter of
 // P-hat over the S columns it has already loaded, so PV(j) reads P from S(j)'s
-// buffer and QK(j+2) reuses the buffer after it (in-order tensor pipe).  Every
+// buffer and QK(j+2) reuses the buffer once PV(j) has completed (pv_done).  Every
 // wait is bounded (sm100.cuh).
 #include <cuda.h>
 
@@ -135,11 +135,17 @@ __device__ __forceinline__ int kv_tiles(const Unit& un, const AttnArgs& p) {
   return p.causal ? un.qt + 1 : p.Tp / attn::BN;
 }
 
+// TRACE: record the event timeline (fp4attn_set_trace); the plain instantiation
+// has no trace code at all.
+template <bool TRACE>
 __global__ void __launch_bounds__(attn::THREADS, 1)
     fp4_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmVhi, const __grid_constant__ CUtensorMap tmVlo,
                     AttnArgs p) {
   using namespace attn;
+  auto tr = [&](uint32_t uc, int slot, int j) {
+    if constexpr (TRACE) trace(p, uc, slot, j);
+  };
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* stat_m = reinterpret_cast<float*>(sm + OFF_STAT);
@@ -155,6 +161,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint64_t* s_full = bar + 18;   // [2] S buffer written (MMA commit)
   uint64_t* s_free = bar + 20;   // [2] S buffer read by every softmax warp
   uint64_t* p_full = bar + 22;   // [2] P of the tile in S/P buffer kb written by every softmax warp
+  uint64_t* pv_done = bar + 24;  // [2] PV has read the P in S/P buffer kb (PV thread's commit)
   uint64_t* o_full = bar + 30;
   uint64_t* o_free = bar + 31;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 32);
@@ -180,6 +187,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], 4 * NWG);  // every softmax warp has stored its P
+      mbar_init(&pv_done[i], 1);
     }
     mbar_init(o_full, 1);
     mbar_init(o_free, 1);
@@ -198,7 +206,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) trace(p, 0, TR_START, 0);
+  if (threadIdx.x == 0) tr(0, TR_START, 0);
 
   if (warp == 0) {
     // ------------------------------------------------- producer: Q and K
@@ -254,22 +262,29 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ----------------------------------------------------------- MMA issue
+    // ------------------------------------------------------- QK^T issue
+    // One elected thread issues every S = Q K^T (both passes) into the two S
+    // buffers.  A buffer is reused once every softmax warp has loaded the
+    // scores in it (s_free) and, after a pass-2 tile, once PV has read the P
+    // that the softmax wrote over them (pv_done, committed by the PV thread).
     if (elect_one_lane()) {
       const uint32_t idq = idesc_nvf4(BM, BN);
-      const uint32_t idv = idesc_f16(BM, HD);
-      uint32_t kc = 0, vc = 0, uc = 0;
-      // uses of each S buffer and pass-2 tiles per buffer (kept in registers:
-      // two scalars selected by the buffer index, not a dynamically indexed array)
-      uint32_t suse0 = 0, suse1 = 0, pu0 = 0, pu1 = 0;
+      uint32_t kc = 0, uc = 0;
+      // per S buffer (two scalars selected by the buffer index): QKs issued into
+      // it, pass-2 tiles whose P went into it, and PV completions waited for
+      uint32_t suse0 = 0, suse1 = 0, pvi0 = 0, pvi1 = 0, pvw0 = 0, pvw1 = 0;
       auto issue_qk = [&](int j, int kb, int pass) {
-        // S buffer kb: its previous scores must have been read by every warpgroup
         const uint32_t su = kb ? suse1 : suse0;
         if (su > 0) mbar_wait(&s_free[kb], (su - 1) & 1, 0x211);
+        if ((kb ? pvw1 : pvw0) < (kb ? pvi1 : pvi0)) {
+          mbar_wait(&pv_done[kb], (kb ? pvw1 : pvw0) & 1, 0x217);
+          if (kb) ++pvw1;
+          else ++pvw0;
+        }
         const int s = kc % NK;
         mbar_wait(&k_full[s], (kc / NK) & 1, 0x212);
         tc_fence_after();
-        trace(p, uc, TR_QK + 32 * pass, j);
+        tr(uc, TR_QK + 32 * pass, j);
         uint8_t* ks = sm + OFF_K + s * K_STAGE;
         const uint32_t sfb = tmem + T_SFB + 8 * s;
         tmem_cp_sf_atom(sfb, smem_desc(smem_u32(ks + 8192), 16, 128, kSwizzleNone));
@@ -283,37 +298,51 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         }
         tc_commit(&k_empty[s]);
         tc_commit(&s_full[kb]);
-        if (kb) ++suse1;
-        else ++suse0;
+        if (kb) {
+          ++suse1;
+          if (pass) ++pvi1;
+        } else {
+          ++suse0;
+          if (pass) ++pvi0;
+        }
         ++kc;
       };
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         mbar_wait(q_full, uc & 1, 0x213);
-        trace(p, uc, TR_UNIT, 0);
+        tr(uc, TR_UNIT, 0);
         tc_fence_after();
         tmem_cp_sf_atom(tmem + T_SFA, smem_desc(smem_u32(sm + OFF_QSF), 16, 128, kSwizzleNone));
         tmem_cp_sf_atom(tmem + T_SFA + 4, smem_desc(smem_u32(sm + OFF_QSF + 512), 16, 128, kSwizzleNone));
-        // pass 1: scores only
-        for (int j = 0; j < n; ++j) issue_qk(j, j & 1, 0);
-        // pass 2: scores again, then PV over the whole tile once every warpgroup
-        // has written its quarter of P.  P(j) lives in S(j)'s TMEM buffer, so
-        // QK(j+2) is issued after PV(j): the tensor pipe runs a thread's MMAs in
-        // order, so PV(j) has read P(j) before QK(j+2) overwrites the buffer.
-        issue_qk(0, 0, 1);
-        if (n > 1) issue_qk(1, 1, 1);
+        for (int pass = 0; pass < 2; ++pass)
+          for (int j = 0; j < n; ++j) issue_qk(j, j & 1, pass);
+        tc_commit(q_empty);
+        tr(uc, TR_UEND, 0);
+      }
+    }
+  } else if (warp == 3) {
+    // --------------------------------------------------------- PV issue
+    // One elected thread issues O += P V-hat (hi and lo planes) per pass-2
+    // tile once every softmax warp has written its rows of P (over the S
+    // columns it has read) and the V-hat tile has landed.
+    if (elect_one_lane()) {
+      const uint32_t idv = idesc_f16(BM, HD);
+      uint32_t vc = 0, uc = 0, pu0 = 0, pu1 = 0;
+      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
+        const Unit un = unit_of(u, p);
+        const int n = kv_tiles(un, p);
         for (int j = 0; j < n; ++j, ++vc) {
           const int kb = j & 1, vs = vc % NV;
           const uint32_t pbuf = tmem + T_S + 128 * kb;
           mbar_wait(&v_full[vs], (vc / NV) & 1, 0x215);
-          trace(p, uc, TR_PWAIT, j);
+          tr(uc, TR_PWAIT, j);
           mbar_wait(&p_full[kb], (kb ? pu1 : pu0) & 1, 0x214);
           if (kb) ++pu1;
           else ++pu0;
           if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
           tc_fence_after();
-          trace(p, uc, TR_PV, j);
+          tr(uc, TR_PV, j);
           const uint32_t v = smem_u32(sm + OFF_V + vs * V_STAGE);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {  // keys 16kk .. 16kk+15
@@ -326,11 +355,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             }
           }
           tc_commit(&v_empty[vs]);
-          if (j + 2 < n) issue_qk(j + 2, kb, 1);
+          tc_commit(&pv_done[kb]);
         }
         tc_commit(o_full);
-        tc_commit(q_empty);
-        trace(p, uc, TR_UEND, 0);
       }
     }
   } else if (warp >= 4) {
@@ -360,7 +387,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x222);
         if (kb) ++sfu1;
         else ++sfu0;
-        if (leader && q == 0) trace(p, uc, TR_SFULL, j);
+        if (leader && q == 0) tr(uc, TR_SFULL, j);
         tc_fence_after();
         uint32_t a[32];
         tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
@@ -376,7 +403,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         else m = chunk_max<false>(a, gk, col0, lim, m);
         __syncwarp();
         if (wlead) mbar_arrive(&k_empty[s]);
-        if (leader && q == 0) trace(p, uc, TR_MDONE, j);
+        if (leader && q == 0) tr(uc, TR_MDONE, j);
       }
       stat_m[q * 128 + r] = m;
       named_bar(1 + NWG, NWG * 128);
@@ -391,7 +418,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x223);
         if (kb) ++sfu1;
         else ++sfu0;
-        if (leader && q == 0) trace(p, uc, TR_SFULL + 32, j);
+        if (leader && q == 0) tr(uc, TR_SFULL + 32, j);
         tc_fence_after();
         uint32_t a[32];
         tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
@@ -400,13 +427,13 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (wlead) mbar_arrive(&s_free[kb]);
-        if (leader && q == 0) trace(p, uc, TR_LDDONE, j);
+        if (leader && q == 0) tr(uc, TR_LDDONE, j);
         const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         uint32_t pk[16];
         if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
         else chunk_p<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
-        if (leader && q == 0) trace(p, uc, TR_COMP, j);
+        if (leader && q == 0) tr(uc, TR_COMP, j);
         // P quarter q goes over the first 16 of this warpgroup's S columns
         tmem_st16(tmem + lane_base + T_S + 128 * kb + col0, pk);
         tmem_st_wait();
@@ -416,8 +443,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           mbar_arrive(&p_full[kb]);
           mbar_arrive(&k_empty[s]);
         }
-        if (leader && q == 0) trace(p, uc, TR_PDONE, j);
-        if (leader && q == 3) trace(p, uc, TR_PDONE3, j);
+        if (leader && q == 0) tr(uc, TR_PDONE, j);
+        if (leader && q == 3) tr(uc, TR_PDONE3, j);
       }
       float l0, l1;
       upk2(add2(add2(lsum2[0], lsum2[1]), add2(lsum2[2], lsum2[3])), l0, l1);
@@ -428,7 +455,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int w = 0; w < NWG; ++w) l += stat_l[w * 128 + r];
       // ---- epilogue: O rows / l, columns 32q .. 32q+31
       mbar_wait(o_full, uc & 1, 0x224);
-      if (threadIdx.x == 128) trace(p, uc, TR_OFULL, 0);
+      if (threadIdx.x == 128) tr(uc, TR_OFULL, 0);
       tc_fence_after();
       const float rl = 1.0f / l;
       uint32_t a[32];
@@ -445,7 +472,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       named_bar(1 + NWG, NWG * 128);
       if (threadIdx.x == 128) {
         mbar_arrive(o_free);
-        trace(p, uc, TR_OFREE, 0);
+        tr(uc, TR_OFREE, 0);
       }
     }
   }
@@ -703,7 +730,8 @@ extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scale
   a.trace = g_trace;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(fp4_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(fp4_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(fp4_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr = true;
   }
   int dev = 0, sms = 148;
@@ -711,6 +739,9 @@ extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scale
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int grid = num_ctas > 0 ? num_ctas : sms;
   if (grid > a.units) grid = a.units;
-  fp4_attn_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mvh, mvl, a);
+  if (a.trace)
+    fp4_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mvh, mvl, a);
+  else
+    fp4_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mvh, mvl, a);
   return check_launch("fp4_attn_kernel");
 }

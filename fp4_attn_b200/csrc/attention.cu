@@ -29,10 +29,9 @@
 // Warp 0 loads Q and K by TMA (codes, scale atoms, global scales), warp 2
 // loads V-hat tiles, warp 1 issues the QK^T MMAs, warp 3 the PV MMAs, and
 // warps 4-19 are four softmax warpgroups: warpgroup q owns key columns 32q..32q+31 of every
-// tile.  S is double-buffered in TMEM; each warpgroup writes its quarter of
-// P-hat over the S columns it has already loaded, so PV(j) reads P from S(j)'s
-// buffer and QK(j+2) reuses the buffer once PV(j) has completed (pv_done).  Every
-// wait is bounded (sm100.cuh).
+// tile.  S is double-buffered in TMEM, so QK(j+2) runs as soon as every softmax
+// warp has loaded S(j); P-hat has its own TMEM buffer, freed by PV's commit.
+// Every wait is bounded (sm100.cuh).
 #include <cuda.h>
 
 #include "common.cuh"
@@ -64,9 +63,9 @@ constexpr int OFF_RCP = OFF_STAT + 2 * NWG * 128 * 4;
 constexpr int OFF_BAR = OFF_RCP + 128 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
-// TMEM columns: S0, S1 (P of a tile is written over the first half of each warpgroup's S
-// columns once they are in registers), O, Q scale atoms, K scale atoms per stage.
-constexpr uint32_t T_S = 0, T_O = 256, T_SFA = 384, T_SFB = 392;
+// TMEM columns: S0, S1, O, P (fp16, single-buffered; warpgroup q writes columns
+// 16q..16q+15), Q scale atoms, K scale atoms per stage (488 of 512 columns).
+constexpr uint32_t T_S = 0, T_O = 256, T_P = 384, T_SFA = 448, T_SFB = 456;
 }  // namespace attn
 
 struct AttnArgs {
@@ -160,8 +159,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint64_t* v_empty = bar + 14;  // [NV]
   uint64_t* s_full = bar + 18;   // [2] S buffer written (MMA commit)
   uint64_t* s_free = bar + 20;   // [2] S buffer read by every softmax warp
-  uint64_t* p_full = bar + 22;   // [2] P of the tile in S/P buffer kb written by every softmax warp
-  uint64_t* pv_done = bar + 24;  // [2] PV has read the P in S/P buffer kb (PV thread's commit)
+  uint64_t* p_full = bar + 22;   // P written by every softmax warp
+  uint64_t* p_free = bar + 23;   // PV has read P (PV thread's commit)
   uint64_t* o_full = bar + 30;
   uint64_t* o_free = bar + 31;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 32);
@@ -185,10 +184,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4 * NWG);  // every softmax warp has loaded its rows
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], 4 * NWG);  // every softmax warp has stored its P
-      mbar_init(&pv_done[i], 1);
-    }
+    mbar_init(p_full, 4 * NWG);  // every softmax warp has stored its P
+    mbar_init(p_free, 1);
     mbar_init(o_full, 1);
     mbar_init(o_free, 1);
     fence_barrier_init();
@@ -264,23 +261,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------- QK^T issue
     // One elected thread issues every S = Q K^T (both passes) into the two S
-    // buffers.  A buffer is reused once every softmax warp has loaded the
-    // scores in it (s_free) and, after a pass-2 tile, once PV has read the P
-    // that the softmax wrote over them (pv_done, committed by the PV thread).
+    // buffers; a buffer is reused once every softmax warp has loaded the
+    // scores in it (s_free).
     if (elect_one_lane()) {
       const uint32_t idq = idesc_nvf4(BM, BN);
       uint32_t kc = 0, uc = 0;
-      // per S buffer (two scalars selected by the buffer index): QKs issued into
-      // it, pass-2 tiles whose P went into it, and PV completions waited for
-      uint32_t suse0 = 0, suse1 = 0, pvi0 = 0, pvi1 = 0, pvw0 = 0, pvw1 = 0;
+      uint32_t suse0 = 0, suse1 = 0;  // QKs issued into each S buffer (scalars, not an indexed array)
       auto issue_qk = [&](int j, int kb, int pass) {
         const uint32_t su = kb ? suse1 : suse0;
         if (su > 0) mbar_wait(&s_free[kb], (su - 1) & 1, 0x211);
-        if ((kb ? pvw1 : pvw0) < (kb ? pvi1 : pvi0)) {
-          mbar_wait(&pv_done[kb], (kb ? pvw1 : pvw0) & 1, 0x217);
-          if (kb) ++pvw1;
-          else ++pvw0;
-        }
         const int s = kc % NK;
         mbar_wait(&k_full[s], (kc / NK) & 1, 0x212);
         tc_fence_after();
@@ -298,13 +287,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         }
         tc_commit(&k_empty[s]);
         tc_commit(&s_full[kb]);
-        if (kb) {
-          ++suse1;
-          if (pass) ++pvi1;
-        } else {
-          ++suse0;
-          if (pass) ++pvi0;
-        }
+        if (kb) ++suse1;
+        else ++suse0;
         ++kc;
       };
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
@@ -324,30 +308,27 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   } else if (warp == 3) {
     // --------------------------------------------------------- PV issue
     // One elected thread issues O += P V-hat (hi and lo planes) per pass-2
-    // tile once every softmax warp has written its rows of P (over the S
-    // columns it has read) and the V-hat tile has landed.
+    // tile once every softmax warp has written its rows of P and the V-hat
+    // tile has landed; its commit frees the P buffer for the next tile.
     if (elect_one_lane()) {
       const uint32_t idv = idesc_f16(BM, HD);
-      uint32_t vc = 0, uc = 0, pu0 = 0, pu1 = 0;
+      uint32_t vc = 0, uc = 0, pu = 0;
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         for (int j = 0; j < n; ++j, ++vc) {
-          const int kb = j & 1, vs = vc % NV;
-          const uint32_t pbuf = tmem + T_S + 128 * kb;
+          const int vs = vc % NV;
           mbar_wait(&v_full[vs], (vc / NV) & 1, 0x215);
           tr(uc, TR_PWAIT, j);
-          mbar_wait(&p_full[kb], (kb ? pu1 : pu0) & 1, 0x214);
-          if (kb) ++pu1;
-          else ++pu0;
+          mbar_wait(p_full, pu & 1, 0x214);
+          ++pu;
           if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
           tc_fence_after();
           tr(uc, TR_PV, j);
           const uint32_t v = smem_u32(sm + OFF_V + vs * V_STAGE);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {  // keys 16kk .. 16kk+15
-            // warpgroup kk/2 wrote these keys' P over its S columns 32(kk/2) .. 32(kk/2)+15
-            const uint32_t a = pbuf + 32 * (kk >> 1) + 8 * (kk & 1);
+            const uint32_t a = tmem + T_P + 8 * kk;  // fp16 P of keys 16kk..16kk+15
 #pragma unroll
             for (int part = 0; part < 2; ++part) {  // hi, lo planes
               const uint32_t vb = v + ((kk >> 2) * 2 + part) * V_HALF + (kk & 3) * 32;
@@ -355,7 +336,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             }
           }
           tc_commit(&v_empty[vs]);
-          tc_commit(&pv_done[kb]);
+          tc_commit(p_free);
         }
         tc_commit(o_full);
       }
@@ -372,7 +353,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     const bool leader = threadIdx.x % 128 == 0;
     const bool wlead = (threadIdx.x & 31) == 0;  // lane 0 arrives on behalf of its warp
     const int col0 = 32 * q;
-    uint32_t kc = 0, uc = 0;
+    uint32_t kc = 0, uc = 0, pt = 0;
     uint32_t sfu0 = 0, sfu1 = 0;  // completions seen per S buffer
     for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
       const Unit un = unit_of(u, p);
@@ -434,13 +415,16 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
         else chunk_p<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
         if (leader && q == 0) tr(uc, TR_COMP, j);
-        // P quarter q goes over the first 16 of this warpgroup's S columns
-        tmem_st16(tmem + lane_base + T_S + 128 * kb + col0, pk);
+        // the previous tile's PV must have read P before quarter q is overwritten
+        if (pt > 0) mbar_wait(p_free, (pt - 1) & 1, 0x225);
+        ++pt;
+        tc_fence_after();
+        tmem_st16(tmem + lane_base + T_P + 16 * q, pk);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (wlead) {
-          mbar_arrive(&p_full[kb]);
+          mbar_arrive(p_full);
           mbar_arrive(&k_empty[s]);
         }
         if (leader && q == 0) tr(uc, TR_PDONE, j);

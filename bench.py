@@ -56,6 +56,18 @@ def parse():
     return ap.parse_args()
 
 
+def profile_traffic(name):
+    """DRAM bytes per launch of a kernel from its committed ncu summary (profiles/<name>.md), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return {"bytes": int(line.split(":")[1]), "source": f"profiles/{name}.md (ncu dram__bytes_read+write)"}
+    except OSError:
+        pass
+    return None
+
+
 def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -199,7 +211,8 @@ class QuantizeWorkload:
         peak = peaks["hbm_gbs"]
         return {"bound": "hbm", "kernel": "quant_rows_kernel", "achieved": round(achieved, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} copy bandwidth",
-                "algorithmic_bytes_per_launch": self.algo_bytes, "traffic": None}
+                "algorithmic_bytes_per_launch": self.algo_bytes,
+                "traffic": profile_traffic("quant_rows_vec_kernel_4096x4096_tensor")}
 
     # CPU: the reference's torch path restated (oracle/torch_port.py), full tensor.
     def cpu_sample(self, reps=None):
@@ -299,7 +312,8 @@ class AttentionWorkload:
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4),
-                "algorithmic_flops_per_launch": self.flops, "traffic": None}
+                "algorithmic_flops_per_launch": self.flops,
+                "traffic": profile_traffic("fp4_attn_kernel_llama3-8b_T4096")}
 
     def cpu_sample(self, reps=None):
         """The reference's CPU path (torch ops) on one KV-head group (4 of 32 query heads)."""

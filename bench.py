@@ -62,7 +62,7 @@ def profile_traffic(name):
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
-                return {"bytes": int(line.split(":")[1]), "source": f"profiles/{name}.md (ncu dram__bytes_read+write)"}
+                return int(line.split(":")[1])
     except OSError:
         pass
     return None
@@ -212,7 +212,8 @@ class QuantizeWorkload:
         return {"bound": "hbm", "kernel": "quant_rows_kernel", "achieved": round(achieved, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} copy bandwidth",
                 "algorithmic_bytes_per_launch": self.algo_bytes,
-                "traffic": profile_traffic("quant_rows_vec_kernel_4096x4096_tensor")}
+                "traffic": profile_traffic("quant_rows_vec_kernel_4096x4096_tensor"),
+                "traffic_source": "profiles/quant_rows_vec_kernel_4096x4096_tensor.md: ncu dram__bytes_read+write per launch"}
 
     # CPU: the reference's torch path restated (oracle/torch_port.py), full tensor.
     def cpu_sample(self, reps=None):
@@ -313,7 +314,8 @@ class AttentionWorkload:
                 "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4),
                 "algorithmic_flops_per_launch": self.flops,
-                "traffic": profile_traffic("fp4_attn_kernel_llama3-8b_T4096")}
+                "traffic": profile_traffic("fp4_attn_kernel_llama3-8b_T4096"),
+                "traffic_source": "profiles/fp4_attn_kernel_llama3-8b_T4096.md: ncu dram__bytes_read+write per launch"}
 
     def cpu_sample(self, reps=None):
         """The reference's CPU path (torch ops) on one KV-head group (4 of 32 query heads)."""

@@ -182,6 +182,8 @@ class QuantizeWorkload:
                       3 | 0x10, 0, 2688.0, self.codes[i].data_ptr(), self.n // 2, self.scales[i].data_ptr(), 0,
                       self.n // 16, self.g[i].data_ptr(), None, 0, 0, self.stream)
 
+    use_graph = True  # ~25 us steps: timed as CUDA graph replays
+
     def step(self, i, ev=None):
         i %= self.nsets
         self._global(i)
@@ -190,6 +192,9 @@ class QuantizeWorkload:
         self._rows(i)
         if ev is not None:
             ev[1].record()
+
+    def kernel(self, i):
+        self._rows(i % self.nsets)
 
     def e2e_step(self, i):
         """Public API, host buffers: H2D input, quantize, D2H codes + scales."""
@@ -375,17 +380,59 @@ def run_ours(args, world, rank, local):
     # device-resident timed region: whole steps, plus the dominant kernel alone
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    n0 = _lib.launch_count()
-    with Clocks(dev) as clk:
-        start.record()
-        for i in range(K):
-            wl.step(W + i, kev[i])
-        end.record()
+    if getattr(wl, "use_graph", False):
+        # short steps: each step replays a CUDA graph of its launches, so host-side
+        # launch cost does not starve the GPU; the dominant kernel is timed from its
+        # own graph replays right after the timed region
+        stream = torch.cuda.Stream(dev)
+        wl.stream = stream.cuda_stream
+        graphs, kgraphs = [], []
+        with torch.cuda.stream(stream):
+            for i in range(wl.nsets):
+                wl.step(i)
+            torch.cuda.synchronize(dev)
+            c0 = _lib.launch_count()
+            for i in range(wl.nsets):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    wl.step(i)
+                graphs.append(g)
+            per_step = (_lib.launch_count() - c0) // wl.nsets
+            for i in range(wl.nsets):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    wl.kernel(i)
+                kgraphs.append(g)
+            for i in range(wl.nsets):
+                graphs[i].replay()
+            torch.cuda.synchronize(dev)
+            barrier(world)
+            torch.cuda.synchronize(dev)
+            with Clocks(dev) as clk:
+                start.record()
+                for i in range(K):
+                    graphs[(W + i) % wl.nsets].replay()
+                end.record()
+                torch.cuda.synchronize(dev)
+            launches = per_step * K
+            for i in range(K):
+                kev[i][0].record()
+                kgraphs[(W + i) % wl.nsets].replay()
+                kev[i][1].record()
+            torch.cuda.synchronize(dev)
+        barrier(world)
+    else:
+        barrier(world)
         torch.cuda.synchronize(dev)
-    launches = _lib.launch_count() - n0
-    barrier(world)
+        n0 = _lib.launch_count()
+        with Clocks(dev) as clk:
+            start.record()
+            for i in range(K):
+                wl.step(W + i, kev[i])
+            end.record()
+            torch.cuda.synchronize(dev)
+        launches = _lib.launch_count() - n0
+        barrier(world)
     ms = start.elapsed_time(end)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / K
     ms_max = max_over_ranks(ms, world, dev)
@@ -417,7 +464,8 @@ def run_ours(args, world, rank, local):
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic (seeded; shapes/distributions of the named configuration)",
-        "config": dict(wl.config, parallelism=f"{world} independent shard(s), no data-path collective"),
+        "config": dict(wl.config, parallelism=f"{world} independent shard(s), no data-path collective",
+                       timing="CUDA graph replay per step" if getattr(wl, "use_graph", False) else "stream launches"),
         "roofline": wl.kernel_roofline(kernel_ms_max / 1e3, peaks, peak_src),
         "cpu_baseline": cpu,
         "e2e": {"value": round(wl.value(e2e_ms / 1e3 / K, world), 3), "unit": wl.unit,

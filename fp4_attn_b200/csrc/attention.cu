@@ -355,6 +355,33 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     const int col0 = 32 * q;
     uint32_t kc = 0, uc = 0, pt = 0;
     uint32_t sfu0 = 0, sfu1 = 0;  // completions seen per S buffer
+    // ---- epilogue of a finished unit: O rows / l, columns 32q .. 32q+31, then O is free
+    bool pend = false;
+    uint32_t pend_uc = 0;
+    float pend_rl = 0.0f;
+    int64_t pend_off = -1;  // element offset of this thread's 32 outputs, -1 for rows past T
+    auto epilogue = [&]() {
+      mbar_wait(o_full, pend_uc & 1, 0x224);
+      if (threadIdx.x == 128) tr(pend_uc, TR_OFULL, 0);
+      tc_fence_after();
+      uint32_t a[32];
+      tmem_ld32(tmem + lane_base + T_O + col0, a);
+      tmem_ld_wait();
+      if (pend_off >= 0) {
+        float4* d4 = reinterpret_cast<float4*>(p.out + pend_off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          d4[i] = make_float4(__uint_as_float(a[4 * i]) * pend_rl, __uint_as_float(a[4 * i + 1]) * pend_rl,
+                              __uint_as_float(a[4 * i + 2]) * pend_rl, __uint_as_float(a[4 * i + 3]) * pend_rl);
+      }
+      tc_fence_before();
+      named_bar(1 + NWG, NWG * 128);
+      if (threadIdx.x == 128) {
+        mbar_arrive(o_free);
+        tr(pend_uc, TR_OFREE, 0);
+      }
+      pend = false;
+    };
     for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
       const Unit un = unit_of(u, p);
       const int n = kv_tiles(un, p);
@@ -390,6 +417,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       named_bar(1 + NWG, NWG * 128);
 #pragma unroll
       for (int w = 0; w < NWG; ++w) m = fmaxf(m, stat_m[w * 128 + r]);
+      // the previous unit's last PV has long finished: write its O now, which
+      // also frees the accumulator for this unit's first PV
+      if (pend) epilogue();
       const float mu = m == -INFINITY ? 0.0f : m * uscale;
       const uint64_t u2 = pk2(uscale, uscale), nmu2 = pk2(-mu, -mu);
       // ---- pass 2: e = exp2(z*u - m*u), sum, NVFP4 fake-quant of e -> P quarter q
@@ -437,28 +467,13 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       float l = 0.0f;
 #pragma unroll
       for (int w = 0; w < NWG; ++w) l += stat_l[w * 128 + r];
-      // ---- epilogue: O rows / l, columns 32q .. 32q+31
-      mbar_wait(o_full, uc & 1, 0x224);
-      if (threadIdx.x == 128) tr(uc, TR_OFULL, 0);
-      tc_fence_after();
-      const float rl = 1.0f / l;
-      uint32_t a[32];
-      tmem_ld32(tmem + lane_base + T_O + col0, a);
-      tmem_ld_wait();
-      if (qpos < p.T) {
-        float4* d4 = reinterpret_cast<float4*>(p.out + (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + col0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          d4[i] = make_float4(__uint_as_float(a[4 * i]) * rl, __uint_as_float(a[4 * i + 1]) * rl,
-                              __uint_as_float(a[4 * i + 2]) * rl, __uint_as_float(a[4 * i + 3]) * rl);
-      }
-      tc_fence_before();
-      named_bar(1 + NWG, NWG * 128);
-      if (threadIdx.x == 128) {
-        mbar_arrive(o_free);
-        tr(uc, TR_OFREE, 0);
-      }
+      // this unit's O is written after the next unit's pass 1 (or after the last unit)
+      pend = true;
+      pend_uc = uc;
+      pend_rl = 1.0f / l;
+      pend_off = qpos < p.T ? (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + col0 : -1;
     }
+    if (pend) epilogue();
   }
   tc_fence_before();
   __syncthreads();

@@ -67,3 +67,52 @@ def nvf4_to_f16(Xout: torch.Tensor, XQin: torch.Tensor, XSin: torch.Tensor) -> N
     """codes + scales -> float16 [M,16]."""
     M = _check_io(XQin, XSin, Xout, torch.float16, "Xout")
     _lib.call("nvfp4sim_nvf4_to_f16", Xout.data_ptr(), XQin.data_ptr(), XSin.data_ptr(), M, _lib.stream_of(Xout))
+
+
+# ---------------------------------------------------------------------------
+# Exports added next to the five reference functions: the packed quantizer,
+# its inverse, the fused round trip and the FP4 attention forward.  They have
+# no counterpart in the reference's extension (wrapper.cpp:40-46); they are
+# the calls its Python layer makes through torch ops today
+# (fp4_quant_utils.py:112-172, llama_patch.py:57-105 and 167-196).
+
+def quantize_nvfp4(x: torch.Tensor, mode: str = "row", global_sf_max: float | None = 1536.0, search: bool = False,
+                   scale_layout: str = "linear", dequant_dtype: torch.dtype = torch.float32):
+    """x [m, n] (CUDA) -> (codes uint8 [m, npad/2], scales E4M3 bytes, g fp32 or None)."""
+    from . import quant
+    if search:
+        raise NotImplementedError("the scale search packs through f32_to_nvf4 ([M,16] groups), not quantize_nvfp4")
+    t = quant.quantize(x, mode, global_sf_max, dequant_dtype, scale_layout)
+    return t.codes, t.scales, t.g
+
+
+def dequantize_nvfp4(codes: torch.Tensor, scales: torch.Tensor, g: torch.Tensor | None, shape, mode: str = "row",
+                     out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Inverse of quantize_nvfp4 (linear scale layout): code * scale * g."""
+    from . import quant
+    t = quant.NVFP4Tensor(codes, scales, g, tuple(shape), mode if g is not None else "none", "linear")
+    return quant.dequantize(t, out_dtype)
+
+
+def qdq_nvfp4(x: torch.Tensor, mode: str = "row", global_sf_max: float | None = 1536.0,
+              dequant_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """single_nvfp4_quant_dequant_fused (fp4_quant_utils.py:112-172) on the GPU, bit for bit."""
+    from . import quant
+    return quant.qdq(x, mode, global_sf_max, dequant_dtype)
+
+
+def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+                      scaling: float | None = None, dual_q: bool = False, dual_p: bool = False,
+                      v_scale_mode: str = "token") -> torch.Tensor:
+    """Q/K/V fake-quant + FP4 attention (llama_patch.py:57-105, 167-196): [B,Hq,T,D] -> fp32 [B,T,Hq,D].
+
+    dual_q / dual_p (residual two-slice quantization) and V scales other than
+    per token (the reference's global_scale_aligned=False) are not
+    implemented by the kernel and raise.
+    """
+    from .attention import fp4_attention_fwd as fwd
+    if dual_q or dual_p:
+        raise NotImplementedError("dual-slice Q/P quantization is not implemented by the FP4 attention kernel")
+    if v_scale_mode != "token":
+        raise NotImplementedError("V is quantized along tokens with a per-token global scale only")
+    return fwd(q, k, v, causal=causal, scaling=scaling)

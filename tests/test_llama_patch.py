@@ -68,3 +68,16 @@ def test_mask_check():
         lp._check_mask(padded, T, T)
     with pytest.raises(ValueError):
         lp._check_mask(causal[..., :4, :], T, T)
+
+
+def test_nvfp4sim_new_exports_refuse_unimplemented_modes():
+    from fp4_attn_b200 import nvfp4sim
+    for name in ("quantize_nvfp4", "dequantize_nvfp4", "qdq_nvfp4", "fp4_attention_fwd"):
+        assert callable(getattr(nvfp4sim, name))
+    q = torch.randn(1, 2, 16, 128)
+    with pytest.raises(NotImplementedError):
+        nvfp4sim.fp4_attention_fwd(q, q[:, :1], q[:, :1], dual_p=True)
+    with pytest.raises(NotImplementedError):
+        nvfp4sim.fp4_attention_fwd(q, q[:, :1], q[:, :1], v_scale_mode="channel")
+    with pytest.raises(NotImplementedError):
+        nvfp4sim.quantize_nvfp4(torch.randn(4, 16), search=True)

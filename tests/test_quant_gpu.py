@@ -239,3 +239,18 @@ def test_errors_are_raised_not_aborted(dev):
         nvfp4sim.f32_to_nvf4(q, s, x)
     with pytest.raises(RuntimeError, match="CUDA"):
         nvfp4sim.f32_to_nvf4(q.cpu(), s, x)
+
+
+def test_nvfp4sim_packed_exports(dev):
+    """quantize_nvfp4 / dequantize_nvfp4 / qdq_nvfp4 agree with the C oracle and with each other."""
+    from fp4_attn_b200 import nvfp4sim
+    for name, x in CASES[:6]:
+        xt = torch.from_numpy(x).bfloat16()
+        ref_out, ref_codes, ref_scales, ref_g = oq.fused_qdq(xt.float().numpy(), "row", "float32", 1536.0)
+        codes, scales, g = nvfp4sim.quantize_nvfp4(xt.to(dev), "row", 1536.0)
+        np.testing.assert_array_equal(codes.cpu().numpy(), ref_codes, err_msg=name)
+        np.testing.assert_array_equal(scales.cpu().numpy(), ref_scales, err_msg=name)
+        y = nvfp4sim.qdq_nvfp4(xt.to(dev), "row", 1536.0)
+        np.testing.assert_array_equal(canon(y.cpu().numpy()), canon(ref_out), err_msg=name)
+        d = nvfp4sim.dequantize_nvfp4(codes, scales, g, xt.shape, "row")
+        np.testing.assert_array_equal(canon(d.cpu().numpy()), canon(ref_out), err_msg=name)

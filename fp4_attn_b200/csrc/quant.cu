@@ -49,6 +49,16 @@ static int quantize_entry(const void* x, int in_dtype, int B, int T, int H, int 
                        ((sH * esz) % 16 == 0 || H == 1) && ((D * esz) % 16 == 0 || H == 1);
   p.vec = aligned ? 1 : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Per-tensor mode on a contiguous tensor that fits on chip: one pass over HBM.
+  if (what == 0 && gmode == 3 && arith == FP4_ARITH_F32 && !out && codes && scales && scale_layout == 0 &&
+      p.vec && T_pad == T) {
+    const int64_t n = (int64_t)H * D;
+    const bool flat = (H == 1 || sH == D) && sT == n && (B == 1 || sB == (int64_t)T * n);
+    if (flat && n % 16 == 0 && codes_ld == n / 2 && scales_ld == n / 16) {
+      const int r = quant_tensor_fused(x, in_dtype, (int64_t)B * T * n, codes, scales, g, global_sf_max, st);
+      if (r >= 0) return r;
+    }
+  }
   switch (in_dtype) {
     case FP4_DT_F32: return quant_dispatch_f32(p, arith, out_dtype, g, global_sf_max, what, st);
     case FP4_DT_BF16: return quant_dispatch_bf16(p, arith, out_dtype, g, global_sf_max, what, st);

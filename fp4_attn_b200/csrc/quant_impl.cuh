@@ -647,6 +647,11 @@ static int dispatch_arith(const QuantArgs& p, int arith, int out_dtype, float* g
   return set_error(FP4ATTN_ERR_ARG, "bad arith");
 }
 
+// Single-pass per-tensor quantize (quant_fused.cu); -1 when not applicable.
+int quant_tensor_fused(const void* x, int in_dtype, int64_t nelem, uint8_t* codes, uint8_t* scales, float* g,
+                       float gsf_max, cudaStream_t st);
+unsigned int quant_status(bool reset);
+
 // One instantiation set per input dtype (quant_f32.cu, quant_bf16.cu, quant_f16.cu).
 int quant_dispatch_f32(const QuantArgs& p, int arith, int out_dtype, float* g, float gsf_max, int what, cudaStream_t st);
 int quant_dispatch_bf16(const QuantArgs& p, int arith, int out_dtype, float* g, float gsf_max, int what, cudaStream_t st);

@@ -38,10 +38,12 @@ extern "C" int fp4attn_version(void) { return 1; }
 // Synchronizes with the device (reads device symbols).  Non-zero means a
 // bounded wait inside a kernel gave up: (site << 16) | (CTA index + 1).
 extern "C" unsigned int fp4attn_device_status(int reset) {
-  unsigned int v = fp4::gemm_status(reset != 0);
-  if (!v) v = fp4::attn_status(reset != 0);
-  else fp4::attn_status(reset != 0);
-  return v;
+  // first non-zero status of the kernels with bounded waits; every word is read (and reset if asked)
+  const unsigned int s[3] = {fp4::gemm_status(reset != 0), fp4::attn_status(reset != 0),
+                             fp4::quant_status(reset != 0)};
+  for (unsigned int v : s)
+    if (v) return v;
+  return 0;
 }
 
 extern "C" unsigned long long fp4attn_launch_count(void) { return __atomic_load_n(&fp4::g_launches, __ATOMIC_RELAXED); }

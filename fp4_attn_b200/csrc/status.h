@@ -19,4 +19,5 @@ void count_launch();
 // Device status words of the translation units with bounded waits.
 unsigned int gemm_status(bool reset);
 unsigned int attn_status(bool reset);
+unsigned int quant_status(bool reset);
 }  // namespace fp4

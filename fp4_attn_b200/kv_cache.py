@@ -1,0 +1,104 @@
+"""NVFP4 KV cache and decode attention (one new query token per sequence).
+
+The reference's patched attention quantizes each call's new Q/K/V on their
+2-D views (llama_patch.py:167-196: Q and K row mode on [B*q, H*D], V column
+mode on the [Hkv*D, B*q] view), appends the dequantized K/V to the HF cache
+(llama_patch.py:212-215) and attends over every cached key with P fake-quant
+(llama_patch.py:57-105).  ``NVFP4KVCache`` keeps the packed NVFP4 data of
+those same values -- codes, E4M3 scales and global scales -- and
+``decode_attention`` runs the FP4 attention of a single new token over it on
+the GPU (``fp4attn_decode`` in the C ABI).  As in the prefill path, Q and K
+are taken after RoPE.
+
+Layout (device tensors):
+  k_codes  uint8 [B, Hkv, Tmax, D/2]   E2M1 pairs, element 2k in the low nibble
+  k_scales uint8 [B, Hkv, Tmax, D/16]  E4M3 block scales along head_dim
+  k_g      fp32  [B, Tmax]             per-token global scale (row max)
+  v_codes  uint8 [B, Hkv, Tmax, D/2]
+  v_scales uint8 [B, Hkv, Tmax, D]     one E4M3 scale per element: a V block of
+                                       16 runs along the tokens of the call
+                                       that appended it
+  v_g      fp32  [B, Tmax]             per-token global scale (column max / 1536)
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib, quant
+
+HEAD_DIM = 128
+
+
+class NVFP4KVCache:
+    def __init__(self, B: int, Hkv: int, Tmax: int, D: int, device):
+        if D != HEAD_DIM:
+            raise NotImplementedError(f"head_dim {D}: the decode kernel implements {HEAD_DIM}")
+        self.B, self.Hkv, self.Tmax, self.D = B, Hkv, Tmax, D
+        u8 = torch.uint8
+        self.k_codes = torch.zeros(B, Hkv, Tmax, D // 2, dtype=u8, device=device)
+        self.k_scales = torch.zeros(B, Hkv, Tmax, D // 16, dtype=u8, device=device)
+        self.k_g = torch.zeros(B, Tmax, dtype=torch.float32, device=device)
+        self.v_codes = torch.zeros(B, Hkv, Tmax, D // 2, dtype=u8, device=device)
+        self.v_scales = torch.zeros(B, Hkv, Tmax, D, dtype=u8, device=device)
+        self.v_g = torch.zeros(B, Tmax, dtype=torch.float32, device=device)
+        self.len = 0
+
+    def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Quantize q new tokens k, v [B, Hkv, q, D] (post-RoPE K) as one call of the reference does, and store them."""
+        _lib.require_cuda(k, v)
+        B, H, q, D = k.shape
+        if (B, H, D) != (self.B, self.Hkv, self.D) or v.shape != k.shape:
+            raise ValueError("k/v must be [B, Hkv, q, D] matching the cache")
+        if self.len + q > self.Tmax:
+            raise ValueError(f"cache holds {self.Tmax} tokens")
+        t0, t1 = self.len, self.len + q
+        # K: row mode on the [B*q, Hkv*D] view (llama_patch.py:167,194)
+        k2d = k.permute(0, 2, 1, 3).reshape(B * q, H * D)
+        pk = quant.quantize(k2d, "row", 1536.0)
+        self.k_codes[:, :, t0:t1] = pk.codes.view(B, q, H, D // 2).permute(0, 2, 1, 3)
+        self.k_scales[:, :, t0:t1] = pk.scales.view(B, q, H, D // 16).permute(0, 2, 1, 3)
+        self.k_g[:, t0:t1] = pk.g.view(B, q)
+        # V: column mode on the [Hkv*D, B*q] view, blocks of 16 along the call's tokens (llama_patch.py:196)
+        v2dT = v.permute(1, 3, 0, 2).reshape(H * D, B * q).contiguous()
+        pv = quant.quantize(v2dT, "col", 1536.0)
+        n = B * q
+        npad = (n + 15) // 16 * 16
+        lo, hi = pv.codes & 15, pv.codes >> 4
+        nib = torch.stack((lo, hi), dim=-1).reshape(H * D, npad)[:, :n]  # [H*D, B*q]
+        sc = pv.scales.repeat_interleave(16, dim=1)[:, :n]  # [H*D, B*q]
+        nib = nib.view(H, D, B, q).permute(2, 0, 3, 1)  # [B, H, q, D]
+        sc = sc.view(H, D, B, q).permute(2, 0, 3, 1)
+        packed = (nib[..., 0::2] | (nib[..., 1::2] << 4)).to(torch.uint8)
+        self.v_codes[:, :, t0:t1] = packed
+        self.v_scales[:, :, t0:t1] = sc
+        self.v_g[:, t0:t1] = pv.g[:n].view(B, q)
+        self.len = t1
+
+
+def decode_attention(q: torch.Tensor, cache: NVFP4KVCache, scaling: float | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """FP4 attention of one new token q [B, Hq, 1, D] (post-RoPE) over the cache -> fp32 [B, 1, Hq, D].
+
+    q is fake-quantized like the reference's Q (row mode on the [B, Hq*D] view);
+    the newest token is assumed to be in the cache already (append first).
+    """
+    _lib.require_cuda(q)
+    B, Hq, one, D = q.shape
+    if one != 1:
+        raise NotImplementedError("decode_attention takes one query token per sequence")
+    if B != cache.B or D != cache.D or Hq % cache.Hkv:
+        raise ValueError("q [B, Hq, 1, D] must match the cache")
+    if cache.len == 0:
+        raise ValueError("empty cache")
+    if scaling is None:
+        scaling = D ** -0.5
+    qhat = quant.qdq(q.reshape(B, Hq * D), "row", 1536.0, torch.float32).view(B, Hq, D).contiguous()
+    need = _lib.load().fp4attn_decode_workspace_size(B, Hq, cache.len)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    out = torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
+    _lib.call("fp4attn_decode", qhat.data_ptr(), cache.k_codes.data_ptr(), cache.k_scales.data_ptr(),
+              cache.k_g.data_ptr(), cache.v_codes.data_ptr(), cache.v_scales.data_ptr(), cache.v_g.data_ptr(),
+              B, Hq, cache.Hkv, D, cache.len, cache.Tmax, float(scaling), out.data_ptr(), workspace.data_ptr(),
+              workspace.numel() * workspace.element_size(), _lib.stream_of(q))
+    return out.view(B, 1, Hq, D)

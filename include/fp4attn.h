@@ -185,6 +185,26 @@ int fp4attn_forward_noalloc(const void* q, const void* k, const void* v, int in_
                             int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling, float* out,
                             void* stream);
 
+/* ------------------------------------------------------------------------
+ * Decode: one new query token per sequence over an NVFP4 KV cache.  The
+ * reference appends each call's fake-quantized K/V to the HF cache
+ * (llama_patch.py:167-215) and attends over every cached key with P
+ * fake-quant (llama_patch.py:57-105); the cache here holds the packed data
+ * of those values (fp4_attn_b200.kv_cache.NVFP4KVCache):
+ *   k_codes [B][Hkv][Tmax][D/2], k_scales E4M3 [B][Hkv][Tmax][D/16],
+ *   k_g [B][Tmax] (per-token row-mode global scale);
+ *   v_codes [B][Hkv][Tmax][D/2], v_scales E4M3 [B][Hkv][Tmax][D] (one per
+ *   element: V's blocks run along the tokens of the call that appended them),
+ *   v_g [B][Tmax].
+ * qhat is the fake-quantized query, fp32 [B][Hq][D]; out fp32 [B][Hq][D];
+ * len cached tokens are attended (no mask: the query is the newest token).
+ * D = 128, Hq/Hkv <= 16.  workspace: fp4attn_decode_workspace_size bytes. */
+int64_t fp4attn_decode_workspace_size(int B, int Hq, int len);
+int fp4attn_decode(const float* qhat, const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                   const uint8_t* v_codes, const uint8_t* v_scales, const float* v_g, int B, int Hq, int Hkv, int D,
+                   int len, int Tmax, float scaling, float* out, void* workspace, int64_t workspace_bytes,
+                   void* stream);
+
 /* Profiling aid: a non-NULL buf makes later fp4attn_fwd_packed calls record
  * an event timeline (SM clock cycles from clock64) of each CTA's first work unit into
  * buf[cta * 512 + slot] (grid * 512 int64 entries); NULL turns it off. */

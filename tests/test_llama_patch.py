@@ -81,3 +81,15 @@ def test_nvfp4sim_new_exports_refuse_unimplemented_modes():
         nvfp4sim.fp4_attention_fwd(q, q[:, :1], q[:, :1], v_scale_mode="channel")
     with pytest.raises(NotImplementedError):
         nvfp4sim.quantize_nvfp4(torch.randn(4, 16), search=True)
+
+
+def test_kv_cache_host_checks():
+    from fp4_attn_b200 import kv_cache
+    with pytest.raises(NotImplementedError):
+        kv_cache.NVFP4KVCache(1, 1, 16, 64, "cpu")
+    c = kv_cache.NVFP4KVCache(1, 2, 16, 128, "cpu")
+    k = torch.randn(1, 2, 4, 128)
+    with pytest.raises(RuntimeError, match="CUDA"):  # no CPU path
+        c.append(k, k)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kv_cache.decode_attention(torch.randn(1, 4, 1, 128), c)

@@ -10,28 +10,72 @@
 //   V: codes [B][Hkv][Tmax][D/2], one E4M3 scale byte per element
 //      [B][Hkv][Tmax][D] (V's blocks of 16 run along the tokens of the call that
 //      appended them, so a token's scale is per channel), per-token g_v [B][Tmax].
-// The query is passed already fake-quantized (Q-hat, fp32 [B][Hq][D]).
+// Tmax is a multiple of 256, so every chunk of 256 keys is whole in memory.
+// The query comes in the same packed form (row mode on its [B, Hq*D] view):
+// codes [B][Hq*D/2], E4M3 scales [B][Hq*D/16], g_q [B].
 //
-// Three kernels, all HBM-bound: scores S = Q-hat K-hat^T * scaling per split of
-// keys (with the split's row maxima); then the exact row max, e =
-// exp2((S - m) log2 e), the NVFP4 fake-quant of e per 16 keys (as the prefill
-// kernel does) and O-partial = P-hat V-hat on CUDA cores; then the combine
-// O = sum O-partial / sum l.
+// Work item = (chunk of 256 keys, b, KV head).  Three kernels, HBM-bound:
+//  * scores: persistent CTAs stream their items' K through a ring of shared
+//    memory stages (one producer warp, bulk copies, mbarriers); eight warps
+//    compute S = (code*scale)_q . (code*scale)_k * g_q * g_k * scaling on
+//    mma.sync m16n8k16 (fp16 products exact, fp32 accumulate; the query heads
+//    of the KV head are the MMA rows, 8 keys its columns), write S and fold
+//    each row's maximum into an order-free atomic maximum;
+//  * pv: the same ring over V and S; the exact row max, e = exp2((S - m)
+//    log2 e), the NVFP4 fake-quant of e per 16 keys (as the prefill kernel
+//    does), then O-partial = (P-hat * g_v) (code*scale)_v on CUDA cores with
+//    packed fp32x2 FMAs (V's per-token g_v is not exact in fp16);
+//  * combine: O = sum O-partial / sum l over the chunks, in a fixed order.
 #include <stdint.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "fp4attn.h"
+#include "sm100.cuh"
 #include "status.h"
 
 namespace fp4 {
+
+FP4_DEFINE_STATUS_READER(decode_status)
+
 namespace {
 
-constexpr int DK_KEYS = 256;     // keys per split (one per thread in the score kernel)
-constexpr int DK_MAXG = 16;      // query heads per KV head
-constexpr int DK_D = 128;        // head dim
+constexpr int DK_KEYS = 256;  // keys per work item
+constexpr int DK_MAXG = 16;   // query heads per KV head
+constexpr int DK_D = 128;     // head dim
+constexpr int DK_WARPS = 8;   // consumer warps (plus one producer warp)
+constexpr int DK_THREADS = (DK_WARPS + 1) * 32;
+
+// scores stage: K codes | K scales | g_k
+constexpr uint32_t SC_KC = DK_KEYS * DK_D / 2;
+constexpr uint32_t SC_KS = DK_KEYS * DK_D / 16;
+constexpr uint32_t SC_KG = DK_KEYS * 4;
+constexpr uint32_t SC_STAGE = SC_KC + SC_KS + SC_KG;
+constexpr int SC_STAGES = 3;
+// pv stage: V codes | V scales | g_v | S of the G heads
+constexpr uint32_t PV_VC = DK_KEYS * DK_D / 2;
+constexpr uint32_t PV_VS = DK_KEYS * DK_D;
+constexpr uint32_t PV_VG = DK_KEYS * 4;
+constexpr uint32_t PV_S1 = DK_KEYS * 4;  // S of one head
+// MG bounds the query heads per KV head; AG heads are accumulated at a time.
+// Dynamic shared memory: the ring, then P-hat * g_v [MG][DK_KEYS], then the
+// cross-warp partial sums [4][AG][DK_D].
+template <int MG>
+struct PvCfg {
+  static constexpr int AG = MG < 8 ? MG : 8;
+  static constexpr int STAGES = MG <= 8 ? 3 : 2;
+  static constexpr uint32_t STAGE = PV_VC + PV_VS + PV_VG + MG * PV_S1;
+  static constexpr uint32_t RING = STAGES * STAGE;
+  static constexpr uint32_t PH = MG * DK_KEYS * 4;
+  static constexpr uint32_t PART = 4 * AG * DK_D * 4;
+  static constexpr uint32_t SMEM = RING + PH + PART;
+};
 
 struct DecodeArgs {
-  const float* qhat;  // [B][Hq][D]
+  const uint8_t* q_codes;   // [B][Hq*D/2]
+  const uint8_t* q_scales;  // [B][Hq*D/16]
+  const float* q_g;         // [B]
   const uint8_t* k_codes;
   const uint8_t* k_scales;
   const float* k_g;
@@ -40,145 +84,410 @@ struct DecodeArgs {
   const float* v_g;
   int B, Hq, Hkv, len, Tmax, nsplit;
   float scaling;
-  float* S;      // [B][Hq][nsplit*DK_KEYS]
-  float* pmax;   // [B][Hq][nsplit]
-  float* opart;  // [B][Hq][nsplit][D]
-  float* lpart;  // [B][Hq][nsplit]
-  float* out;    // [B][Hq][D]
+  float* S;            // [B*Hq][nsplit*DK_KEYS]
+  float* opart;        // [B*Hq][nsplit][D]
+  float* lpart;        // [B*Hq][nsplit]
+  unsigned int* mrow;  // [B*Hq] row maximum of S (float bits, atomic; 0xFFFFFFFF = none yet)
+  float* out;          // [B][Hq][D]
 };
 
-__global__ void __launch_bounds__(DK_KEYS) decode_scores_kernel(DecodeArgs p) {
-  const int split = blockIdx.x, bk = blockIdx.y;
-  const int b = bk / p.Hkv, hk = bk % p.Hkv;
-  const int G = p.Hq / p.Hkv;
-  __shared__ float q_s[DK_MAXG][DK_D];
-  __shared__ float red[DK_KEYS / 32][DK_MAXG];
-  for (int i = threadIdx.x; i < G * DK_D; i += DK_KEYS)
-    q_s[i / DK_D][i % DK_D] = p.qhat[((int64_t)b * p.Hq + hk * G + i / DK_D) * DK_D + i % DK_D];
+__device__ __forceinline__ uint32_t cvt_e2m1x2_f16x2(uint32_t byte) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(r) : "r"(byte));
+  return r;
+}
+__device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint32_t two_bytes) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(two_bytes));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+// acc += {a, a} * {x, y}, one packed fp32x2 FMA (two IEEE fp32 FMAs)
+__device__ __forceinline__ void fma2(float& acc0, float& acc1, float a, float x, float y) {
+  unsigned long long A, X, C;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a), "f"(a));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(X) : "f"(x), "f"(y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(C) : "f"(acc0), "f"(acc1));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(C) : "l"(A), "l"(X));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(acc0), "=f"(acc1) : "l"(C));
+}
+// order-preserving float maximum on the bit pattern (exact, order-free)
+__device__ __forceinline__ void atomic_max_f32(unsigned int* a, float v) {
+  if (!(v < 0.0f)) atomicMax(reinterpret_cast<int*>(a), __float_as_int(v));
+  else atomicMin(a, __float_as_uint(v));
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"r"(DK_WARPS * 32) : "memory"); }
+// consumers_sync that also ANDs a flag over the consumer threads (every warp sees the same answer)
+__device__ __forceinline__ bool consumers_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "r"(DK_WARPS * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Wait for a bulk copy to land before the CTA exits, whatever the failure flag says (bounded).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > kWaitNs) return;
+}
+
+__device__ __forceinline__ void item_range(int n, int& i0, int& i1) {
+  i0 = (int)((int64_t)blockIdx.x * n / gridDim.x);
+  i1 = (int)((int64_t)(blockIdx.x + 1) * n / gridDim.x);
+}
+
+// The producer lane of a ring: item it of this CTA goes to stage it % NS once
+// the consumers released that stage's previous item; load(item, stage, bar)
+// issues the bulk copies.  Before returning it waits (bounded) for the copies
+// of the last items it issued, so none is in flight when the CTA exits.
+template <int NS, typename Load>
+__device__ __forceinline__ void produce(uint64_t* full, uint64_t* empty, uint8_t* ring, uint32_t stage_bytes,
+                                        int i0, int i1, unsigned int site, Load load) {
+  int issued = 0;
+  for (int it = 0; it < i1 - i0; ++it) {
+    const int s = it % NS;
+    if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, site)) break;
+    load(i0 + it, ring + (size_t)s * stage_bytes, &full[s]);
+    issued = it + 1;
+  }
+  for (int it = issued > NS ? issued - NS : 0; it < issued; ++it) mbar_drain(&full[it % NS], (it / NS) & 1);
+}
+
+// ---------------------------------------------------------------- scores
+// Lane (r, q) of a warp: key r of the warp's group of 8; the MMA's K index
+// is permuted so that lane q's B values for chunk c (k = 2q, 2q+1, 2q+8,
+// 2q+9) are dims 32q + 4c + 0..3: its code bytes of a key are one contiguous
+// run (bytes 16q..16q+15) and its scales two bytes (2q, 2q+1).  The A
+// fragment uses the same permutation, so the dot product is unchanged.
+__global__ void __launch_bounds__(DK_THREADS) decode_scores_kernel(DecodeArgs p) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ __align__(8) uint64_t full[SC_STAGES], empty[SC_STAGES];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int i0, i1;
+  item_range(p.nsplit * p.B * p.Hkv, i0, i1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SC_STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], DK_WARPS);
+    fence_barrier_init();
+  }
   __syncthreads();
-  const int k = split * DK_KEYS + threadIdx.x;
-  float acc[DK_MAXG];
+  if (warp == DK_WARPS) {
+    if (lane == 0)
+      produce<SC_STAGES>(full, empty, ring, SC_STAGE, i0, i1, 0x401, [&](int item, uint8_t* st, uint64_t* bar) {
+        const int bk = item / p.nsplit, split = item % p.nsplit, b = bk / p.Hkv;
+        const int64_t row = (int64_t)bk * p.Tmax + (int64_t)split * DK_KEYS;
+        mbar_arrive_expect_tx(bar, SC_STAGE);
+        bulk_load(st, p.k_codes + row * (DK_D / 2), SC_KC, bar);
+        bulk_load(st + SC_KC, p.k_scales + row * (DK_D / 16), SC_KS, bar);
+        bulk_load(st + SC_KC + SC_KS, p.k_g + (int64_t)b * p.Tmax + (int64_t)split * DK_KEYS, SC_KG, bar);
+      });
+    return;
+  }
+  const int G = p.Hq / p.Hkv;
+  const int r = lane / 4, q = lane % 4;
+  const int ks = p.nsplit * DK_KEYS;
+  int cur = -1;
+  uint32_t afr[DK_D / 16][4];
+  float gq = 0.0f;
+  float mx[2] = {-INFINITY, -INFINITY};  // rows r, r+8
+  auto flush = [&](int bk) {
 #pragma unroll
-  for (int g = 0; g < DK_MAXG; ++g) acc[g] = 0.0f;
-  const bool live = k < p.len;
-  if (live) {
-    const int64_t row = ((int64_t)b * p.Hkv + hk) * p.Tmax + k;
-    const uint4* c4 = reinterpret_cast<const uint4*>(p.k_codes + row * (DK_D / 2));
-    const uint2 sc = *reinterpret_cast<const uint2*>(p.k_scales + row * (DK_D / 16));
-    const uint8_t* sb = reinterpret_cast<const uint8_t*>(&sc);
+    for (int i = 0; i < 2; ++i) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+    }
+    const int64_t bh0 = (int64_t)(bk / p.Hkv) * p.Hq + (bk % p.Hkv) * G;
+    if (q == 0) {
+      if (r < G) atomic_max_f32(&p.mrow[bh0 + r], mx[0]);
+      if (r + 8 < G) atomic_max_f32(&p.mrow[bh0 + r + 8], mx[1]);
+    }
+  };
+  for (int it = 0; it < i1 - i0; ++it) {
+    const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
+    const int b = bk / p.Hkv, hk = bk % p.Hkv;
+    if (bk != cur) {
+      if (cur >= 0) flush(cur);
+      cur = bk;
+      mx[0] = mx[1] = -INFINITY;
+      gq = p.q_g[b];
+      // A: rows r, r+8 (query heads); k = 2q,2q+1 -> dims 32q+4c+0,1; k = 2q+8,2q+9 -> dims 32q+4c+2,3
+      const int64_t qel = ((int64_t)b * p.Hq + hk * G) * DK_D;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {  // 32 dims per 16-byte word
-      const uint4 u = c4[w];
-      const uint32_t words[4] = {u.x, u.y, u.z, u.w};
+      for (int c = 0; c < DK_D / 16; ++c)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const int d = w * 32 + j * 8 + n;
-          const float kv = __fmul_rn(e2m1_value((words[j] >> (4 * n)) & 15u), e4m3_to_f32(sb[d / 16]));
-#pragma unroll
-          for (int g = 0; g < DK_MAXG; ++g)
-            if (g < G) acc[g] = __fmaf_rn(q_s[g][d], kv, acc[g]);
+        for (int i = 0; i < 4; ++i) {
+          const int row = r + (i & 1) * 8, dim = 32 * q + 4 * c + 2 * (i >> 1);
+          uint32_t v = 0;
+          if (row < G) {
+            const int64_t el = qel + row * DK_D + dim;
+            const uint32_t sb = p.q_scales[el / 16];
+            v = hmul2u(cvt_e2m1x2_f16x2(p.q_codes[el / 2]), cvt_e4m3x2_f16x2(sb | (sb << 8)));
+          }
+          afr[c][i] = v;
         }
+    }
+    const int s = it % SC_STAGES;
+    if (!mbar_wait(&full[s], (it / SC_STAGES) & 1, 0x402)) break;
+    const uint8_t* st = ring + (size_t)s * SC_STAGE;
+    const int64_t srow = ((int64_t)b * p.Hq + hk * G) * ks;
+#pragma unroll
+    for (int gi = 0; gi < DK_KEYS / 8 / DK_WARPS; ++gi) {
+      const int kl = (warp + gi * DK_WARPS) * 8;  // first key of the group (in the item)
+      const uint4 cw = *reinterpret_cast<const uint4*>(st + (kl + r) * (DK_D / 2) + 16 * q);
+      const uint32_t sw = *reinterpret_cast<const uint16_t*>(st + SC_KC + (kl + r) * (DK_D / 16) + 2 * q);
+      const float2 kg = *reinterpret_cast<const float2*>(st + SC_KC + SC_KS + (kl + 2 * q) * 4);
+      const uint32_t s0 = cvt_e4m3x2_f16x2((sw & 0xFFu) * 0x101u), s1 = cvt_e4m3x2_f16x2((sw >> 8) * 0x101u);
+      const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int c = 0; c < DK_D / 16; ++c) {
+        // dims 32q + 4c + 0..3 = bytes 2c, 2c+1 of the lane's run (block 2q + c/4)
+        const uint32_t w = words[c / 2] >> (16 * (c & 1));
+        const uint32_t sc = c < 4 ? s0 : s1;
+        mma16816(acc, afr[c], hmul2u(cvt_e2m1x2_f16x2(w & 0xFFu), sc),
+                 hmul2u(cvt_e2m1x2_f16x2((w >> 8) & 0xFFu), sc));
+      }
+      // acc: rows r (0,1) and r+8 (2,3); keys kl + 2q, +1
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = r + (i >> 1) * 8, key = split * DK_KEYS + kl + 2 * q + (i & 1);
+        if (row >= G) continue;
+        float sv = -INFINITY;
+        if (key < p.len) sv = __fmul_rn(__fmul_rn(__fmul_rn(acc[i], gq), (i & 1) ? kg.y : kg.x), p.scaling);
+        p.S[srow + (int64_t)row * ks + key] = sv;
+        mx[i >> 1] = fmaxf(mx[i >> 1], sv);
       }
     }
-    const float gk = p.k_g[(int64_t)b * p.Tmax + k];
-#pragma unroll
-    for (int g = 0; g < DK_MAXG; ++g) acc[g] = __fmul_rn(__fmul_rn(acc[g], gk), p.scaling);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
-  const int ks = p.nsplit * DK_KEYS;
-#pragma unroll
-  for (int g = 0; g < DK_MAXG; ++g) {
-    if (g >= G) break;
-    const float s = live ? acc[g] : -INFINITY;
-    p.S[((int64_t)b * p.Hq + hk * G + g) * ks + k] = s;
-    float m = s;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5][g] = m;
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    float m = -INFINITY;
-    for (int w = 0; w < DK_KEYS / 32; ++w) m = fmaxf(m, red[w][threadIdx.x]);
-    p.pmax[((int64_t)b * p.Hq + hk * G + threadIdx.x) * p.nsplit + split] = m;
-  }
+  if (cur >= 0) flush(cur);
 }
 
-// e = exp2((S - m) log2 e) for one key of every head of the group, the NVFP4
-// fake-quant of e per 16 keys (16 consecutive threads hold one block), then
-// O-partial = P-hat V-hat over the split's keys.
-__global__ void __launch_bounds__(DK_KEYS) decode_pv_kernel(DecodeArgs p) {
-  const int split = blockIdx.x, bk = blockIdx.y;
-  const int b = bk / p.Hkv, hk = bk % p.Hkv;
+// -------------------------------------------------------------------- pv
+// Phase e: thread t handles key t of the item.  Accumulation: thread (oct,
+// slot) sums dims 8*oct..+7 over keys 16*slot..+15, for AG heads at a time.
+template <int MG>
+__global__ void __launch_bounds__(DK_THREADS) decode_pv_kernel(DecodeArgs p) {
+  using C = PvCfg<MG>;
+  constexpr int AG = C::AG;
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES];
+  __shared__ float lred[DK_WARPS][MG];
+  float(*ph)[DK_KEYS] = reinterpret_cast<float(*)[DK_KEYS]>(ring + C::RING);           // P-hat * g_v
+  float(*part)[AG][DK_D] = reinterpret_cast<float(*)[AG][DK_D]>(ring + C::RING + C::PH);  // partial sums
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, t = threadIdx.x;
   const int G = p.Hq / p.Hkv;
-  __shared__ float ph[DK_MAXG][DK_KEYS];  // P-hat
-  __shared__ float lred[DK_KEYS / 32][DK_MAXG];
-  __shared__ float opart[2][DK_MAXG][DK_D];
-  const int ks = p.nsplit * DK_KEYS;
-  const int k = split * DK_KEYS + threadIdx.x;
+  int i0, i1;
+  item_range(p.nsplit * p.B * p.Hkv, i0, i1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], DK_WARPS);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == DK_WARPS) {
+    if (lane == 0)
+      produce<C::STAGES>(full, empty, ring, C::STAGE, i0, i1, 0x411, [&](int item, uint8_t* st, uint64_t* bar) {
+        const int bk = item / p.nsplit, split = item % p.nsplit, b = bk / p.Hkv, hk = bk % p.Hkv;
+        const int64_t row = (int64_t)bk * p.Tmax + (int64_t)split * DK_KEYS;
+        const int ks = p.nsplit * DK_KEYS;
+        mbar_arrive_expect_tx(bar, PV_VC + PV_VS + PV_VG + (uint32_t)G * PV_S1);
+        bulk_load(st, p.v_codes + row * (DK_D / 2), PV_VC, bar);
+        bulk_load(st + PV_VC, p.v_scales + row * DK_D, PV_VS, bar);
+        bulk_load(st + PV_VC + PV_VS, p.v_g + (int64_t)b * p.Tmax + (int64_t)split * DK_KEYS, PV_VG, bar);
+        for (int g = 0; g < G; ++g)
+          bulk_load(st + PV_VC + PV_VS + PV_VG + g * PV_S1,
+                    p.S + ((int64_t)b * p.Hq + hk * G + g) * ks + (int64_t)split * DK_KEYS, PV_S1, bar);
+      });
+    return;
+  }
   const float log2e = 1.4426950408889634f, r6 = __frcp_rn(6.0f);
-  for (int g = 0; g < G; ++g) {
-    const int h = hk * G + g;
-    float m = -INFINITY;
-    for (int s = 0; s < p.nsplit; ++s) m = fmaxf(m, p.pmax[((int64_t)b * p.Hq + h) * p.nsplit + s]);
-    const float sv = p.S[((int64_t)b * p.Hq + h) * ks + k];
-    const float e = (k < p.len && m != -INFINITY) ? exp2f(__fmul_rn(sv - m, log2e)) : 0.0f;
-    // block of 16 keys = 16 consecutive lanes
-    float am = e;
+  const int oct = t % 16, slot = t / 16;
+  int cur = -1;
+  float m[MG];
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const uint8_t sb = e4m3_satfinite(__fmul_rn(am, r6));
-    const float s = e4m3_to_f32(sb);
-    const float rs = s == 0.0f ? 0.0f : __frcp_rn(s);
-    const uint32_t byte = e2m1x2(__fmaf_rn(e, rs, 0.0f), 0.0f);
-    ph[g][threadIdx.x] = __fmul_rn(e2m1_value(byte & 15u), s);
-    float l = e;
+  for (int g = 0; g < MG; ++g) m[g] = 0.0f;
+  for (int it = 0; it < i1 - i0; ++it) {
+    const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
+    const int b = bk / p.Hkv, hk = bk % p.Hkv;
+    const int64_t bh0 = (int64_t)b * p.Hq + hk * G;
+    if (bk != cur) {
+      cur = bk;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if ((threadIdx.x & 31) == 0) lred[threadIdx.x >> 5][g] = l;
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    float l = 0.0f;
-    for (int w = 0; w < DK_KEYS / 32; ++w) l += lred[w][threadIdx.x];
-    p.lpart[((int64_t)b * p.Hq + hk * G + threadIdx.x) * p.nsplit + split] = l;
-  }
-  // O-partial: thread (half, d) sums keys of its parity
-  const int d = threadIdx.x % DK_D, half = threadIdx.x / DK_D;
-  float o[DK_MAXG];
+      for (int g = 0; g < MG; ++g)
+        if (g < G) m[g] = __uint_as_float(p.mrow[bh0 + g]);
+    }
+    const int s = it % C::STAGES;
+    // a failed wait reads stale shared memory below; all consumers then leave together at consumers_all
+    const bool landed = mbar_wait(&full[s], (it / C::STAGES) & 1, 0x412);
+    uint8_t* st = ring + (size_t)s * C::STAGE;
+    const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
+    if (nlive < DK_KEYS) {
+      // keys past len: whatever the cache holds there becomes V = 0 (P-hat is 0 there too)
+      uint4* vc = reinterpret_cast<uint4*>(st);
+      uint4* vs = reinterpret_cast<uint4*>(st + PV_VC);
+      for (int i = nlive * (DK_D / 2 / 16) + t; i < DK_KEYS * (DK_D / 2 / 16); i += DK_WARPS * 32)
+        vc[i] = make_uint4(0u, 0u, 0u, 0u);
+      for (int i = nlive * (DK_D / 16) + t; i < DK_KEYS * (DK_D / 16); i += DK_WARPS * 32)
+        vs[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    {
+      const bool live = t < nlive;
+      const float gv = live ? reinterpret_cast<const float*>(st + PV_VC + PV_VS)[t] : 0.0f;
+      const float* Ss = reinterpret_cast<const float*>(st + PV_VC + PV_VS + PV_VG);
 #pragma unroll
-  for (int g = 0; g < DK_MAXG; ++g) o[g] = 0.0f;
-  const int kend = min(DK_KEYS, p.len - split * DK_KEYS);
-  for (int kk = half; kk < kend; kk += 2) {
-    const int key = split * DK_KEYS + kk;
-    const int64_t row = ((int64_t)b * p.Hkv + hk) * p.Tmax + key;
-    const uint8_t cb = p.v_codes[row * (DK_D / 2) + d / 2];
-    const float code = e2m1_value((d & 1) ? (cb >> 4) : (cb & 15u));
-    const float v = __fmul_rn(__fmul_rn(code, e4m3_to_f32(p.v_scales[row * DK_D + d])),
-                              p.v_g[(int64_t)b * p.Tmax + key]);
+      for (int g = 0; g < MG; ++g) {
+        if (g >= G) break;
+        const float e = live ? exp2f(__fmul_rn(Ss[g * DK_KEYS + t] - m[g], log2e)) : 0.0f;
+        float am = e;  // block of 16 keys = 16 consecutive lanes
 #pragma unroll
-    for (int g = 0; g < DK_MAXG; ++g)
-      if (g < G) o[g] = __fmaf_rn(ph[g][kk], v, o[g]);
-  }
+        for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        const uint8_t sb = e4m3_satfinite(__fmul_rn(am, r6));
+        const float sf = e4m3_to_f32(sb);
+        const float rs = sf == 0.0f ? 0.0f : __frcp_rn(sf);
+        const uint32_t byte = e2m1x2(__fmaf_rn(e, rs, 0.0f), 0.0f);
+        ph[g][t] = live ? __fmul_rn(__fmul_rn(e2m1_value(byte & 15u), sf), gv) : 0.0f;
+        float l = e;
 #pragma unroll
-  for (int g = 0; g < DK_MAXG; ++g)
-    if (g < G) opart[half][g][d] = o[g];
-  __syncthreads();
-  for (int i = threadIdx.x; i < G * DK_D; i += DK_KEYS) {
-    const int g = i / DK_D, dd = i % DK_D;
-    p.opart[(((int64_t)b * p.Hq + hk * G + g) * p.nsplit + split) * DK_D + dd] = opart[0][g][dd] + opart[1][g][dd];
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) lred[warp][g] = l;
+      }
+    }
+    if (!consumers_all(landed)) break;  // ph, lred and the zeroed V are visible
+    if (t < G) {
+      float l = 0.0f;
+      for (int w = 0; w < DK_WARPS; ++w) l += lred[w][t];
+      p.lpart[(bh0 + t) * p.nsplit + split] = l;
+    }
+    for (int g0 = 0; g0 < G; g0 += AG) {
+      float acc[AG][8];
+#pragma unroll
+      for (int g = 0; g < AG; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[g][i] = 0.0f;
+#pragma unroll
+      for (int u4 = 0; u4 < 4; ++u4) {
+        float v[4][8];  // code * scale of 4 keys, 8 dims each
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int key = slot * 16 + u4 * 4 + u;
+          const uint32_t cw = *reinterpret_cast<const uint32_t*>(st + key * (DK_D / 2) + 4 * oct);
+          const uint2 sw = *reinterpret_cast<const uint2*>(st + PV_VC + key * DK_D + 8 * oct);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t sc = ((i < 2 ? sw.x : sw.y) >> (16 * (i & 1))) & 0xFFFFu;
+            const uint32_t w = hmul2u(cvt_e2m1x2_f16x2((cw >> (8 * i)) & 0xFFu), cvt_e4m3x2_f16x2(sc));
+            v[u][2 * i] = half_lo(w);
+            v[u][2 * i + 1] = half_hi(w);
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < AG; ++g)
+          if (g0 + g < G) {
+            const float4 pg = *reinterpret_cast<const float4*>(&ph[g0 + g][slot * 16 + u4 * 4]);
+            const float pa[4] = {pg.x, pg.y, pg.z, pg.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                fma2(acc[g][2 * i], acc[g][2 * i + 1], pa[u], v[u][2 * i], v[u][2 * i + 1]);
+          }
+      }
+      if (g0 + AG >= G) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // the stage is no longer read
+      }
+      // slots 2w and 2w+1 share a warp: fold lane l + 16 into lane l
+#pragma unroll
+      for (int g = 0; g < AG; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[g][i] += __shfl_xor_sync(0xffffffffu, acc[g][i], 16);
+      if (warp >= 4 && lane < 16) {
+#pragma unroll
+        for (int g = 0; g < AG; ++g)
+          if (g0 + g < G)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) part[warp - 4][g][8 * oct + i] = acc[g][i];
+      }
+      consumers_sync();
+      if (warp < 4 && lane < 16) {
+#pragma unroll
+        for (int g = 0; g < AG; ++g)
+          if (g0 + g < G)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) part[warp][g][8 * oct + i] += acc[g][i];
+      }
+      consumers_sync();
+      // ((w0 + w4) + (w2 + w6)) + ((w1 + w5) + (w3 + w7)), in a fixed order
+      const int ng = min(AG, G - g0);
+      for (int i = t; i < ng * DK_D; i += DK_WARPS * 32) {
+        const int g = i / DK_D, dd = i % DK_D;
+        p.opart[((bh0 + g0 + g) * p.nsplit + split) * DK_D + dd] =
+            (part[0][g][dd] + part[2][g][dd]) + (part[1][g][dd] + part[3][g][dd]);
+      }
+      if (g0 + AG < G) consumers_sync();  // part is rewritten by the next head group
+    }
   }
 }
 
+// O = sum over chunks of O-partial / sum of l, four interleaved partial sums in a fixed order.
 __global__ void __launch_bounds__(DK_D) decode_combine_kernel(DecodeArgs p) {
   const int bh = blockIdx.x, d = threadIdx.x;
-  float o = 0.0f, l = 0.0f;
-  for (int s = 0; s < p.nsplit; ++s) {
-    o += p.opart[((int64_t)bh * p.nsplit + s) * DK_D + d];
-    l += p.lpart[(int64_t)bh * p.nsplit + s];
+  const float* op = p.opart + (int64_t)bh * p.nsplit * DK_D + d;
+  const float* lp = p.lpart + (int64_t)bh * p.nsplit;
+  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f}, l[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int s = 0;
+  for (; s + 8 <= p.nsplit; s += 8) {
+    float ov[8], lv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) ov[u] = op[(int64_t)(s + u) * DK_D], lv[u] = lp[s + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) o[u & 3] += ov[u], l[u & 3] += lv[u];
   }
-  p.out[(int64_t)bh * DK_D + d] = o / l;
+  for (; s < p.nsplit; ++s) o[0] += op[(int64_t)s * DK_D], l[0] += lp[s];
+  p.out[(int64_t)bh * DK_D + d] = ((o[0] + o[1]) + (o[2] + o[3])) / ((l[0] + l[1]) + (l[2] + l[3]));
+}
+
+// Persistent grid: as many CTAs as are resident at once, at most one per item.
+int persistent_grid(const void* fn, uint32_t smem, int items) {
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, DK_THREADS, smem) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  return std::min(items, sms * per_sm);
+}
+
+template <int MG>
+int launch_pv(const DecodeArgs& a, int items, cudaStream_t st) {
+  using C = PvCfg<MG>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(decode_pv_kernel<MG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    attr = true;
+  }
+  const int grid = persistent_grid((const void*)decode_pv_kernel<MG>, C::SMEM, items);
+  decode_pv_kernel<MG><<<grid, DK_THREADS, C::SMEM, st>>>(a);
+  return check_launch("decode_pv_kernel");
 }
 
 }  // namespace
@@ -190,37 +499,53 @@ extern "C" int64_t fp4attn_decode_workspace_size(int B, int Hq, int len) {
   if (B <= 0 || Hq <= 0 || len <= 0) return -1;
   const int64_t nsplit = (len + DK_KEYS - 1) / DK_KEYS;
   const int64_t bh = (int64_t)B * Hq;
-  return (bh * nsplit * DK_KEYS + bh * nsplit * (DK_D + 2)) * (int64_t)sizeof(float);
+  return (bh * nsplit * DK_KEYS + bh * nsplit * (DK_D + 1) + bh) * (int64_t)sizeof(float);
 }
 
-extern "C" int fp4attn_decode(const float* qhat, const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+extern "C" int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                              const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
                               const uint8_t* v_codes, const uint8_t* v_scales, const float* v_g, int B, int Hq,
                               int Hkv, int D, int len, int Tmax, float scaling, float* out, void* workspace,
                               int64_t workspace_bytes, void* stream) {
   clear_error();
-  if (!qhat || !k_codes || !k_scales || !k_g || !v_codes || !v_scales || !v_g || !out || !workspace)
+  if (!q_codes || !q_scales || !q_g || !k_codes || !k_scales || !k_g || !v_codes || !v_scales || !v_g || !out ||
+      !workspace)
     return set_error(FP4ATTN_ERR_ARG, "null pointer");
   if (D != DK_D) return set_error(FP4ATTN_ERR_UNSUPPORTED, "head_dim must be %d", DK_D);
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || len <= 0 || Tmax < len)
     return set_error(FP4ATTN_ERR_ARG, "bad shape");
+  if (Tmax % DK_KEYS) return set_error(FP4ATTN_ERR_ARG, "Tmax must be a multiple of %d", DK_KEYS);
   if (Hq / Hkv > DK_MAXG) return set_error(FP4ATTN_ERR_UNSUPPORTED, "more than %d query heads per KV head", DK_MAXG);
-  if (((uintptr_t)k_codes | (uintptr_t)v_codes) % 16 || (uintptr_t)k_scales % 8)
-    return set_error(FP4ATTN_ERR_ARG, "cache buffers must be 16-byte (codes) / 8-byte (K scales) aligned");
+  if (((uintptr_t)k_codes | (uintptr_t)v_codes | (uintptr_t)k_scales | (uintptr_t)v_scales | (uintptr_t)k_g |
+       (uintptr_t)v_g | (uintptr_t)workspace) % 16)
+    return set_error(FP4ATTN_ERR_ARG, "cache buffers and workspace must be 16-byte aligned");
   const int64_t need = fp4attn_decode_workspace_size(B, Hq, len);
   if (workspace_bytes < need) return set_error(FP4ATTN_ERR_ARG, "workspace of %lld bytes, %lld needed",
                                                (long long)workspace_bytes, (long long)need);
   const int nsplit = (len + DK_KEYS - 1) / DK_KEYS;
   const int64_t bh = (int64_t)B * Hq;
-  float* ws = static_cast<float*>(workspace);
-  DecodeArgs a{qhat, k_codes, k_scales, k_g, v_codes, v_scales, v_g, B, Hq, Hkv, len, Tmax, nsplit, scaling,
-               ws, ws + bh * nsplit * DK_KEYS, ws + bh * nsplit * (DK_KEYS + 1),
-               ws + bh * nsplit * (DK_KEYS + 1 + DK_D), out};
+  float* S = static_cast<float*>(workspace);
+  float* opart = S + bh * nsplit * DK_KEYS;
+  float* lpart = opart + bh * nsplit * DK_D;
+  unsigned int* mrow = reinterpret_cast<unsigned int*>(lpart + bh * nsplit);
+  DecodeArgs a{q_codes, q_scales, q_g, k_codes, k_scales, k_g,   v_codes, v_scales, v_g,  B,  Hq,
+               Hkv,     len,      Tmax, nsplit, scaling,  S,     opart,   lpart,    mrow, out};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const dim3 grid(nsplit, B * Hkv);
-  decode_scores_kernel<<<grid, DK_KEYS, 0, st>>>(a);
+  if (cudaMemsetAsync(mrow, 0xFF, bh * sizeof(unsigned int), st) != cudaSuccess)
+    return set_error(FP4ATTN_ERR_CUDA, "memset: %s", cudaGetErrorString(cudaGetLastError()));
+  const int items = nsplit * B * Hkv;
+  constexpr uint32_t sc_smem = SC_STAGES * SC_STAGE;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(decode_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem);
+    attr = true;
+  }
+  decode_scores_kernel<<<persistent_grid((const void*)decode_scores_kernel, sc_smem, items), DK_THREADS, sc_smem,
+                         st>>>(a);
   if (int e = check_launch("decode_scores_kernel")) return e;
-  decode_pv_kernel<<<grid, DK_KEYS, 0, st>>>(a);
-  if (int e = check_launch("decode_pv_kernel")) return e;
+  const int G = Hq / Hkv;
+  const int e = G <= 4 ? launch_pv<4>(a, items, st) : G <= 8 ? launch_pv<8>(a, items, st) : launch_pv<16>(a, items, st);
+  if (e) return e;
   decode_combine_kernel<<<(unsigned)bh, DK_D, 0, st>>>(a);
   return check_launch("decode_combine_kernel");
 }

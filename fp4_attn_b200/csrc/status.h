@@ -20,4 +20,5 @@ void count_launch();
 unsigned int gemm_status(bool reset);
 unsigned int attn_status(bool reset);
 unsigned int quant_status(bool reset);
+unsigned int decode_status(bool reset);
 }  // namespace fp4

@@ -10,7 +10,8 @@ those same values -- codes, E4M3 scales and global scales -- and
 the GPU (``fp4attn_decode`` in the C ABI).  As in the prefill path, Q and K
 are taken after RoPE.
 
-Layout (device tensors):
+Layout (device tensors; Tmax is rounded up to a multiple of 256 so that the
+decode kernels stream whole chunks of 256 keys):
   k_codes  uint8 [B, Hkv, Tmax, D/2]   E2M1 pairs, element 2k in the low nibble
   k_scales uint8 [B, Hkv, Tmax, D/16]  E4M3 block scales along head_dim
   k_g      fp32  [B, Tmax]             per-token global scale (row max)
@@ -33,7 +34,10 @@ class NVFP4KVCache:
     def __init__(self, B: int, Hkv: int, Tmax: int, D: int, device):
         if D != HEAD_DIM:
             raise NotImplementedError(f"head_dim {D}: the decode kernel implements {HEAD_DIM}")
-        self.B, self.Hkv, self.Tmax, self.D = B, Hkv, Tmax, D
+        self.B, self.Hkv, self.D = B, Hkv, D
+        self.capacity = Tmax
+        Tmax = (Tmax + 255) // 256 * 256
+        self.Tmax = Tmax
         u8 = torch.uint8
         self.k_codes = torch.zeros(B, Hkv, Tmax, D // 2, dtype=u8, device=device)
         self.k_scales = torch.zeros(B, Hkv, Tmax, D // 16, dtype=u8, device=device)
@@ -49,8 +53,8 @@ class NVFP4KVCache:
         B, H, q, D = k.shape
         if (B, H, D) != (self.B, self.Hkv, self.D) or v.shape != k.shape:
             raise ValueError("k/v must be [B, Hkv, q, D] matching the cache")
-        if self.len + q > self.Tmax:
-            raise ValueError(f"cache holds {self.Tmax} tokens")
+        if self.len + q > self.capacity:
+            raise ValueError(f"cache holds {self.capacity} tokens")
         t0, t1 = self.len, self.len + q
         # K: row mode on the [B*q, Hkv*D] view (llama_patch.py:167,194)
         k2d = k.permute(0, 2, 1, 3).reshape(B * q, H * D)
@@ -92,12 +96,12 @@ def decode_attention(q: torch.Tensor, cache: NVFP4KVCache, scaling: float | None
         raise ValueError("empty cache")
     if scaling is None:
         scaling = D ** -0.5
-    qhat = quant.qdq(q.reshape(B, Hq * D), "row", 1536.0, torch.float32).view(B, Hq, D).contiguous()
+    pq = quant.quantize(q.reshape(B, Hq * D), "row", 1536.0)
     need = _lib.load().fp4attn_decode_workspace_size(B, Hq, cache.len)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
     out = torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
-    _lib.call("fp4attn_decode", qhat.data_ptr(), cache.k_codes.data_ptr(), cache.k_scales.data_ptr(),
+    _lib.call("fp4attn_decode", pq.codes.data_ptr(), pq.scales.data_ptr(), pq.g.data_ptr(), cache.k_codes.data_ptr(), cache.k_scales.data_ptr(),
               cache.k_g.data_ptr(), cache.v_codes.data_ptr(), cache.v_scales.data_ptr(), cache.v_g.data_ptr(),
               B, Hq, cache.Hkv, D, cache.len, cache.Tmax, float(scaling), out.data_ptr(), workspace.data_ptr(),
               workspace.numel() * workspace.element_size(), _lib.stream_of(q))

@@ -196,14 +196,18 @@ int fp4attn_forward_noalloc(const void* q, const void* k, const void* v, int in_
  *   v_codes [B][Hkv][Tmax][D/2], v_scales E4M3 [B][Hkv][Tmax][D] (one per
  *   element: V's blocks run along the tokens of the call that appended them),
  *   v_g [B][Tmax].
- * qhat is the fake-quantized query, fp32 [B][Hq][D]; out fp32 [B][Hq][D];
+ * The query is packed the same way, row mode on its [B, Hq*D] view:
+ * q_codes [B][Hq*D/2], q_scales E4M3 [B][Hq*D/16], q_g [B]; out fp32 [B][Hq][D];
  * len cached tokens are attended (no mask: the query is the newest token).
- * D = 128, Hq/Hkv <= 16.  workspace: fp4attn_decode_workspace_size bytes. */
+ * D = 128, Hq/Hkv <= 16, Tmax a multiple of 256 (the kernels copy whole
+ * chunks of 256 keys; keys past len are read but not used).  The cache
+ * buffers, g arrays and workspace are 16-byte aligned.  workspace:
+ * fp4attn_decode_workspace_size bytes, nothing has to start zeroed. */
 int64_t fp4attn_decode_workspace_size(int B, int Hq, int len);
-int fp4attn_decode(const float* qhat, const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
-                   const uint8_t* v_codes, const uint8_t* v_scales, const float* v_g, int B, int Hq, int Hkv, int D,
-                   int len, int Tmax, float scaling, float* out, void* workspace, int64_t workspace_bytes,
-                   void* stream);
+int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g, const uint8_t* k_codes,
+                   const uint8_t* k_scales, const float* k_g, const uint8_t* v_codes, const uint8_t* v_scales,
+                   const float* v_g, int B, int Hq, int Hkv, int D, int len, int Tmax, float scaling, float* out,
+                   void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Profiling aid: a non-NULL buf makes later fp4attn_fwd_packed calls record
  * an event timeline (SM clock cycles from clock64) of each CTA's first work unit into

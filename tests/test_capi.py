@@ -90,3 +90,27 @@ def test_attention_forward_argument_errors():
     args = [p, p, p, 1, 1, 2, 1, 128, 128] + [0] * 9 + [1, 0.1, p, p, 16, None]
     assert L.fp4attn_forward(*args) == 1
     assert b"workspace" in L.fp4attn_last_error()
+
+
+def test_decode_argument_errors():
+    """fp4attn_decode rejects bad arguments with a status code before touching the device."""
+    from fp4_attn_b200 import _lib
+    L = _lib.load()
+    assert L.fp4attn_decode_workspace_size(0, 32, 10) == -1
+    B, Hq, Hkv, D, len_ = 2, 32, 8, 128, 300
+    need = L.fp4attn_decode_workspace_size(B, Hq, len_)
+    nsplit = (len_ + 255) // 256
+    assert need == (B * Hq * nsplit * 256 + B * Hq * nsplit * (D + 1) + B * Hq) * 4
+    p = ctypes.c_void_p(256)
+
+    def call(ptr=p, Hq=Hq, Hkv=Hkv, D=D, len_=len_, Tmax=512, ws_bytes=need, ws=p):
+        return L.fp4attn_decode(ptr, ptr, ptr, ptr, ptr, ptr, ptr, ptr, ptr, B, Hq, Hkv, D, len_, Tmax, 0.088,
+                                ptr, ws, ws_bytes, None)
+
+    assert call(ptr=None) == 1 and b"null" in L.fp4attn_last_error()
+    assert call(D=64) == 3 and b"head_dim" in L.fp4attn_last_error()
+    assert call(Tmax=299) == 1 and b"shape" in L.fp4attn_last_error()
+    assert call(Tmax=400) == 1 and b"multiple of 256" in L.fp4attn_last_error()
+    assert call(Hq=34, Hkv=2) == 3 and b"query heads" in L.fp4attn_last_error()
+    assert call(ptr=ctypes.c_void_p(264)) == 1 and b"aligned" in L.fp4attn_last_error()
+    assert call(ws_bytes=need - 4) == 1 and b"workspace" in L.fp4attn_last_error()

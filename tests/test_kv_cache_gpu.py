@@ -37,13 +37,14 @@ def _dequant_cache(c):
     return k, v
 
 
-@pytest.mark.parametrize("B,Hq,Hkv", [(2, 8, 2), (3, 4, 4)])
-def test_decode_over_nvfp4_cache(B, Hq, Hkv):
+@pytest.mark.parametrize("B,Hq,Hkv,T0", [(2, 8, 2, 300), (3, 4, 4, 300), (1, 16, 2, 520), (2, 16, 1, 700)])
+def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0):
+    """Query heads per KV head 4, 1, 8 and 16; one to three splits of 256 keys."""
     from fp4_attn_b200.gemm import device_status
     from fp4_attn_b200.kv_cache import NVFP4KVCache, decode_attention
-    D, T0, steps = 128, 300, 5
+    D, steps = 128, 5
     dev = torch.device("cuda", 0)
-    g = torch.Generator().manual_seed(17 + B)
+    g = torch.Generator().manual_seed(17 + B + Hq + T0)
     cache = NVFP4KVCache(B, Hkv, T0 + steps, D, dev)
     ks, vs = [], []
 

@@ -6,7 +6,7 @@ plus the Q/K/V fake-quant of llama_patch.py:167-196): it takes post-RoPE
 query/key/value in the HF layout [B, H, T, D] and returns the attention
 output in the layout the reference returns, [B, T, Hq, D], in fp32.
 
-Steps (all on the GPU, no CPU path), one C ABI call (fp4attn_forward):
+Steps (all on the GPU, no CPU path), one C ABI call (fp4attn_forward_ex):
   1. Q and K -> NVFP4 codes + E4M3 scales (tcgen05 layout) + per-token global
      scale, on their [B*T, H*D] views (fp4q_quantize, row mode);
   2. V -> Vhat (NVFP4 along tokens, per-token global scale) as fp16 hi/lo
@@ -20,6 +20,7 @@ import torch
 from . import _lib
 
 HEAD_DIM = 128
+DUAL_Q, DUAL_P = 1, 2  # fp4attn_forward_ex flags
 
 
 class AttentionWorkspace:
@@ -30,13 +31,15 @@ class AttentionWorkspace:
     gq/gk per-token global scales [B*Tp], vhi/vlo V-hat planes [B*Hkv*D, Tp].
     """
 
-    def __init__(self, B, Hq, Hkv, T, D, device):
+    def __init__(self, B, Hq, Hkv, T, D, device, dual_q: bool = False):
         import ctypes
         self.shape = (B, Hq, Hkv, T, D)
+        self.dual_q = bool(dual_q)
+        self.flags = DUAL_Q if dual_q else 0
         self.Tp = (T + 127) // 128 * 128
         Tp = self.Tp
-        offs = (ctypes.c_int64 * 8)()
-        size = _lib.load().fp4attn_workspace_layout(B, Hq, Hkv, T, D, offs)
+        offs = (ctypes.c_int64 * 12)()
+        size = _lib.load().fp4attn_workspace_layout_ex(B, Hq, Hkv, T, D, self.flags, offs)
         if size < 0:
             raise ValueError(f"unsupported attention shape B={B} Hq={Hq} Hkv={Hkv} T={T} D={D}")
         self.nbytes = int(size)
@@ -61,6 +64,10 @@ class AttentionWorkspace:
         self.gk = view(5, f32, (B * Tp,))
         self.vhi = view(6, f16, (B * Hkv * D, Tp))
         self.vlo = view(7, f16, (B * Hkv * D, Tp))
+        if dual_q:  # the residual Q slice (fp4attn_workspace_layout_ex pieces 8-11)
+            self.qc_lo = view(8, u8, (B * Tp, Hq * D // 2))
+            self.qs_lo = view(9, u8, (B * Tp // 128 * Hq * (D // 64) * 512,))
+            self.gq_lo = view(10, f32, (B * Tp,))
 
     def ptr(self) -> int:
         return self.buf.data_ptr() + self.base
@@ -91,11 +98,15 @@ def prepare_v(v: torch.Tensor, vhi, vlo, Tp: int, vhat=None, g=None) -> None:
 
 def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
                       scaling: float | None = None, out: torch.Tensor | None = None,
-                      workspace: AttentionWorkspace | None = None, num_ctas: int = 0) -> torch.Tensor:
+                      workspace: AttentionWorkspace | None = None, num_ctas: int = 0,
+                      dual_q: bool = False, dual_p: bool = False) -> torch.Tensor:
     """NVFP4 attention forward.  q [B,Hq,T,D], k/v [B,Hkv,T,D] (CUDA) -> fp32 [B,T,Hq,D].
 
-    One call of the C ABI's fp4attn_forward (quantize Q/K, prepare V-hat,
-    attention) with the packed operands in ``workspace``.
+    One call of the C ABI's fp4attn_forward_ex (quantize Q/K, prepare V-hat,
+    attention) with the packed operands in ``workspace``.  dual_q / dual_p
+    select the reference's dual-slice Q / P (FP4_USE_DUAL_QUANT_Q /
+    FP4_USE_DUAL_QUANT_ATTN, llama_patch.py:84,183; dual_nvfp4,
+    fp4_quant_utils.py:307-315).
     """
     _lib.require_cuda(q, k, v)
     q, k, v = _bhtd(q), _bhtd(k), _bhtd(v)
@@ -110,9 +121,13 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
         raise ValueError("q [B,Hq,T,D], k/v [B,Hkv,T,D] with Hq % Hkv == 0 expected")
     if scaling is None:
         scaling = D ** -0.5
-    ws = workspace or AttentionWorkspace(B, Hq, Hkv, T, D, q.device)
+    ws = workspace or AttentionWorkspace(B, Hq, Hkv, T, D, q.device, dual_q=dual_q)
     if ws.shape != (B, Hq, Hkv, T, D):
         raise ValueError(f"workspace made for {ws.shape}, called with {(B, Hq, Hkv, T, D)}")
+    if dual_q and not ws.dual_q:
+        raise ValueError("dual_q needs a workspace made with dual_q=True")
+    if num_ctas and (dual_q or dual_p):
+        raise ValueError("num_ctas is a single-slice profiling option")
     if out is None:
         out = torch.empty(B, T, Hq, D, dtype=torch.float32, device=q.device)
     elif out.shape != (B, T, Hq, D) or out.dtype != torch.float32 or not out.is_contiguous():
@@ -125,8 +140,9 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
                   ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), out.data_ptr(), B, Hq,
                   Hkv, T, ws.Tp, D, 1 if causal else 0, float(scaling), int(num_ctas), _lib.stream_of(q))
         return out
-    _lib.call("fp4attn_forward", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], B, Hq, Hkv, T, D,
-              q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
-              v.stride(2), 1 if causal else 0, float(scaling), out.data_ptr(), ws.ptr(), ws.nbytes,
-              _lib.stream_of(q))
+    flags = (DUAL_Q if dual_q else 0) | (DUAL_P if dual_p else 0)
+    _lib.call("fp4attn_forward_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], B, Hq, Hkv, T,
+              D, q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0),
+              v.stride(1), v.stride(2), 1 if causal else 0, float(scaling), flags, out.data_ptr(), ws.ptr(),
+              ws.nbytes, _lib.stream_of(q))
     return out

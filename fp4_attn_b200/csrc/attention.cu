@@ -53,24 +53,30 @@ constexpr int THREADS = 128 + NWG * 128;
 // shared memory map (bytes, all pieces 1024-aligned where TMA/UMMA need it)
 constexpr int Q_BYTES = BM * HD / 2;  // 8 KB of E2M1 codes
 constexpr int OFF_Q = 0, OFF_QSF = 8192, OFF_GQ = 9216;
+// second (residual) Q slice of dual-slice Q: codes, scale atoms, g
+constexpr int OFF_QLO = 10240, OFF_QLOSF = 18432, OFF_GQLO = 19456;
 constexpr int K_STAGE = 10240;  // codes 8 KB, scale atoms 1 KB, gk 512 B
-constexpr int OFF_K = 10240;
+constexpr int OFF_K = 20480;
 constexpr int V_HALF = HD * 64 * 2;  // 128 rows (d) x 64 keys x fp16 = one plane of a half tile (one TMA box)
 constexpr int V_STAGE = 4 * V_HALF;  // keys 0-63 hi, lo; keys 64-127 hi, lo
 constexpr int OFF_V = OFF_K + NK * K_STAGE;
-constexpr int OFF_STAT = OFF_V + NV * V_STAGE;  // m[NWG][128], l[NWG][128]
-constexpr int OFF_RCP = OFF_STAT + 2 * NWG * 128 * 4;
+constexpr int OFF_STAT = OFF_V + NV * V_STAGE;  // m[NWG][128], l[NWG][128], residual max[NWG][128]
+constexpr int OFF_RCP = OFF_STAT + 3 * NWG * 128 * 4;
 constexpr int OFF_BAR = OFF_RCP + 128 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 // TMEM columns: S0, S1, O, P (fp16, single-buffered; warpgroup q writes columns
-// 16q..16q+15), Q scale atoms, K scale atoms per stage (488 of 512 columns).
-constexpr uint32_t T_S = 0, T_O = 256, T_P = 384, T_SFA = 448, T_SFB = 456;
+// 16q..16q+15), Q scale atoms, K scale atoms per stage, the residual Q
+// slice's scale atoms (496 of 512 columns).  With dual-slice Q, S0 and S1
+// hold the two slices' products of the same key tile (S single-buffered).
+constexpr uint32_t T_S = 0, T_O = 256, T_P = 384, T_SFA = 448, T_SFB = 456, T_SFA_LO = 488;
 }  // namespace attn
 
 struct AttnArgs {
   const uint8_t* qsf;  // tcgen05 atoms, nkb4q = Hq*2 groups per 128-row block
   const float* gq;     // [B*Tp]
+  const uint8_t* qsf_lo;  // residual Q slice (dual-slice Q), same layouts
+  const float* gq_lo;
   const uint8_t* ksf;
   const float* gk;
   float* out;  // [B, T, Hq, HD] fp32
@@ -135,13 +141,17 @@ __device__ __forceinline__ int kv_tiles(const Unit& un, const AttnArgs& p) {
 }
 
 // TRACE: record the event timeline (fp4attn_set_trace); the plain instantiation
-// has no trace code at all.
-template <bool TRACE>
+// has no trace code at all.  DQ: dual-slice Q (a second, residual Q slice;
+// both QK products of a key tile go to the two S accumulators and combine per
+// row).  DP: dual-slice P (a residual pass between the max pass and the PV
+// pass finds each row's residual scale; the PV pass writes hi + lo).
+template <bool TRACE, bool DQ, bool DP>
 __global__ void __launch_bounds__(attn::THREADS, 1)
-    fp4_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmVhi, const __grid_constant__ CUtensorMap tmVlo,
-                    AttnArgs p) {
+    fp4_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmQlo,
+                    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmVhi,
+                    const __grid_constant__ CUtensorMap tmVlo, AttnArgs p) {
   using namespace attn;
+  constexpr int NPASS = DP ? 3 : 2;  // QK passes per unit; the last one feeds PV
   auto tr = [&](uint32_t uc, int slot, int j) {
     if constexpr (TRACE) trace(p, uc, slot, j);
   };
@@ -149,6 +159,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* stat_m = reinterpret_cast<float*>(sm + OFF_STAT);
   float* stat_l = stat_m + NWG * 128;
+  float* stat_r = stat_m + 2 * NWG * 128;
   float* rcp = reinterpret_cast<float*>(sm + OFF_RCP);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bar + 0;
@@ -209,6 +220,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     // ------------------------------------------------- producer: Q and K
     if (elect_one_lane()) {
       tma_prefetch_desc(&tmQ);
+      if constexpr (DQ) tma_prefetch_desc(&tmQlo);
       tma_prefetch_desc(&tmK);
       uint32_t kc = 0, uc = 0;
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
@@ -217,11 +229,16 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const int hk = un.h / group;
         const int qrow = un.b * p.Tp + un.qt * BM;
         if (uc > 0) mbar_wait(q_empty, (uc - 1) & 1, 0x201);
-        mbar_arrive_expect_tx(q_full, Q_BYTES + 1024 + 512);
+        mbar_arrive_expect_tx(q_full, (DQ ? 2 : 1) * (Q_BYTES + 1024 + 512));
         tma_load_2d(sm + OFF_Q, &tmQ, q_full, un.h * (HD / 2), qrow);
         bulk_load(sm + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * nkb4q + 2 * un.h) * 512, 1024, q_full);
         bulk_load(sm + OFF_GQ, p.gq + qrow, 512, q_full);
-        for (int pass = 0; pass < 2; ++pass) {
+        if constexpr (DQ) {
+          tma_load_2d(sm + OFF_QLO, &tmQlo, q_full, un.h * (HD / 2), qrow);
+          bulk_load(sm + OFF_QLOSF, p.qsf_lo + ((int64_t)(qrow / 128) * nkb4q + 2 * un.h) * 512, 1024, q_full);
+          bulk_load(sm + OFF_GQLO, p.gq_lo + qrow, 512, q_full);
+        }
+        for (int pass = 0; pass < NPASS; ++pass) {
           for (int j = 0; j < n; ++j, ++kc) {
             const int s = kc % NK;
             if (kc >= NK) mbar_wait(&k_empty[s], ((kc / NK) - 1) & 1, 0x202);
@@ -273,7 +290,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const int s = kc % NK;
         mbar_wait(&k_full[s], (kc / NK) & 1, 0x212);
         tc_fence_after();
-        tr(uc, TR_QK + 32 * pass, j);
+        if (pass < 2) tr(uc, TR_QK + 32 * pass, j);
         uint8_t* ks = sm + OFF_K + s * K_STAGE;
         const uint32_t sfb = tmem + T_SFB + 8 * s;
         tmem_cp_sf_atom(sfb, smem_desc(smem_u32(ks + 8192), 16, 128, kSwizzleNone));
@@ -284,6 +301,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           const uint64_t ad = smem_desc(smem_u32(sm + OFF_Q) + kk * 32, 16, 512, kSwizzle64B);
           const uint64_t bd = smem_desc(smem_u32(ks) + kk * 32, 16, 512, kSwizzle64B);
           mma_nvf4(d, ad, bd, idq, tmem + T_SFA + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
+        }
+        if constexpr (DQ) {  // residual slice into the second accumulator
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint64_t ad = smem_desc(smem_u32(sm + OFF_QLO) + kk * 32, 16, 512, kSwizzle64B);
+            const uint64_t bd = smem_desc(smem_u32(ks) + kk * 32, 16, 512, kSwizzle64B);
+            mma_nvf4(tmem + T_S + 128, ad, bd, idq, tmem + T_SFA_LO + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
+          }
         }
         tc_commit(&k_empty[s]);
         tc_commit(&s_full[kb]);
@@ -299,8 +324,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tc_fence_after();
         tmem_cp_sf_atom(tmem + T_SFA, smem_desc(smem_u32(sm + OFF_QSF), 16, 128, kSwizzleNone));
         tmem_cp_sf_atom(tmem + T_SFA + 4, smem_desc(smem_u32(sm + OFF_QSF + 512), 16, 128, kSwizzleNone));
-        for (int pass = 0; pass < 2; ++pass)
-          for (int j = 0; j < n; ++j) issue_qk(j, j & 1, pass);
+        if constexpr (DQ) {
+          tmem_cp_sf_atom(tmem + T_SFA_LO, smem_desc(smem_u32(sm + OFF_QLOSF), 16, 128, kSwizzleNone));
+          tmem_cp_sf_atom(tmem + T_SFA_LO + 4, smem_desc(smem_u32(sm + OFF_QLOSF + 512), 16, 128, kSwizzleNone));
+        }
+        for (int pass = 0; pass < NPASS; ++pass)
+          for (int j = 0; j < n; ++j) issue_qk(j, DQ ? 0 : (j & 1), pass);
         tc_commit(q_empty);
         tr(uc, TR_UEND, 0);
       }
@@ -387,19 +416,48 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const int n = kv_tiles(un, p);
       const int qpos = un.qt * BM + r;  // query index within the sequence
       mbar_wait(q_full, uc & 1, 0x221);
-      const float uscale = reinterpret_cast<const float*>(sm + OFF_GQ)[r] * p.scale_log2;
+      const float ghi = reinterpret_cast<const float*>(sm + OFF_GQ)[r];
+      const float uscale = ghi * p.scale_log2;
+      // dual-slice Q: acc = acc_hi + acc_lo * (g_lo / g_hi), so the row keeps u = g_hi * scaling * log2 e
+      float ratio = 0.0f;
+      if constexpr (DQ) {
+        const float glo = reinterpret_cast<const float*>(sm + OFF_GQLO)[r];
+        ratio = ghi == 0.0f ? 0.0f : __fdiv_rn(glo, ghi);
+      }
+      const uint64_t ratio2 = pk2(ratio, ratio);
+      auto load_s = [&](int kb, uint32_t(&a)[32]) {
+        tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
+        if constexpr (DQ) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // the residual slice's scores, 16 columns at a time
+            uint32_t b[16];
+            tmem_ld16(tmem + lane_base + T_S + 128 + col0 + 16 * h, b);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+              float x0, x1;
+              upk2(fma2(pk2(__uint_as_float(b[i]), __uint_as_float(b[i + 1])), ratio2,
+                        pk2(__uint_as_float(a[16 * h + i]), __uint_as_float(a[16 * h + i + 1]))),
+                   x0, x1);
+              a[16 * h + i] = __float_as_uint(x0);
+              a[16 * h + i + 1] = __float_as_uint(x1);
+            }
+          }
+        } else {
+          tmem_ld_wait();
+        }
+      };
       // ---- pass 1: row maximum of z = acc * gk over this quarter's keys
       float m = -INFINITY;
       for (int j = 0; j < n; ++j, ++kc) {
-        const int kb = j & 1, s = kc % NK;
+        const int kb = DQ ? 0 : (j & 1), s = kc % NK;
         mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x222);
         if (kb) ++sfu1;
         else ++sfu0;
         if (leader && q == 0) tr(uc, TR_SFULL, j);
         tc_fence_after();
         uint32_t a[32];
-        tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
-        tmem_ld_wait();
+        load_s(kb, a);
         // every warp releases what it has read on its own (no warpgroup barrier)
         tc_fence_before();
         __syncwarp();
@@ -422,18 +480,46 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       if (pend) epilogue();
       const float mu = m == -INFINITY ? 0.0f : m * uscale;
       const uint64_t u2 = pk2(uscale, uscale), nmu2 = pk2(-mu, -mu);
+      // ---- dual-slice P: residual pass, row max of |e - hi| over this quarter's keys
+      float gr = 0.0f, rg = 0.0f;
+      if constexpr (DP) {
+        float rm = 0.0f;
+        for (int j = 0; j < n; ++j, ++kc) {
+          const int kb = DQ ? 0 : (j & 1), s = kc % NK;
+          mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x226);
+          if (kb) ++sfu1;
+          else ++sfu0;
+          tc_fence_after();
+          uint32_t a[32];
+          load_s(kb, a);
+          tc_fence_before();
+          __syncwarp();
+          if (wlead) mbar_arrive(&s_free[kb]);
+          const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
+          const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
+          if (lim < col0 + 31) rm = chunk_rmax<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, rm);
+          else rm = chunk_rmax<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, rm);
+          __syncwarp();
+          if (wlead) mbar_arrive(&k_empty[s]);
+        }
+        stat_r[q * 128 + r] = rm;
+        named_bar(1 + NWG, NWG * 128);
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) rm = fmaxf(rm, stat_r[w * 128 + r]);
+        gr = rm;
+        rg = rm == 0.0f ? 0.0f : __frcp_rn(rm);
+      }
       // ---- pass 2: e = exp2(z*u - m*u), sum, NVFP4 fake-quant of e -> P quarter q
       uint64_t lsum2[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
       for (int j = 0; j < n; ++j, ++kc) {
-        const int kb = j & 1, s = kc % NK;
+        const int kb = DQ ? 0 : (j & 1), s = kc % NK;
         mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x223);
         if (kb) ++sfu1;
         else ++sfu0;
         if (leader && q == 0) tr(uc, TR_SFULL + 32, j);
         tc_fence_after();
         uint32_t a[32];
-        tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
-        tmem_ld_wait();
+        load_s(kb, a);
         // this warp's scores are in registers: release its share of the S buffer now
         tc_fence_before();
         __syncwarp();
@@ -442,8 +528,13 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         uint32_t pk[16];
-        if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
-        else chunk_p<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
+        if constexpr (DP) {
+          if (lim < col0 + 31) chunk_p_dual<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, rg, gr, lsum2, pk);
+          else chunk_p_dual<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, rg, gr, lsum2, pk);
+        } else {
+          if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
+          else chunk_p<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
+        }
         if (leader && q == 0) tr(uc, TR_COMP, j);
         // the previous tile's PV must have read P before quarter q is overwritten
         if (pt > 0) mbar_wait(p_free, (pt - 1) & 1, 0x225);
@@ -685,10 +776,12 @@ extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, in
   return launch_vprep(a, st);
 }
 
-extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
-                                  const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
-                                  const uint16_t* v_hi, const uint16_t* v_lo, float* out, int B, int Hq, int Hkv,
-                                  int T, int Tp, int D, int causal, float scaling, int num_ctas, void* stream) {
+extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                                       const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
+                                       const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                                       const uint16_t* v_hi, const uint16_t* v_lo, float* out, int B, int Hq,
+                                       int Hkv, int T, int Tp, int D, int causal, float scaling, int dual_p,
+                                       int num_ctas, void* stream) {
   using namespace attn;
   clear_error();
   if (D != HD) return set_error(FP4ATTN_ERR_UNSUPPORTED, "head_dim must be %d", HD);
@@ -696,13 +789,23 @@ extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scale
   if (Tp % 128 != 0 || Tp < T) return set_error(FP4ATTN_ERR_ARG, "Tp must be a multiple of 128 >= T");
   if (!q_codes || !q_scales || !q_g || !k_codes || !k_scales || !k_g || !v_hi || !v_lo || !out)
     return set_error(FP4ATTN_ERR_ARG, "null pointer");
+  const bool dq = q_codes_lo != nullptr;
+  if (dq && (!q_scales_lo || !q_g_lo)) return set_error(FP4ATTN_ERR_ARG, "null pointer (residual Q slice)");
   if (((uintptr_t)q_codes | (uintptr_t)k_codes | (uintptr_t)v_hi | (uintptr_t)v_lo | (uintptr_t)q_scales |
-       (uintptr_t)k_scales | (uintptr_t)q_g | (uintptr_t)k_g | (uintptr_t)out) % 16)
+       (uintptr_t)k_scales | (uintptr_t)q_g | (uintptr_t)k_g | (uintptr_t)out | (uintptr_t)q_codes_lo |
+       (uintptr_t)q_scales_lo | (uintptr_t)q_g_lo) % 16)
     return set_error(FP4ATTN_ERR_ARG, "buffers must be 16-byte aligned");
-  CUtensorMap mq, mk, mvh, mvl;
+  CUtensorMap mq, mql, mk, mvh, mvl;
   if (int e = encode_tiled_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, q_codes, (uint64_t)Hq * (HD / 2), (uint64_t)B * Tp,
                               (uint64_t)Hq * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
+  if (dq) {
+    if (int e = encode_tiled_2d(&mql, CU_TENSOR_MAP_DATA_TYPE_UINT8, q_codes_lo, (uint64_t)Hq * (HD / 2),
+                                (uint64_t)B * Tp, (uint64_t)Hq * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+      return e;
+  } else {
+    mql = mq;  // not read
+  }
   if (int e = encode_tiled_2d(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_codes, (uint64_t)Hkv * (HD / 2), (uint64_t)B * Tp,
                               (uint64_t)Hkv * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
@@ -715,6 +818,8 @@ extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scale
   AttnArgs a{};
   a.qsf = q_scales;
   a.gq = q_g;
+  a.qsf_lo = q_scales_lo;
+  a.gq_lo = q_g_lo;
   a.ksf = k_scales;
   a.gk = k_g;
   a.out = out;
@@ -726,21 +831,32 @@ extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scale
   a.causal = causal ? 1 : 0;
   a.scale_log2 = scaling * 1.4426950408889634f;
   a.units = B * Hq * (Tp / 128);
-  a.trace = g_trace;
+  // the event timeline is recorded by the single-slice kernel only
+  a.trace = (dq || dual_p) ? nullptr : g_trace;
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                        AttnArgs);
+  static const Kern kerns[5] = {fp4_attn_kernel<false, false, false>, fp4_attn_kernel<false, true, false>,
+                                fp4_attn_kernel<false, false, true>, fp4_attn_kernel<false, true, true>,
+                                fp4_attn_kernel<true, false, false>};
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(fp4_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    cudaFuncSetAttribute(fp4_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    for (Kern k : kerns) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr = true;
   }
+  const Kern kern = a.trace ? kerns[4] : kerns[(dq ? 1 : 0) + (dual_p ? 2 : 0)];
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int grid = num_ctas > 0 ? num_ctas : sms;
   if (grid > a.units) grid = a.units;
-  if (a.trace)
-    fp4_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mvh, mvl, a);
-  else
-    fp4_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mvh, mvl, a);
+  kern<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mql, mk, mvh, mvl, a);
   return check_launch("fp4_attn_kernel");
+}
+
+extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                                  const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                                  const uint16_t* v_hi, const uint16_t* v_lo, float* out, int B, int Hq, int Hkv,
+                                  int T, int Tp, int D, int causal, float scaling, int num_ctas, void* stream) {
+  return fp4attn_fwd_packed_dual(q_codes, q_scales, q_g, nullptr, nullptr, nullptr, k_codes, k_scales, k_g, v_hi, v_lo,
+                                 out, B, Hq, Hkv, T, Tp, D, causal, scaling, 0, num_ctas, stream);
 }

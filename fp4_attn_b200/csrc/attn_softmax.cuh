@@ -159,4 +159,112 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk
   for (int i = 0; i < 32; i += 2) lsum2[(i >> 1) & 3] = add2(lsum2[(i >> 1) & 3], pk2(e[i], e[i + 1]));
 }
 
+// ---------------------------------------------------------------- dual-slice P
+// The reference's dual_nvfp4 on P (fp4_quant_utils.py:307-315 via
+// llama_patch.py:84-95): hi = qdq(P), lo = qdq(P - hi), both row-aligned
+// (global scale = the row's max |.|), P-hat = hi + lo.  In the kernel's units
+// (e = P / rowmax P) hi is the single-slice code * scale; the residual's row
+// global scale gr = rowmax |e - hi| comes from an extra pass (chunk_rmax), and
+// lo = (E2M1(x * rcp(s')) * s') * gr with x = (e - hi) * recip(gr) and
+// s' = E4M3(max_block |x| * recip(6)), as fp4_quant_utils.py:118-169 does.
+
+// e = exp2(z*u - m*u) of one 32-key chunk (keys with column > lim zeroed when MASK).
+template <bool MASK>
+__device__ __forceinline__ void chunk_e(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
+                                        uint64_t nmu2, float (&e)[32]) {
+  const float4* g4 = reinterpret_cast<const float4*>(gk);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) exp4(a + 4 * q, g4[q], u2, nmu2, e + 4 * q);
+  if constexpr (MASK) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
+  }
+}
+
+// hi slice of 16 values: fp16 pairs code * scale (exact), as chunk_p forms them.
+__device__ __forceinline__ void slice_hi(const float* eb, const float* rcp, float r6, uint32_t (&hp)[8]) {
+  uint64_t rs2;
+  uint32_t s14;
+  block_scale(eb, rcp, r6, rs2, s14);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    float x0, x1;
+    upk2(mul2(pk2(eb[i], eb[i + 1]), rs2), x0, x1);
+    hp[i / 2] = quant_pair_f16(x0, x1, s14);
+  }
+}
+
+__device__ __forceinline__ float2 f16x2_to_f32(uint32_t h) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// Residual pass on one 32-key chunk: running max of |e - hi|.
+template <bool MASK>
+__device__ __forceinline__ float chunk_rmax(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
+                                            uint64_t nmu2, const float* rcp, float r6, float rm) {
+  float e[32];
+  chunk_e<MASK>(a, gk, col0, lim, u2, nmu2, e);
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    uint32_t hp[8];
+    slice_hi(e + 16 * blk, rcp, r6, hp);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 h = f16x2_to_f32(hp[i]);
+      rm = max3f(rm, fabsf(e[16 * blk + 2 * i] - h.x), fabsf(e[16 * blk + 2 * i + 1] - h.y));
+    }
+  }
+  return rm;
+}
+
+// Final pass of dual-slice P on one 32-key chunk: running sum of e, then
+// P-hat = hi + lo per key, rounded to fp16 pairs (pk).  rg = recip(gr).
+template <bool MASK>
+__device__ __forceinline__ void chunk_p_dual(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
+                                             uint64_t nmu2, const float* rcp, float r6, float rg, float gr,
+                                             uint64_t (&lsum2)[4], uint32_t (&pk)[16]) {
+  float e[32];
+  chunk_e<MASK>(a, gk, col0, lim, u2, nmu2, e);
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) lsum2[(i >> 1) & 3] = add2(lsum2[(i >> 1) & 3], pk2(e[i], e[i + 1]));
+  const uint64_t rg2 = pk2(rg, rg), gr2 = pk2(gr, gr);
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    const float* eb = e + 16 * blk;
+    uint32_t hp[8];
+    slice_hi(eb, rcp, r6, hp);
+    float xr[16];
+    float am = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 h = f16x2_to_f32(hp[i]);
+      upk2(mul2(add2(pk2(eb[2 * i], eb[2 * i + 1]), pk2(-h.x, -h.y)), rg2), xr[2 * i], xr[2 * i + 1]);
+      am = max3f(am, fabsf(xr[2 * i]), fabsf(xr[2 * i + 1]));
+    }
+    const uint32_t sb = e4m3_satfinite(am * r6);
+    const float rs = rcp[sb & 127];
+    const uint64_t rs2 = pk2(rs, rs);
+    uint32_t s2;
+    asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(s2) : "r"(sb * 0x101u));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float x0, x1;
+      upk2(mul2(pk2(xr[2 * i], xr[2 * i + 1]), rs2), x0, x1);
+      uint32_t qs;  // (E2M1(x) * s') as fp16 pair, exact, signed
+      asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\t"
+          "cvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+          : "=r"(qs)
+          : "f"(x0), "f"(x1));
+      qs = hmul2_u32(qs, s2);
+      const float2 lq = f16x2_to_f32(qs);
+      const float2 h = f16x2_to_f32(hp[i]);
+      float p0, p1;
+      upk2(add2(pk2(h.x, h.y), mul2(pk2(lq.x, lq.y), gr2)), p0, p1);
+      uint32_t w;
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(p1), "f"(p0));
+      pk[8 * blk + i] = w;
+    }
+  }
+}
+
 }  // namespace fp4

@@ -6,4 +6,5 @@ int quant_dispatch_bf16(const QuantArgs& p, int arith, int out_dtype, float* g, 
                         cudaStream_t st) {
   return dispatch_arith<FP4_DT_BF16>(p, arith, out_dtype, g, gsf_max, what, st);
 }
+int quant_dual_bf16(const QuantArgs& p, cudaStream_t st) { return launch_rows_dual<FP4_DT_BF16>(p, st); }
 }  // namespace fp4

@@ -6,4 +6,5 @@ int quant_dispatch_f32(const QuantArgs& p, int arith, int out_dtype, float* g, f
                         cudaStream_t st) {
   return dispatch_arith<FP4_DT_F32>(p, arith, out_dtype, g, gsf_max, what, st);
 }
+int quant_dual_f32(const QuantArgs& p, cudaStream_t st) { return launch_rows_dual<FP4_DT_F32>(p, st); }
 }  // namespace fp4

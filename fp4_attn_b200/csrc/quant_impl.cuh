@@ -51,6 +51,11 @@ struct QuantArgs {
   int64_t scales_ld;  // linear: bytes per row; tcgen05: 4-block groups per row
   void* out;
   int64_t out_ld;  // elements per output row
+  // dual-slice row mode (quant_rows_vec_kernel<..., DUAL>): the second slice's
+  // codes / scales (same layouts as codes / scales) and per-row g
+  uint8_t* codes_lo;
+  uint8_t* scales_lo;
+  float* g_row_lo;
 };
 
 template <int DT, int A>
@@ -165,7 +170,7 @@ __device__ __forceinline__ uint32_t e2m1x8(const float* v) {
 // (row and tensor modes; none mode runs with g = rg = 1, which is exact).
 template <int A, int ODT, bool COLG, bool OUT>
 __device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int64_t orow, int kb, float g, float rg,
-                                            const float* rcp_tab) {
+                                            const float* rcp_tab, uint32_t* wout = nullptr, float* sout = nullptr) {
   const float r6 = recip<A>(6.0f);
   if constexpr (COLG) {
 #pragma unroll
@@ -192,6 +197,11 @@ __device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int
   uint32_t w[2];
   w[0] = nan_block ? 0u : e2m1x8(v);
   w[1] = nan_block ? 0u : e2m1x8(v + 8);
+  if (wout) {  // the block's codes and scale, for a caller that needs the dequantized values
+    wout[0] = w[0];
+    wout[1] = w[1];
+    *sout = s;
+  }
   if (p.codes) {
     *reinterpret_cast<uint2*>(p.codes + orow * p.codes_ld + (int64_t)kb * 8) = make_uint2(w[0], w[1]);
   }
@@ -450,11 +460,24 @@ __device__ __forceinline__ void unpack_raw(float v[16], const RawBlock<DT>& r) {
 // group's raw vectors before it quantizes the current one, so a thread keeps
 // one row's bytes in flight while it computes.  Same arithmetic as
 // quant_rows_kernel (quant_block).
-template <int DT, int A, int ODT, int TPR, bool OUT>
+// x - (code * s) * g for the 16 values of a block quantized to (w, s) under g:
+// the residual dual_nvfp4 quantizes second (fp4_quant_utils.py:313-315).
+template <int A>
+__device__ __forceinline__ void block_residual(float v[16], const uint32_t w[2], float s, float g) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    v[j] = __fsub_rn(v[j], mul<A>(mul<A>(e2m1_value((w[j >> 3] >> (4 * (j & 7))) & 15u), s), g));
+}
+
+// DUAL (row mode only): after the first slice, the same row-mode quantizer
+// runs on the fp32 residual x - dequant(first slice), held in registers as
+// the raw block and the first slice's codes, into codes_lo / scales_lo / g_row_lo.
+template <int DT, int A, int ODT, int TPR, bool OUT, bool DUAL = false>
 __global__ void __launch_bounds__(kVecThreads, 3) quant_rows_vec_kernel(QuantArgs p) {
   constexpr int ROWS = kVecThreads / TPR;
   constexpr int WPR = TPR / 32;
   __shared__ float red[2][kVecThreads / 32];
+  __shared__ float red2[2][kVecThreads / 32];
   __shared__ float rcp_tab[128];
   if (threadIdx.x < 128) rcp_tab[threadIdx.x] = recip<A>(e4m3_to_f32((uint8_t)threadIdx.x));
   __syncthreads();
@@ -477,6 +500,8 @@ __global__ void __launch_bounds__(kVecThreads, 3) quant_rows_vec_kernel(QuantArg
     }
   };
   RawBlock<DT> cur[2], nxt[2];
+  uint32_t whi[2][2] = {{0u, 0u}, {0u, 0u}};  // DUAL: first-slice codes and scales of this thread's blocks
+  float shi[2] = {0.0f, 0.0f};
   int64_t base = (int64_t)blockIdx.x * ROWS;
   {
     const int64_t orow = base + rloc;
@@ -544,13 +569,80 @@ __global__ void __launch_bounds__(kVecThreads, 3) quant_rows_vec_kernel(QuantArg
           if (i < nmine) {
             float v[16];
             unpack_raw<DT, A>(v, cur[i]);
-            quant_block<A, ODT, false, OUT>(v, p, orow, lane + i * TPR, g, rg, rcp_tab);
+            if constexpr (DUAL) quant_block<A, ODT, false, OUT>(v, p, orow, lane + i * TPR, g, rg, rcp_tab, whi[i], &shi[i]);
+            else quant_block<A, ODT, false, OUT>(v, p, orow, lane + i * TPR, g, rg, rcp_tab);
           }
+      }
+    }
+    if constexpr (DUAL) {
+      float m = 0.0f;
+      if (!pad_row) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (i < nmine) {
+            float v[16];
+            unpack_raw<DT, A>(v, cur[i]);
+            block_residual<A>(v, whi[i], shi[i], g);
+            m = nanmax(m, block_absmax(v));
+          }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (WPR > 1) {
+        if ((threadIdx.x & 31) == 0) red2[it & 1][threadIdx.x / 32] = m;
+        __syncthreads();
+        m = red2[it & 1][rloc * WPR];
+#pragma unroll
+        for (int w = 1; w < WPR; ++w) m = nanmax(m, red2[it & 1][rloc * WPR + w]);
+      }
+      const float g2 = m;
+      if (p.g_row_lo && lane == 0 && live) p.g_row_lo[orow] = pad_row ? 0.0f : g2;
+      if (live) {
+        QuantArgs pl = p;
+        pl.codes = p.codes_lo;
+        pl.scales = p.scales_lo;
+        if (pad_row) {
+          for (int kb = lane; kb < nblk; kb += TPR) {
+            *reinterpret_cast<uint2*>(pl.codes + orow * pl.codes_ld + (int64_t)kb * 8) = make_uint2(0u, 0u);
+            pl.scales[pl.scale_layout ? sf_tcgen05_offset(orow, kb, pl.scales_ld) : orow * pl.scales_ld + kb] = 0;
+          }
+        } else {
+          const float rg2 = recip<A>(g2);
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            if (i < nmine) {
+              float v[16];
+              unpack_raw<DT, A>(v, cur[i]);
+              block_residual<A>(v, whi[i], shi[i], g);
+              quant_block<A, ODT, false, false>(v, pl, orow, lane + i * TPR, g2, rg2, rcp_tab);
+            }
+        }
       }
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) cur[i] = nxt[i];
   }
+}
+
+// Dual-slice row mode (fp32 arithmetic) on the persistent row kernel; -1 when
+// the layout is not one it takes (unaligned rows, more than 512 blocks a row).
+template <int DT>
+static int launch_rows_dual(const QuantArgs& p, cudaStream_t st) {
+  constexpr int A = FP4_ARITH_F32;
+  const int64_t n = (int64_t)p.H * p.D;
+  const int64_t nblk = (n + 15) / 16;
+  const int64_t nrows = (int64_t)p.B * p.T_pad;
+  if (!(p.vec && n % 16 == 0 && nblk <= 256 * 2 && (p.H == 1 || p.D % 16 == 0))) return -1;
+  const int tpr = nblk <= 64 ? 32 : nblk <= 128 ? 64 : nblk <= 256 ? 128 : 256;
+  const int64_t groups = (nrows + (kVecThreads / tpr) - 1) / (kVecThreads / tpr);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(groups, 148 * 3));
+  switch (tpr) {
+    case 32: quant_rows_vec_kernel<DT, A, A, 32, false, true><<<grid, kVecThreads, 0, st>>>(p); break;
+    case 64: quant_rows_vec_kernel<DT, A, A, 64, false, true><<<grid, kVecThreads, 0, st>>>(p); break;
+    case 128: quant_rows_vec_kernel<DT, A, A, 128, false, true><<<grid, kVecThreads, 0, st>>>(p); break;
+    default: quant_rows_vec_kernel<DT, A, A, 256, false, true><<<grid, kVecThreads, 0, st>>>(p); break;
+  }
+  return check_launch("quant_rows_vec_kernel(dual)");
 }
 
 template <int DT, int A, int ODT, bool COLG, bool OUT>
@@ -656,5 +748,9 @@ unsigned int quant_status(bool reset);
 int quant_dispatch_f32(const QuantArgs& p, int arith, int out_dtype, float* g, float gsf_max, int what, cudaStream_t st);
 int quant_dispatch_bf16(const QuantArgs& p, int arith, int out_dtype, float* g, float gsf_max, int what, cudaStream_t st);
 int quant_dispatch_f16(const QuantArgs& p, int arith, int out_dtype, float* g, float gsf_max, int what, cudaStream_t st);
+// dual-slice row mode (launch_rows_dual); -1 when the layout is not supported
+int quant_dual_f32(const QuantArgs& p, cudaStream_t st);
+int quant_dual_bf16(const QuantArgs& p, cudaStream_t st);
+int quant_dual_f16(const QuantArgs& p, cudaStream_t st);
 
 }  // namespace fp4

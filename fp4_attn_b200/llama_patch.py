@@ -39,11 +39,10 @@ from .attention import fp4_attention_fwd
 _ORIGINAL = None
 
 
-def _dual_requested(name: str) -> bool:
-    v = os.getenv(name)
-    if v is None:
-        return False
-    return v.strip().lower() == "true"
+def dual_enabled(name: str) -> bool:
+    """The reference's reading of its dual-slice switches (llama_patch.py:84,183):
+    os.getenv(name, 'true').lower() == 'true' -- unset means dual."""
+    return os.getenv(name, "true").lower() == "true"
 
 
 def _check_mask(mask: torch.Tensor | None, T: int, S: int) -> None:
@@ -62,9 +61,13 @@ def _check_mask(mask: torch.Tensor | None, T: int, S: int) -> None:
 
 
 def fp4_eager_attention(module, query, key, value, attention_mask, scaling, dropout=0.0, **kwargs):
-    """eager_attention_forward (llama_patch.py:57-105) on the FP4 kernel: ([B, T, Hq, D], None)."""
-    if _dual_requested("FP4_USE_DUAL_QUANT_ATTN"):
-        raise NotImplementedError("dual-slice P quantization is not implemented by the FP4 kernel")
+    """eager_attention_forward (llama_patch.py:57-105) on the FP4 kernel: ([B, T, Hq, D], None).
+
+    Takes the unquantized post-RoPE query/key/value: the Q/K/V fake-quant of
+    llama_patch.py:183-196 runs inside the kernel call, with dual-slice Q and P
+    as FP4_USE_DUAL_QUANT_Q / FP4_USE_DUAL_QUANT_ATTN say (both dual when unset,
+    as in the reference).
+    """
     if dropout and getattr(module, "training", False):
         raise NotImplementedError("attention dropout is not supported")
     B, Hq, T, D = query.shape
@@ -72,7 +75,8 @@ def fp4_eager_attention(module, query, key, value, attention_mask, scaling, drop
     if S != T:
         raise NotImplementedError(f"prefill only: query length {T} != key length {S}")
     _check_mask(attention_mask, T, S)
-    out = fp4_attention_fwd(query, key, value, causal=True, scaling=float(scaling))
+    out = fp4_attention_fwd(query, key, value, causal=True, scaling=float(scaling),
+                            dual_q=dual_enabled("FP4_USE_DUAL_QUANT_Q"), dual_p=dual_enabled("FP4_USE_DUAL_QUANT_ATTN"))
     return out.to(query.dtype), None
 
 
@@ -85,8 +89,6 @@ def llama_fp4_attention_forward(self, hidden_states, position_embeddings=None, a
     """LlamaAttention.forward with FP4 attention (llama_patch.py:108-250, post-RoPE quantization)."""
     from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
-    if _dual_requested("FP4_USE_DUAL_QUANT_Q"):
-        raise NotImplementedError("dual-slice Q quantization is not implemented by the FP4 kernel")
     if "past_key_value" in kwargs and past_key_values is None:  # older transformers keyword
         past_key_values = kwargs.pop("past_key_value")
     input_shape = hidden_states.shape[:-1]

@@ -106,13 +106,11 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
                       v_scale_mode: str = "token") -> torch.Tensor:
     """Q/K/V fake-quant + FP4 attention (llama_patch.py:57-105, 167-196): [B,Hq,T,D] -> fp32 [B,T,Hq,D].
 
-    dual_q / dual_p (residual two-slice quantization) and V scales other than
-    per token (the reference's global_scale_aligned=False) are not
-    implemented by the kernel and raise.
+    dual_q / dual_p: the reference's residual two-slice quantization of Q / P
+    (dual_nvfp4, fp4_quant_utils.py:307-315).  V scales other than per token
+    (the reference's global_scale_aligned=False) are not implemented and raise.
     """
     from .attention import fp4_attention_fwd as fwd
-    if dual_q or dual_p:
-        raise NotImplementedError("dual-slice Q/P quantization is not implemented by the FP4 attention kernel")
     if v_scale_mode != "token":
         raise NotImplementedError("V is quantized along tokens with a per-token global scale only")
-    return fwd(q, k, v, causal=causal, scaling=scaling)
+    return fwd(q, k, v, causal=causal, scaling=scaling, dual_q=dual_q, dual_p=dual_p)

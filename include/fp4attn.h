@@ -112,6 +112,18 @@ int fp4q_quantize(const void* x, int in_dtype, int B, int T, int H, int D, int64
                   uint8_t* scales, int scale_layout, int64_t scales_ld, float* g, void* out, int out_dtype,
                   int64_t out_ld, void* stream);
 
+/* Dual-slice row mode in one pass (dual_nvfp4 without search,
+ * fp4_quant_utils.py:307-315, on the row-aligned quantizer): slice 1 as
+ * fp4q_quantize gmode 1 (fp32 arithmetic) into codes / scales / g, slice 2 =
+ * the same quantizer on the fp32 residual x - dequant(slice 1) into codes_lo /
+ * scales_lo / g_lo (same layouts).  Returns FP4ATTN_ERR_UNSUPPORTED for
+ * layouts the one-pass kernel does not take (rows not 16-byte aligned, more
+ * than 8192 columns); fp4q_quantize with an fp32 out then does the same in
+ * three steps. */
+int fp4q_quantize_dual(const void* x, int in_dtype, int B, int T, int H, int D, int64_t sB, int64_t sT, int64_t sH,
+                       int T_pad, uint8_t* codes, int64_t codes_ld, uint8_t* scales, int scale_layout,
+                       int64_t scales_ld, float* g, uint8_t* codes_lo, uint8_t* scales_lo, float* g_lo, void* stream);
+
 /* The global-scale reduction of fp4q_quantize alone (gmode 2: column, 3:
  * tensor): g = max|x| * recip(global_sf_max) in the dequant dtype, written to
  * g ([npad] or [1]).  Same input description as fp4q_quantize.  Replaces the
@@ -150,6 +162,20 @@ int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const fl
                        float* out, int B, int Hq, int Hkv, int T, int Tp, int D, int causal, float scaling,
                        int num_ctas, void* stream);
 
+/* fp4attn_fwd_packed with the reference's dual-slice options
+ * (fp4_quant_utils.py:307-315 dual_nvfp4; FP4_USE_DUAL_QUANT_Q at
+ * llama_patch.py:183-189 and FP4_USE_DUAL_QUANT_ATTN at llama_patch.py:84-95,
+ * both default true in the reference).  q_codes_lo / q_scales_lo / q_g_lo:
+ * the second (residual) Q slice, the same quantizer on Q - dequant(first
+ * slice), same layouts; NULL = single-slice Q.  dual_p != 0: P-hat = hi + lo
+ * with lo the row-aligned NVFP4 fake-quant of P - hi (one more pass over the
+ * keys finds each row's residual scale). */
+int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                            const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
+                            const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g, const uint16_t* v_hi,
+                            const uint16_t* v_lo, float* out, int B, int Hq, int Hkv, int T, int Tp, int D,
+                            int causal, float scaling, int dual_p, int num_ctas, void* stream);
+
 /* Workspace of fp4attn_forward for a shape: writes the byte offsets of its
  * eight pieces -- Q codes, Q scale atoms, Q g, K codes, K scale atoms, K g,
  * V-hat hi plane, V-hat lo plane, each 256-byte aligned, laid out as steps 1
@@ -157,6 +183,15 @@ int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const fl
  * total size in bytes; -1 for a bad shape.  No reference counterpart: the
  * reference materialises the fake-quantized tensors in torch instead. */
 int64_t fp4attn_workspace_layout(int B, int Hq, int Hkv, int T, int D, int64_t* offsets);
+
+/* Flags of fp4attn_forward_ex / fp4attn_workspace_layout_ex. */
+#define FP4ATTN_DUAL_Q 1 /* dual-slice Q (FP4_USE_DUAL_QUANT_Q=true) */
+#define FP4ATTN_DUAL_P 2 /* dual-slice P (FP4_USE_DUAL_QUANT_ATTN=true) */
+
+/* fp4attn_workspace_layout with flags: offsets[0..11], the eight pieces
+ * above, then (FP4ATTN_DUAL_Q only; empty otherwise) the residual Q slice's
+ * codes, scale atoms and g, and an fp32 [B*Tp][Hq*D] scratch. */
+int64_t fp4attn_workspace_layout_ex(int B, int Hq, int Hkv, int T, int D, int flags, int64_t* offsets);
 
 /* Steps 1-3 as one call: q [B,Hq,T,D], k and v [B,Hkv,T,D] in in_dtype
  * (FP4_DT_F32 / BF16 / F16) with element strides (sB, sH, sT) each and d
@@ -168,6 +203,15 @@ int fp4attn_forward(const void* q, const void* k, const void* v, int in_dtype, i
                     int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH, int64_t k_sT, int64_t v_sB,
                     int64_t v_sH, int64_t v_sT, int causal, float scaling, float* out, void* workspace,
                     int64_t workspace_bytes, void* stream);
+
+/* fp4attn_forward with flags (FP4ATTN_DUAL_Q, FP4ATTN_DUAL_P): the reference's
+ * dual-slice Q and / or P.  workspace: fp4attn_workspace_layout_ex(..., flags)
+ * bytes.  With FP4ATTN_DUAL_Q the second Q slice is the row-mode quantizer on
+ * the fp32 residual Q - dequant(first slice), bit-exact to dual_nvfp4. */
+int fp4attn_forward_ex(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv, int T, int D,
+                       int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH, int64_t k_sT,
+                       int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling, int flags, float* out,
+                       void* workspace, int64_t workspace_bytes, void* stream);
 
 /* fp4attn_forward without a caller workspace; allocates no device memory.
  * No counterpart in the reference.  For callers that cannot hand the library

@@ -97,3 +97,83 @@ def test_attention_llama3_8b_shape_full():
     ref, flags = tp.attention_with_margins(q, k, v, True, delta=DELTA)
     cos, worst = check(o, ref, flags)
     print(f"config2: cosine {cos:.9f}, max-abs/RMS on decided rows {worst:.3e}, masked {flags.float().mean():.4f}")
+
+
+# ---------------------------------------------------------------- dual-slice Q / P
+def _run_dual(q, k, v, causal, dual_q, dual_p, workspace=None):
+    from fp4_attn_b200.attention import fp4_attention_fwd
+    from fp4_attn_b200.gemm import device_status
+    dev = torch.device("cuda", 0)
+    o = fp4_attention_fwd(q.to(dev), k.to(dev), v.to(dev), causal=causal, dual_q=dual_q, dual_p=dual_p,
+                          workspace=workspace).cpu()
+    assert device_status() == 0
+    return o
+
+
+def test_attention_dual_p_against_reference_goldens():
+    """The reference's own outputs with FP4_USE_DUAL_QUANT_ATTN=true (tests/golden/attention.npz), head_dim 128."""
+    z = np.load(os.path.join(GOLD, "attention.npz"))
+    idx = json.loads(bytes(z["index"]).decode())
+    ran = 0
+    for c in idx:
+        if not c["dual_p"] or c["D"] != 128:
+            continue
+        q, k, v = (torch.from_numpy(z[c["inputs"] + s]).view(torch.bfloat16) for s in ("_q", "_k", "_v"))
+        o = _run_dual(q, k, v, c["causal"], False, True)
+        _, flags = tp.attention_with_margins(q, k, v, c["causal"], delta=DELTA)
+        check(o, torch.from_numpy(z[c["key"] + "_o"]), flags)
+        ran += 1
+    assert ran >= 3
+
+
+@pytest.mark.parametrize("dual_q,dual_p", [(True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("B,Hq,Hkv,T,causal", [(1, 4, 2, 384, True), (2, 2, 1, 200, True), (1, 2, 2, 256, False)])
+def test_attention_dual_against_oracle(B, Hq, Hkv, T, causal, dual_q, dual_p):
+    """Dual-slice Q and/or P (the reference's defaults) against oracle.torch_port.attention(dual_q, dual_p)."""
+    g = torch.Generator().manual_seed(B * 977 + Hq * 31 + T + 7 * dual_q + 3 * dual_p)
+    q = torch.randn(B, Hq, T, 128, generator=g).bfloat16()
+    k = torch.randn(B, Hkv, T, 128, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, T, 128, generator=g).bfloat16()
+    o = _run_dual(q, k, v, causal, dual_q, dual_p)
+    ref = tp.attention(q, k, v, causal, dual_q=dual_q, dual_p=dual_p)
+    _, flags = tp.attention_with_margins(q, k, v, causal, delta=DELTA)
+    check(o, ref, flags)
+
+
+@pytest.mark.parametrize("strided", [False, True])
+def test_dual_q_slices_bit_exact(strided):
+    """Both Q slices against the C oracle: slice 1 = row mode on Q, slice 2 = row mode on the fp32 Q - slice 1.
+
+    strided=False takes the one-pass dual quantizer; a token stride of 129
+    elements (rows not 16-byte aligned) takes the three-step path.
+    """
+    from fp4_attn_b200.attention import AttentionWorkspace
+    B, Hq, Hkv, T, D = 2, 4, 2, 200, 128
+    g = torch.Generator().manual_seed(91)
+    q = (torch.randn(B, Hq, T, D + (1 if strided else 0), generator=g) * 3).bfloat16()
+    k = torch.randn(B, Hkv, T, D, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, T, D, generator=g).bfloat16()
+    dev = torch.device("cuda", 0)
+    qd = q.to(dev)[..., :D]
+    assert (qd.stride(2) * 2) % 16 == (2 if strided else 0)
+    q = q[..., :D]
+    ws = AttentionWorkspace(B, Hq, Hkv, T, D, dev, dual_q=True)
+    from fp4_attn_b200.attention import fp4_attention_fwd
+    from fp4_attn_b200.gemm import device_status
+    fp4_attention_fwd(qd, k.to(dev), v.to(dev), causal=True, dual_q=True, workspace=ws)
+    assert device_status() == 0
+    q2 = q.permute(0, 2, 1, 3).reshape(B * T, Hq * D).float()
+    hi, c1, s1, g1 = oq.fused_qdq(np.ascontiguousarray(q2.numpy()), "row", "float32", 1536.0)
+    _, c2, s2, g2 = oq.fused_qdq(np.ascontiguousarray(q2.numpy() - hi), "row", "float32", 1536.0)
+    Tp = ws.Tp
+    rows = (np.arange(B)[:, None] * Tp + np.arange(T)[None, :]).reshape(-1)  # workspace row of (b, t)
+    nblk = Hq * D // 16
+    r = rows[:, None]
+    kb = np.arange(nblk)[None, :]
+    off = ((r >> 7) * (nblk // 4) + (kb >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (kb & 3)
+    for qc, qs, gq, codes, scales, gl in ((ws.qc, ws.qs, ws.gq, c1, s1, g1), (ws.qc_lo, ws.qs_lo, ws.gq_lo, c2, s2, g2)):
+        np.testing.assert_array_equal(qc.cpu().numpy()[rows], codes)
+        np.testing.assert_array_equal(gq.cpu().numpy()[rows].view(np.uint32), gl.view(np.uint32))
+        np.testing.assert_array_equal(qs.cpu().numpy()[off], scales)
+    pad = np.setdiff1d(np.arange(B * Tp), rows)  # padding rows read as zeros
+    assert (ws.qc_lo.cpu().numpy()[pad] == 0).all() and (ws.gq_lo.cpu().numpy()[pad] == 0).all()

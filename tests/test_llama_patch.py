@@ -30,16 +30,40 @@ def test_install_uninstall_restores_forward():
     assert M.LlamaAttention.forward is orig
 
 
-def test_dual_quant_request_is_refused(monkeypatch):
+def test_dual_switches_read_as_the_reference_reads_them(monkeypatch):
+    """os.getenv(name, 'true').lower() == 'true' (llama_patch.py:84,183): unset means dual."""
+    for name in ("FP4_USE_DUAL_QUANT_Q", "FP4_USE_DUAL_QUANT_ATTN"):
+        monkeypatch.delenv(name, raising=False)
+        assert lp.dual_enabled(name)
+        for v, want in (("true", True), ("TRUE", True), ("false", False), ("1", False), ("", False)):
+            monkeypatch.setenv(name, v)
+            assert lp.dual_enabled(name) is want
+
+
+def test_patched_model_reaches_the_kernel_with_dual_defaults(monkeypatch):
+    """With the switches unset the patched Llama asks the kernel for dual-slice Q and P."""
     model = _tiny_model()
     ids = torch.randint(0, 64, (1, 8))
-    monkeypatch.setenv("FP4_USE_DUAL_QUANT_Q", "true")
+    seen = []
+
+    def fake(q, k, v, causal=True, scaling=None, dual_q=False, dual_p=False):
+        seen.append((dual_q, dual_p))
+        raise RuntimeError("stop before the GPU")
+
+    monkeypatch.delenv("FP4_USE_DUAL_QUANT_Q", raising=False)
+    monkeypatch.setenv("FP4_USE_DUAL_QUANT_ATTN", "true")
+    monkeypatch.setattr(lp, "fp4_attention_fwd", fake)
     lp.install()
     try:
-        with pytest.raises(NotImplementedError):
+        with pytest.raises(RuntimeError, match="stop before"):
+            model(ids)
+        monkeypatch.setenv("FP4_USE_DUAL_QUANT_Q", "false")
+        monkeypatch.setenv("FP4_USE_DUAL_QUANT_ATTN", "false")
+        with pytest.raises(RuntimeError, match="stop before"):
             model(ids)
     finally:
         lp.uninstall()
+    assert seen == [(True, True), (False, False)]
 
 
 def test_cpu_tensors_are_refused():
@@ -75,7 +99,7 @@ def test_nvfp4sim_new_exports_refuse_unimplemented_modes():
     for name in ("quantize_nvfp4", "dequantize_nvfp4", "qdq_nvfp4", "fp4_attention_fwd"):
         assert callable(getattr(nvfp4sim, name))
     q = torch.randn(1, 2, 16, 128)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="CUDA"):  # dual modes exist; no CPU path
         nvfp4sim.fp4_attention_fwd(q, q[:, :1], q[:, :1], dual_p=True)
     with pytest.raises(NotImplementedError):
         nvfp4sim.fp4_attention_fwd(q, q[:, :1], q[:, :1], v_scale_mode="channel")

@@ -16,9 +16,17 @@ from oracle import torch_port as tp
 pytestmark = pytest.mark.gpu
 
 
-def test_patched_llama_matches_oracle_per_layer(monkeypatch):
+@pytest.mark.parametrize("dual", [False, True])
+def test_patched_llama_matches_oracle_per_layer(monkeypatch, dual):
+    """dual=True leaves FP4_USE_DUAL_QUANT_Q / _ATTN unset: the reference's default, dual-slice Q and P."""
     from transformers import LlamaConfig, LlamaForCausalLM
     from fp4_attn_b200.attention import fp4_attention_fwd
+
+    for name in ("FP4_USE_DUAL_QUANT_Q", "FP4_USE_DUAL_QUANT_ATTN"):
+        if dual:
+            monkeypatch.delenv(name, raising=False)
+        else:
+            monkeypatch.setenv(name, "false")
 
     cfg = LlamaConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=4,
                       num_key_value_heads=2, head_dim=128, vocab_size=256, max_position_embeddings=512,
@@ -34,9 +42,11 @@ def test_patched_llama_matches_oracle_per_layer(monkeypatch):
 
     def checked(module, q, k, v, mask, scaling, dropout=0.0, **kw):
         lp._check_mask(mask, q.shape[2], k.shape[2])
-        o = fp4_attention_fwd(q, k, v, causal=True, scaling=float(scaling))
-        ref, flags = tp.attention_with_margins(q.float().cpu(), k.float().cpu(), v.float().cpu(), True,
-                                               float(scaling), delta=DELTA)
+        o = fp4_attention_fwd(q, k, v, causal=True, scaling=float(scaling), dual_q=dual, dual_p=dual)
+        qc, kc, vc = q.float().cpu(), k.float().cpu(), v.float().cpu()
+        ref, flags = tp.attention_with_margins(qc, kc, vc, True, float(scaling), delta=DELTA)
+        if dual:
+            ref = tp.attention(qc, kc, vc, True, float(scaling), dual_q=True, dual_p=True)
         results.append(check(o.cpu(), ref, flags))
         return o.to(q.dtype), None
 

@@ -29,7 +29,7 @@ FP4_DEFINE_STATUS_READER(quant_status)
 namespace {
 
 constexpr int QF_THREADS = 1024;
-constexpr int QF_PIECES = 4;  // bulk copies per slice, each with its own barrier
+constexpr int QF_PIECES = 8;  // bulk copies per slice, each with its own barrier (the max runs as they land)
 constexpr int QF_SMEM_MAX = 232448 - 1024;  // dynamic shared memory for the slice (sm_100 limit minus headroom)
 
 struct QFArgs {
@@ -42,27 +42,47 @@ struct QFArgs {
   float gsf_max;
 };
 
-// Bounded spin until *w >= target (volatile reads); false after 2 s.
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* w) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(w) : "memory");
+  return v;
+}
+// Every memory operation of this thread before it is visible before the increment.
+__device__ __forceinline__ void add_release(unsigned int* w, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(w), "r"(v) : "memory");
+}
+
+// Bounded spin until *w >= target (acquire loads: what the arriving threads
+// wrote before their release is visible afterwards); false after 2 s.
 __device__ bool wait_count(const unsigned int* w, unsigned int target, unsigned int site) {
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 0;; ++i) {
-    if (*reinterpret_cast<const volatile unsigned int*>(w) >= target) return true;
+    if (ld_acquire(w) >= target) return true;
     if ((i & 63) == 63) {
       if (dev_failed()) return false;
       if (globaltimer() - t0 > kWaitNs) {
         dev_fail(site);
         return false;
       }
-      __nanosleep(64);
     }
   }
+}
+
+// Per 16-bit lane: max(|a|, |b|) in the input type, NaN winning (max.NaN), exact.
+template <int DT>
+__device__ __forceinline__ uint32_t absmax_x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (DT == FP4_DT_BF16)
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a & 0x7FFF7FFFu), "r"(b & 0x7FFF7FFFu));
+  else
+    asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a & 0x7FFF7FFFu), "r"(b & 0x7FFF7FFFu));
+  return r;
 }
 
 template <int DT>
 __global__ void __launch_bounds__(QF_THREADS, 1) quant_tensor_fused_kernel(QFArgs p) {
   using T = typename In<DT>::T;
   constexpr int A = FP4_ARITH_F32;
-  constexpr int PER = 16 / (int)sizeof(T);  // elements per 16-byte vector
   extern __shared__ __align__(128) uint8_t qf_slice[];
   __shared__ __align__(8) uint64_t bar[QF_PIECES];
   __shared__ float wmax[QF_THREADS / 32];
@@ -98,8 +118,10 @@ __global__ void __launch_bounds__(QF_THREADS, 1) quant_tensor_fused_kernel(QFArg
       }
     }
   }
-  // ---- maximum of |x| over the slice (torch.max semantics: NaN wins), piece by piece as it lands
+  // ---- maximum of |x| over the slice (torch.max semantics: NaN wins), piece by piece as it lands.
+  // 16-bit inputs: on packed pairs in the input type (|x| by clearing the sign bits, exact), widened once at the end.
   float m = 0.0f;
+  uint32_t m2 = 0u;
   const uint4* s4 = reinterpret_cast<const uint4*>(qf_slice);
   bool loaded = true;
   for (int k = 0; k < QF_PIECES; ++k) {
@@ -108,10 +130,17 @@ __global__ void __launch_bounds__(QF_THREADS, 1) quant_tensor_fused_kernel(QFArg
     const int v1 = (k + 1) * pv < nv ? (k + 1) * pv : nv;
     for (int i = k * pv + threadIdx.x; i < v1; i += QF_THREADS) {
       const uint4 u = s4[i];
-      const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-      for (int j = 0; j < PER; ++j) m = nanmax(m, fabsf(rnd<A>(In<DT>::f(e[j]))));
+      if constexpr (sizeof(T) == 2) {
+        m2 = absmax_x2<DT>(m2, absmax_x2<DT>(absmax_x2<DT>(u.x, u.y), absmax_x2<DT>(u.z, u.w)));
+      } else {
+        const float* e = reinterpret_cast<const float*>(&u);
+        m = nanmax(m, nanmax(absmax3(e[0], e[1], e[2]), fabsf(e[3])));
+      }
     }
+  }
+  if constexpr (sizeof(T) == 2) {
+    const T* h = reinterpret_cast<const T*>(&m2);
+    m = nanmax(In<DT>::f(h[0]), In<DT>::f(h[1]));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -121,65 +150,83 @@ __global__ void __launch_bounds__(QF_THREADS, 1) quant_tensor_fused_kernel(QFArg
 #pragma unroll
     for (int w = 1; w < QF_THREADS / 32; ++w) m = nanmax(m, wmax[w]);
     atomicMax(&cw[0], __float_as_uint(m));
-    __threadfence();
-    atomicAdd(&cw[1], 1u);
+    add_release(&cw[1], 1u);  // arrival, after the max
     bool ok = loaded && wait_count(&cw[1], G, 0x302);
-    __threadfence();
-    const float mx = __uint_as_float(*reinterpret_cast<const volatile unsigned int*>(&cw[0]));
+    const float mx = __uint_as_float(ld_acquire(&cw[0]));
     const float g = mul<A>(mx, recip<A>(rnd<A>(p.gsf_max)));  // fp4_quant_utils.py:139
     s_g = g;
     s_rg = recip<A>(g);
-    __threadfence();
-    atomicAdd(&cw[2], 1u);
+    add_release(&cw[2], 1u);  // departure, after reading the max
     s_ok = ok ? 1 : 0;
   }
   __syncthreads();
   if (!s_ok) return;
-  // ---- quantize from shared memory: lanes 2i and 2i+1 hold the two halves of a block
+  // ---- quantize from shared memory: lanes 2i and 2i+1 hold the two halves of a block;
+  // each thread takes two halves per step (independent chains the scheduler interleaves)
   const float rg = s_rg, r6 = recip<A>(6.0f);
   const int64_t b0 = e0 / 16;  // first block of the slice
   const int nhalf = (int)(cnt / 8);
-  for (int base = 0; base < nhalf; base += QF_THREADS) {
-    const int hidx = base + (int)threadIdx.x;
-    const bool live = hidx < nhalf;
-    float v[8];
-    if (live) {
-      if constexpr (sizeof(T) == 4) {
-        const uint4 u0 = s4[2 * hidx], u1 = s4[2 * hidx + 1];
-        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  const float2 rg2 = make_float2(rg, rg), zero2 = make_float2(0.0f, 0.0f);
+  for (int base = 0; base < nhalf; base += 2 * QF_THREADS) {
+    float2 v[2][4];  // (x, x') pairs of a half block, kept as register pairs for the f32x2 ops
+    float am[2];
+    bool live[2];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = rnd<A>(__uint_as_float(w[k]));
+    for (int u = 0; u < 2; ++u) {
+      const int hidx = base + u * QF_THREADS + (int)threadIdx.x;
+      live[u] = hidx < nhalf;
+      if (live[u]) {
+        if constexpr (sizeof(T) == 4) {
+          const uint4 u0 = s4[2 * hidx], u1 = s4[2 * hidx + 1];
+          v[u][0] = make_float2(__uint_as_float(u0.x), __uint_as_float(u0.y));
+          v[u][1] = make_float2(__uint_as_float(u0.z), __uint_as_float(u0.w));
+          v[u][2] = make_float2(__uint_as_float(u1.x), __uint_as_float(u1.y));
+          v[u][3] = make_float2(__uint_as_float(u1.z), __uint_as_float(u1.w));
+        } else {
+          const uint4 q = s4[hidx];
+          const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) v[u][k] = make_float2(In<DT>::f(e[2 * k]), In<DT>::f(e[2 * k + 1]));
+        }
       } else {
-        const uint4 u = s4[hidx];
-        const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = rnd<A>(In<DT>::f(e[k]));
+        for (int k = 0; k < 4; ++k) v[u][k] = zero2;
       }
-    } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = 0.0f;
+      for (int k = 0; k < 4; ++k) v[u][k] = __fmul2_rn(v[u][k], rg2);  // x * recip(g)
+      float a = absmax3(v[u][0].x, v[u][0].y, v[u][1].x);
+      a = absmax3(a, v[u][1].y, v[u][2].x);
+      a = absmax3(a, v[u][2].y, v[u][3].x);
+      am[u] = nanmax(a, fabsf(v[u][3].y));
     }
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) mul2(v[k], v[k + 1], rg);
-    float am = absmax3(v[0], v[1], v[2]);
-    am = absmax3(am, v[3], v[4]);
-    am = absmax3(am, v[5], v[6]);
-    am = nanmax(am, fabsf(v[7]));
-    am = nanmax(am, __shfl_xor_sync(0xffffffffu, am, 1));  // the block's other half
-    if (!live) continue;
-    const uint8_t sb = e4m3_torch(mul<A>(am, r6));
-    const float rs = rcp_tab[sb & 0x7F];
-    const bool nan_block = (sb & 0x7F) == 0x7F;
+    for (int u = 0; u < 2; ++u) am[u] = nanmax(am[u], __shfl_xor_sync(0xffffffffu, am[u], 1));  // the block's other half
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) mulz2(v[k], v[k + 1], rs);
-    const uint32_t word = nan_block ? 0u : e2m1x8(v);
-    const int64_t blk = b0 + (hidx >> 1);
-    if (blk < 2) {  // only in CTA 0 (its slice starts at block 0 and holds at least 2 blocks)
-      stash[hidx] = word;  // bytes 0..15 of codes hold the barrier words until the end
-    } else {
-      reinterpret_cast<uint32_t*>(p.codes)[2 * blk + (hidx & 1)] = word;
+    for (int u = 0; u < 2; ++u) {
+      const int hidx = base + u * QF_THREADS + (int)threadIdx.x;
+      const uint8_t sb = e4m3_torch(mul<A>(am[u], r6));
+      const float rs = rcp_tab[sb & 0x7F];
+      const bool nan_block = (sb & 0x7F) == 0x7F;
+      const float2 rs2 = make_float2(rs, rs);
+      float q[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        // x * recip(s) + 0: one rounding of the product; + 0 turns -0.0 into +0.0 (torch.sign(-0.0) == 0)
+        const float2 t = __ffma2_rn(v[u][k], rs2, zero2);
+        q[2 * k] = t.x;
+        q[2 * k + 1] = t.y;
+      }
+      const uint32_t word = nan_block ? 0u : e2m1x8(q);
+      if (live[u]) {
+        const int64_t blk = b0 + (hidx >> 1);
+        if (blk < 2) {  // only in CTA 0 (its slice starts at block 0 and holds at least 2 blocks)
+          stash[hidx] = word;  // bytes 0..15 of codes hold the barrier words until the end
+        } else {
+          reinterpret_cast<uint32_t*>(p.codes)[2 * blk + (hidx & 1)] = word;
+        }
+        if ((hidx & 1) == 0) p.scales[blk] = sb;
+      }
     }
-    if ((hidx & 1) == 0) p.scales[blk] = sb;
   }
   if (blockIdx.x == 0) {
     __syncthreads();

@@ -286,22 +286,28 @@ class AttentionWorkload:
         self.out_host = torch.empty(self.B, self.T, self.Hq, self.D).pin_memory()
         self.config["l2"] = f"rotating {self.nsets} input sets (> L2)"
 
+    use_graph = True  # each step (one C ABI call, several launches on forked streams) is a CUDA graph replay
+
     def step(self, i, ev=None):
+        """One fp4attn_forward call: Q/K quantize and V-hat prep (K and V on forked streams), then the kernel."""
         from fp4_attn_b200 import _lib
         i %= self.nsets
         q, k, v = self.sets[i]
         ws = self.ws[i]
-        A = self.A
-        A.quantize_qk(q, ws.qc, ws.qs, ws.gq, ws.Tp)
-        A.quantize_qk(k, ws.kc, ws.ks, ws.gk, ws.Tp)
-        A.prepare_v(v, ws.vhi, ws.vlo, ws.Tp)
-        if ev is not None:
-            ev[0].record()
+        _lib.call("fp4attn_forward", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], self.B,
+                  self.Hq, self.Hkv, self.T, self.D, q.stride(0), q.stride(1), q.stride(2), k.stride(0),
+                  k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), 1, self.D ** -0.5,
+                  self.out[i].data_ptr(), ws.ptr(), ws.nbytes, _lib.stream_of(q))
+
+    def kernel(self, i):
+        """The attention kernel alone on the operands step(i) prepared."""
+        from fp4_attn_b200 import _lib
+        i %= self.nsets
+        ws = self.ws[i]
         _lib.call("fp4attn_fwd_packed", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), ws.kc.data_ptr(),
                   ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), self.out[i].data_ptr(),
-                  self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, 1, self.D ** -0.5, 0, _lib.stream_of(q))
-        if ev is not None:
-            ev[1].record()
+                  self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, 1, self.D ** -0.5, 0,
+                  _lib.stream_of(self.sets[i][0]))
 
     def e2e_step(self, i):
         """Public API, host buffers: H2D q/k/v, fp4_attention_fwd, D2H the output."""

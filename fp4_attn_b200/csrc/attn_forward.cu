@@ -92,6 +92,33 @@ int q_residual(const void* x, int in_dtype, int64_t sB, int64_t sT, int64_t sH, 
   return fp4::check_launch("q_residual_kernel");
 }
 
+// Two side streams and their fork/join events for the calling host thread on
+// one device, created on first use (one set per thread, so concurrent callers
+// never wait on each other's events).  nullptr if they cannot be created.
+struct SideStreams {
+  cudaStream_t s[2];
+  cudaEvent_t fork, join[2];
+};
+
+SideStreams* side_streams() {
+  constexpr int kMaxDev = 64;
+  thread_local SideStreams tab[kMaxDev];
+  thread_local signed char state[kMaxDev] = {};  // 0 untried, 1 ready, -1 failed
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+  if (state[dev] == 0) {
+    SideStreams& t = tab[dev];
+    bool ok = cudaStreamCreateWithFlags(&t.s[0], cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&t.s[1], cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&t.fork, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&t.join[0], cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&t.join[1], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) cudaGetLastError();
+    state[dev] = ok ? 1 : -1;
+  }
+  return state[dev] == 1 ? &tab[dev] : nullptr;
+}
+
 }  // namespace
 
 extern "C" int64_t fp4attn_workspace_layout_ex(int B, int Hq, int Hkv, int T, int D, int flags, int64_t* offsets) {
@@ -138,6 +165,27 @@ extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, i
   float* gq_lo = dq ? reinterpret_cast<float*>(ws + off[10]) : nullptr;
   float* qres = dq ? reinterpret_cast<float*>(ws + off[11]) : nullptr;
   const int64_t qld = (int64_t)Hq * D;
+  // The three operand preparations are independent: K and V run on side streams
+  // forked from and joined back to the caller's stream (capturable in a CUDA graph),
+  // so the latency-bound K and V kernels overlap the Q quantization.
+  SideStreams* side = side_streams();
+  void* k_stream = stream;
+  void* v_stream = stream;
+  if (side && cudaEventRecord(side->fork, st) == cudaSuccess &&
+      cudaStreamWaitEvent(side->s[0], side->fork, 0) == cudaSuccess &&
+      cudaStreamWaitEvent(side->s[1], side->fork, 0) == cudaSuccess) {
+    k_stream = side->s[0];
+    v_stream = side->s[1];
+  } else {
+    cudaGetLastError();
+    side = nullptr;
+  }
+  if (int e = fp4q_quantize(k, in_dtype, B, T, Hkv, D, k_sB, k_sT, k_sH, Tp, 1, 0, 1536.0f, kc,
+                            (int64_t)Hkv * D / 2, ks, 1, (int64_t)Hkv * D / 64, gk, nullptr, 0, 0, k_stream))
+    return e;
+  if (int e = fp4attn_prepare_v(v, in_dtype, B, Hkv, T, D, v_sB, v_sH, v_sT, Tp, vhi, vlo, nullptr, nullptr,
+                                v_stream))
+    return e;
   // Q and K: row mode (per-token global scale) on the [B*T, H*D] views, tcgen05 scale atoms.
   // Dual-slice Q: both slices in one pass over Q when the quantizer takes the layout; otherwise
   // the first slice's dequantized values go to the fp32 scratch, Q - hi is formed there and
@@ -161,11 +209,12 @@ extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, i
         return e;
     }
   }
-  if (int e = fp4q_quantize(k, in_dtype, B, T, Hkv, D, k_sB, k_sT, k_sH, Tp, 1, 0, 1536.0f, kc,
-                            (int64_t)Hkv * D / 2, ks, 1, (int64_t)Hkv * D / 64, gk, nullptr, 0, 0, stream))
-    return e;
-  if (int e = fp4attn_prepare_v(v, in_dtype, B, Hkv, T, D, v_sB, v_sH, v_sT, Tp, vhi, vlo, nullptr, nullptr, stream))
-    return e;
+  if (side) {
+    if (cudaEventRecord(side->join[0], side->s[0]) != cudaSuccess ||
+        cudaEventRecord(side->join[1], side->s[1]) != cudaSuccess ||
+        cudaStreamWaitEvent(st, side->join[0], 0) != cudaSuccess || cudaStreamWaitEvent(st, side->join[1], 0) != cudaSuccess)
+      return set_error(FP4ATTN_ERR_CUDA, "stream join: %s", cudaGetErrorString(cudaGetLastError()));
+  }
   return fp4attn_fwd_packed_dual(qc, qs, gq, qc_lo, qs_lo, gq_lo, kc, ks, gk, vhi, vlo, out, B, Hq, Hkv, T, Tp, D,
                                  causal, scaling, (flags & FP4ATTN_DUAL_P) ? 1 : 0, 0, stream);
 }

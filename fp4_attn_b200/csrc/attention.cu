@@ -34,6 +34,8 @@
 // Every wait is bounded (sm100.cuh).
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "attn_softmax.cuh"
 #include "sm100.cuh"
@@ -579,13 +581,17 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 // One CTA per 16 consecutive tokens of the flattened B*T axis (one NVFP4
 // block along tokens for every channel); the 16 x Hkv*D slab stays in
 // shared memory in the input's own type (exact), so Hkv*D is limited by it.
-constexpr int VP_THREADS = 256;
+// One CTA per 16 consecutive tokens of the flattened B*T axis (one NVFP4 block
+// along tokens for every channel).  A thread owns channel pairs (2c, 2c+1) of
+// one head (D is even) and reads their 16 token values as 16 two-element loads
+// (consecutive pairs are consecutive addresses); sweep 2 reads them again (from
+// L1: keeping them across the reduction costs more in spills).  Sweep 1
+// takes the per-token max |v| on packed pairs in the input type (exact), a
+// 16-shuffle transpose-reduce and a shared-memory pass finish it over the CTA;
+// sweep 2 quantizes each channel's block of 16 tokens.
+constexpr int VP_THREADS = 512;  // two CTAs per SM
 constexpr int VP_MAX_HD_16 = 6144;  // bf16 / fp16 inputs
 constexpr int VP_MAX_HD_32 = 3072;  // fp32 inputs
-__host__ __device__ constexpr int vp_ld(int hdn, int esz) { return hdn + (esz == 2 ? 2 : 1); }
-__host__ __device__ constexpr size_t vp_smem_bytes(int hdn, int esz) {
-  return (size_t)16 * vp_ld(hdn, esz) * esz + 32 * sizeof(float);
-}
 
 struct VPrepArgs {
   const void* v;  // bf16 / f16 / f32, [B, Hkv, T, D] with element strides
@@ -596,148 +602,257 @@ struct VPrepArgs {
   __half* lo;
   float* vhat;  // optional fp32 Vhat, same layout
   float* g;     // optional per-token global scale [B*T]
-  int vec;      // 16-byte aligned rows of 8 channels: vector loads
+  int vec;      // channel pairs are aligned words (even D and strides, aligned base): one load per pair
 };
 
+// fp16 pair -> two floats
+__device__ __forceinline__ float2 vp_h2f(uint32_t h) { return __half22float2(*reinterpret_cast<const __half2*>(&h)); }
+
+// Two channels' values: 16-bit inputs as one packed 32-bit word, fp32 as a float2.
 template <int DT>
-__global__ void __launch_bounds__(VP_THREADS) vprep_kernel(VPrepArgs p) {
+struct VPair {
+  using W = typename std::conditional<DT == FP4_DT_F32, float2, uint32_t>::type;
+  static __device__ __forceinline__ float2 f(W w) {
+    if constexpr (DT == FP4_DT_F32) {
+      return w;
+    } else {
+      using T = typename In<DT>::T;
+      const T* e = reinterpret_cast<const T*>(&w);
+      return make_float2(In<DT>::f(e[0]), In<DT>::f(e[1]));
+    }
+  }
+  // per-lane max(|a|, |b|), NaN winning, in the input type (exact)
+  static __device__ __forceinline__ W absmax(W a, W b) {
+    if constexpr (DT == FP4_DT_F32) {
+      return make_float2(nanmax(fabsf(a.x), fabsf(b.x)), nanmax(fabsf(a.y), fabsf(b.y)));
+    } else {
+      uint32_t r;
+      if constexpr (DT == FP4_DT_BF16)
+        asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a & 0x7FFF7FFFu), "r"(b & 0x7FFF7FFFu));
+      else
+        asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a & 0x7FFF7FFFu), "r"(b & 0x7FFF7FFFu));
+      return r;
+    }
+  }
+  static __device__ __forceinline__ W zero() {
+    if constexpr (DT == FP4_DT_F32) return make_float2(0.0f, 0.0f);
+    else return 0u;
+  }
+};
+
+// One channel pair at q (q[0], q[1]): a single load when the pair is an aligned word.
+template <int DT>
+__device__ __forceinline__ typename VPair<DT>::W vp_pair(const typename In<DT>::T* q, bool vec) {
+  using W = typename VPair<DT>::W;
+  if (vec) return *reinterpret_cast<const W*>(q);
+  if constexpr (DT == FP4_DT_F32) {
+    return make_float2(q[0], q[1]);
+  } else {
+    const uint16_t* u = reinterpret_cast<const uint16_t*>(q);
+    return (uint32_t)u[0] | ((uint32_t)u[1] << 16);
+  }
+}
+
+// The 16 token values of the channel pair starting at c (zeros past B*T: the
+// reference pads B*T to x16).  D is even, so a pair never straddles two heads.
+template <int DT>
+__device__ __forceinline__ void vp_load2(const VPrepArgs& p, int64_t j0, int c, typename VPair<DT>::W (&w)[16]) {
   using T = typename In<DT>::T;
-  extern __shared__ __align__(16) unsigned char vp_raw[];  // [16][ld] token slab in T, then g[16], rg[16]
-  T* vp_smem = reinterpret_cast<T*>(vp_raw);
+  using W = typename VPair<DT>::W;
+  const bool vec = p.vec != 0;
+  const int h = c / p.D, d = c - h * p.D;
+  const T* base = reinterpret_cast<const T*>(p.v) + (int64_t)h * p.sH + d;
+  const int64_t BT = (int64_t)p.B * p.T;
+  const int b0 = (int)(j0 / p.T), t0 = (int)(j0 - (int64_t)b0 * p.T);
+  if (j0 + 16 <= BT && t0 + 16 <= p.T) {  // one batch row: a fixed token stride
+    const T* q = base + (int64_t)b0 * p.sB + (int64_t)t0 * p.sT;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = vp_pair<DT>(q + (int64_t)i * p.sT, vec);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int64_t jj = j0 + i;
+      W x = VPair<DT>::zero();
+      if (jj < BT) {
+        const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
+        x = vp_pair<DT>(base + (int64_t)b * p.sB + (int64_t)t * p.sT, vec);
+      }
+      w[i] = x;
+    }
+  }
+}
+
+// NVFP4 block of 16 tokens of channel e of the pair values w -> fp16 hi/lo words
+// of token pairs; with VHAT the fp32 Vhat values too.  x * recip(g) is formed
+// twice (for the block max, then for the codes) instead of being kept.
+template <int DT, bool VHAT>
+__device__ __forceinline__ void vp_quant16(const typename VPair<DT>::W (&w)[16], int e, const float* gtok,
+                                           const float* rgtok, float r6, uint32_t (&hi2)[8], uint32_t (&lo2)[8],
+                                           float* vh) {
+  auto xs = [&](int i) {  // tokens i, i+1 of channel e, times recip(g) of each token
+    const float2 a = VPair<DT>::f(w[i]), b = VPair<DT>::f(w[i + 1]);
+    return __fmul2_rn(make_float2(e ? a.y : a.x, e ? b.y : b.x), make_float2(rgtok[i], rgtok[i + 1]));
+  };
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) {
+    const float2 t0 = xs(i), t1 = xs(i + 2);
+    amax = nanmax(amax, nanmax(absmax3(t0.x, t0.y, t1.x), fabsf(t1.y)));
+  }
+  const uint8_t sb = e4m3_torch(mul<FP4_ARITH_F32>(amax, r6));
+  const float rs = recip<FP4_ARITH_F32>(e4m3_to_f32(sb));
+  const bool nan_block = (sb & 0x7F) == 0x7F;
+  uint32_t s2;  // the scale as an fp16 pair (exact: E4M3 values are fp16 values)
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(s2) : "r"((uint32_t)sb * 0x101u));
+  const float2 rs2 = make_float2(rs, rs), zero2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    // x * recip(s) + 0 (one rounding; + 0 turns -0.0 into +0.0 like torch.sign), E2M1 RNE of tokens i, i+1
+    const float2 a = __ffma2_rn(xs(i), rs2, zero2);
+    uint32_t cs;  // (code * s) of both tokens as fp16: exact (|code * s| <= 6 * 448)
+    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+        : "=r"(cs)
+        : "f"(a.x), "f"(a.y));
+    if (nan_block) cs = 0u;
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(cs) : "r"(s2));
+    const float2 q = __fmul2_rn(vp_h2f(cs), make_float2(gtok[i], gtok[i + 1]));  // (code * s) * g
+    if constexpr (VHAT) {
+      vh[i] = q.x;
+      vh[i + 1] = q.y;
+    }
+    // hi = fp16(Vhat), lo = fp16(Vhat - hi)
+    uint32_t hw, lw;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hw) : "f"(q.y), "f"(q.x));
+    const float2 hf = vp_h2f(hw);
+    const float2 r = __fadd2_rn(q, make_float2(-hf.x, -hf.y));  // exactly q - hf
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lw) : "f"(r.y), "f"(r.x));
+    hi2[i / 2] = hw;
+    lo2[i / 2] = lw;
+  }
+}
+
+// VHAT: also write the fp32 Vhat.
+template <int DT, bool VHAT>
+__global__ void __launch_bounds__(VP_THREADS, 2) vprep_kernel(VPrepArgs p) {
+  using W = typename VPair<DT>::W;
+  __shared__ float red[VP_THREADS / 32][16];
+  __shared__ float gtok[16], rgtok[16];
   const int HDn = p.Hkv * p.D;
-  const int ld = vp_ld(HDn, (int)sizeof(T));
-  float* gtok = reinterpret_cast<float*>(vp_raw + (size_t)16 * ld * sizeof(T));
-  float* rgtok = gtok + 16;
-#define slab(tk, c) vp_smem[(tk) * ld + (c)]
-#define slabf(tk, c) In<DT>::f(vp_smem[(tk) * ld + (c)])
   const int64_t BT = (int64_t)p.B * p.T;
   const int64_t j0 = (int64_t)blockIdx.x * 16;
-  // load 16 tokens x all channels (zeros past the end: the reference pads B*T to x16);
-  // 8 consecutive channels of one head per 16-byte load when D % 8 == 0
-  const int dv = p.D / 8;
-  if (p.vec && DT != FP4_DT_F32) {
-    for (int idx = threadIdx.x; idx < 16 * p.Hkv * dv; idx += VP_THREADS) {
-      const int tk = idx / (p.Hkv * dv);
-      const int rem = idx - tk * (p.Hkv * dv);
-      const int h = rem / dv, d0 = (rem - h * dv) * 8;
-      const int64_t jj = j0 + tk;
-      uint4 u = make_uint4(0u, 0u, 0u, 0u);  // zeros are +0 in every input type
-      if (jj < BT) {
-        const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
-        u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + (int64_t)b * p.sB +
-                                                 (int64_t)h * p.sH + (int64_t)t * p.sT + d0));
-      }
-      const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) slab(tk, h * p.D + d0 + k) = e[k];
-    }
-  } else {
-    for (int idx = threadIdx.x; idx < 16 * HDn; idx += VP_THREADS) {
-      const int tk = idx / HDn, c = idx - tk * HDn;
-      const int64_t jj = j0 + tk;
-      T x{};
-      if (jj < BT) {
-        const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
-        const int h = c / p.D, d = c - h * p.D;
-        x = reinterpret_cast<const T*>(p.v)[(int64_t)b * p.sB + (int64_t)h * p.sH + (int64_t)t * p.sT + d];
-      }
-      slab(tk, c) = x;
-    }
-  }
-  __syncthreads();
-  // per-token global scale: colmax of v2d.T * recip(1536) (fp4_quant_utils.py:136,139)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (int tk = warp; tk < 16; tk += VP_THREADS / 32) {
-    float mx = 0.0f;
-    for (int c = lane; c < HDn; c += 32) mx = nanmax(mx, fabsf(slabf(tk, c)));
+  // ---- sweep 1: per-token max |v| over this thread's channel pairs (packed, exact)
+  W w[16];
+  W mw[16];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = nanmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) {
-      const float g = mul<FP4_ARITH_F32>(mx, recip<FP4_ARITH_F32>(1536.0f));
-      gtok[tk] = g;
-      rgtok[tk] = recip<FP4_ARITH_F32>(g);
-      if (p.g && j0 + tk < BT) p.g[j0 + tk] = g;
-    }
+  for (int i = 0; i < 16; ++i) mw[i] = VPair<DT>::zero();
+  for (int c = 2 * threadIdx.x; c < HDn; c += 2 * VP_THREADS) {
+    vp_load2<DT>(p, j0, c, w);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) mw[i] = VPair<DT>::absmax(mw[i], w[i]);
+  }
+  float m[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 t = VPair<DT>::f(mw[i]);
+    m[i] = nanmax(t.x, t.y);
+  }
+  // transpose-reduce over the warp: after offsets 16, 8, 4, 2 a lane keeps one token's
+  // partial max (token bits from lane bits 4..1), offset 1 completes it
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const bool up = lane & 16;
+    const float keep = up ? m[k + 8] : m[k], send = up ? m[k] : m[k + 8];
+    m[k] = nanmax(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const bool up = lane & 8;
+    const float keep = up ? m[k + 4] : m[k], send = up ? m[k] : m[k + 4];
+    m[k] = nanmax(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const bool up = lane & 4;
+    const float keep = up ? m[k + 2] : m[k], send = up ? m[k] : m[k + 2];
+    m[k] = nanmax(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  {
+    const bool up = lane & 2;
+    const float keep = up ? m[1] : m[0], send = up ? m[0] : m[1];
+    m[0] = nanmax(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+  }
+  m[0] = nanmax(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1));
+  if ((lane & 1) == 0) {
+    const int tok = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+    red[warp][tok] = m[0];
   }
   __syncthreads();
+  if (threadIdx.x < 16) {
+    float mx = 0.0f;
+    for (int wi = 0; wi < VP_THREADS / 32; ++wi) mx = nanmax(mx, red[wi][threadIdx.x]);
+    // per-token global scale: colmax of v2d.T * recip(1536) (fp4_quant_utils.py:136,139)
+    const float g = mul<FP4_ARITH_F32>(mx, recip<FP4_ARITH_F32>(1536.0f));
+    gtok[threadIdx.x] = g;
+    rgtok[threadIdx.x] = recip<FP4_ARITH_F32>(g);
+    if (p.g && j0 + threadIdx.x < BT) p.g[j0 + threadIdx.x] = g;
+  }
+  __syncthreads();
+  // ---- sweep 2: NVFP4 block of 16 tokens per channel -> Vhat -> fp16 hi/lo planes
   const float r6 = recip<FP4_ARITH_F32>(6.0f);
-  for (int c = threadIdx.x; c < HDn; c += VP_THREADS) {
-    float x[16];
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      x[i] = mul<FP4_ARITH_F32>(slabf(i, c), rgtok[i]);
-      amax = nanmax(amax, fabsf(x[i]));
-    }
-    const uint8_t sb = e4m3_torch(mul<FP4_ARITH_F32>(amax, r6));
-    const float s = e4m3_to_f32(sb);
-    const float rs = recip<FP4_ARITH_F32>(s);
-    const bool nan_block = (sb & 0x7F) == 0x7F;
+  const int b0 = (int)(j0 / p.T), t0 = (int)(j0 - (int64_t)b0 * p.T);
+  const bool fast_store = j0 + 16 <= BT && t0 + 16 <= p.T && t0 % 8 == 0 && p.Tp % 8 == 0;
+  for (int c = 2 * threadIdx.x; c < HDn; c += 2 * VP_THREADS) {
+    vp_load2<DT>(p, j0, c, w);
     const int h = c / p.D, d = c - h * p.D;
-    float vh[16];
 #pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      const float a0 = __fmaf_rn(x[i], rs, 0.0f), a1 = __fmaf_rn(x[i + 1], rs, 0.0f);
-      const uint32_t byte = nan_block ? 0u : e2m1x2(a0, a1);
-      vh[i] = mul<FP4_ARITH_F32>(mul<FP4_ARITH_F32>(e2m1_value(byte & 15u), s), gtok[i]);
-      vh[i + 1] = mul<FP4_ARITH_F32>(mul<FP4_ARITH_F32>(e2m1_value(byte >> 4), s), gtok[i + 1]);
-    }
-    __half hi[16], lo[16];
+    for (int e = 0; e < 2; ++e) {  // the pair's two channels
+      float vh[VHAT ? 16 : 1];
+      uint32_t hi2[8], lo2[8];
+      vp_quant16<DT, VHAT>(w, e, gtok, rgtok, r6, hi2, lo2, vh);
+      const int de = d + e;
+      if (fast_store) {
+        // 16 tokens of one batch, contiguous in the output row: 16-byte stores
+        const int64_t o = ((int64_t)(b0 * p.Hkv + h) * p.D + de) * p.Tp + t0;
+        uint4* h4 = reinterpret_cast<uint4*>(p.hi + o);
+        uint4* l4 = reinterpret_cast<uint4*>(p.lo + o);
+        h4[0] = make_uint4(hi2[0], hi2[1], hi2[2], hi2[3]);
+        h4[1] = make_uint4(hi2[4], hi2[5], hi2[6], hi2[7]);
+        l4[0] = make_uint4(lo2[0], lo2[1], lo2[2], lo2[3]);
+        l4[1] = make_uint4(lo2[4], lo2[5], lo2[6], lo2[7]);
+        if constexpr (VHAT) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      hi[i] = __float2half_rn(vh[i]);
-      lo[i] = __float2half_rn(vh[i] - __half2float(hi[i]));
-    }
-    const int b0 = (int)(j0 / p.T), t0 = (int)(j0 - (int64_t)b0 * p.T);
-    if (j0 + 16 <= BT && t0 + 16 <= p.T && t0 % 8 == 0 && p.Tp % 8 == 0) {
-      // 16 tokens of one batch, contiguous in the output row: 16-byte stores
-      const int64_t o = ((int64_t)(b0 * p.Hkv + h) * p.D + d) * p.Tp + t0;
-      uint4* h4 = reinterpret_cast<uint4*>(p.hi + o);
-      uint4* l4 = reinterpret_cast<uint4*>(p.lo + o);
-      h4[0] = *reinterpret_cast<const uint4*>(&hi[0]);
-      h4[1] = *reinterpret_cast<const uint4*>(&hi[8]);
-      l4[0] = *reinterpret_cast<const uint4*>(&lo[0]);
-      l4[1] = *reinterpret_cast<const uint4*>(&lo[8]);
-      if (p.vhat) {
+          for (int i = 0; i < 16; ++i) p.vhat[o + i] = vh[i];
+        }
+      } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) p.vhat[o + i] = vh[i];
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int64_t jj = j0 + i;
-        if (jj >= BT) continue;
-        const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
-        const int64_t o = ((int64_t)(b * p.Hkv + h) * p.D + d) * p.Tp + t;
-        p.hi[o] = hi[i];
-        p.lo[o] = lo[i];
-        if (p.vhat) p.vhat[o] = vh[i];
+        for (int i = 0; i < 16; ++i) {
+          const int64_t jj = j0 + i;
+          if (jj >= BT) continue;
+          const int b = (int)(jj / p.T), t = (int)(jj - (int64_t)b * p.T);
+          const int64_t oo = ((int64_t)(b * p.Hkv + h) * p.D + de) * p.Tp + t;
+          const uint32_t hw = hi2[i / 2] >> (16 * (i & 1)), lw = lo2[i / 2] >> (16 * (i & 1));
+          p.hi[oo] = __ushort_as_half((unsigned short)(hw & 0xFFFFu));
+          p.lo[oo] = __ushort_as_half((unsigned short)(lw & 0xFFFFu));
+          if constexpr (VHAT) p.vhat[oo] = vh[i];
+        }
       }
     }
   }
-#undef slab
-#undef slabf
 }
 
 template <int DT>
-static void vprep_launch(const VPrepArgs& a, unsigned blocks, size_t smem, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(vprep_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)vp_smem_bytes(DT == FP4_DT_F32 ? VP_MAX_HD_32 : VP_MAX_HD_16,
-                                            DT == FP4_DT_F32 ? 4 : 2));
-    attr = true;
-  }
-  vprep_kernel<DT><<<blocks, VP_THREADS, smem, st>>>(a);
+static void vprep_launch(const VPrepArgs& a, unsigned blocks, cudaStream_t st) {
+  if (a.vhat) vprep_kernel<DT, true><<<blocks, VP_THREADS, 0, st>>>(a);
+  else vprep_kernel<DT, false><<<blocks, VP_THREADS, 0, st>>>(a);
 }
 
 static int launch_vprep(const VPrepArgs& a, cudaStream_t st) {
   const unsigned blocks = (unsigned)(((int64_t)a.B * a.T + 15) / 16);
-  const size_t smem = vp_smem_bytes(a.Hkv * a.D, a.in_dtype == FP4_DT_F32 ? 4 : 2);
   switch (a.in_dtype) {
-    case FP4_DT_F32: vprep_launch<FP4_DT_F32>(a, blocks, smem, st); break;
-    case FP4_DT_BF16: vprep_launch<FP4_DT_BF16>(a, blocks, smem, st); break;
-    case FP4_DT_F16: vprep_launch<FP4_DT_F16>(a, blocks, smem, st); break;
+    case FP4_DT_F32: vprep_launch<FP4_DT_F32>(a, blocks, st); break;
+    case FP4_DT_BF16: vprep_launch<FP4_DT_BF16>(a, blocks, st); break;
+    case FP4_DT_F16: vprep_launch<FP4_DT_F16>(a, blocks, st); break;
     default: return set_error(FP4ATTN_ERR_ARG, "bad dtype");
   }
   return check_launch("vprep_kernel");
@@ -768,9 +883,9 @@ extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, in
     if (cudaMemsetAsync(v_hi, 0, bytes, st) != cudaSuccess || cudaMemsetAsync(v_lo, 0, bytes, st) != cudaSuccess)
       return set_error(FP4ATTN_ERR_CUDA, "memset");
   }
+  if (D % 2) return set_error(FP4ATTN_ERR_UNSUPPORTED, "head_dim must be even");
   const int esz = in_dtype == FP4_DT_F32 ? 4 : 2;
-  const int vec = (D % 8 == 0) && ((uintptr_t)v % 16 == 0) && ((sB * esz) % 16 == 0) && ((sH * esz) % 16 == 0) &&
-                  ((sT * esz) % 16 == 0);
+  const int vec = ((uintptr_t)v % (2 * esz) == 0) && sB % 2 == 0 && sH % 2 == 0 && sT % 2 == 0;
   VPrepArgs a{v, in_dtype, sB, sH, sT, B, Hkv, T, D, Tp, reinterpret_cast<__half*>(v_hi),
               reinterpret_cast<__half*>(v_lo), vhat, g, vec};
   return launch_vprep(a, st);

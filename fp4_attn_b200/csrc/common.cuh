@@ -54,6 +54,13 @@ __device__ __forceinline__ float nanmax(float a, float b) {
   return r;
 }
 
+// max(|a|,|b|,|c|) with NaN winning.
+__device__ __forceinline__ float absmax3(float a, float b, float c) {
+  float r;
+  asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // torch's float32 -> float8_e4m3fn cast: round to nearest even, any
 // magnitude above 464 (and NaN) becomes NaN (0x7F with the sign bit).
 __device__ __forceinline__ uint8_t e4m3_torch(float v) {

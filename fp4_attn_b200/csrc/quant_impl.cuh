@@ -113,13 +113,6 @@ __device__ __forceinline__ void load_block(float v[16], const QuantArgs& p, int 
   }
 }
 
-// max(|a|,|b|,|c|) with NaN winning.
-__device__ __forceinline__ float absmax3(float a, float b, float c) {
-  float r;
-  asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
 __device__ __forceinline__ float block_absmax(const float v[16]) {
   float m0 = absmax3(v[0], v[1], v[2]);
   float m1 = absmax3(v[3], v[4], v[5]);

@@ -145,6 +145,50 @@ def quantize_input(rank=0):
     return x.bfloat16()
 
 
+class E2EPipe:
+    """Host-buffer steps overlapped the way a serving loop runs them: step i's H2D
+    copy (copy stream), compute (compute stream) and D2H read-back (second copy
+    stream) wait only on what they use, so the next step's inputs cross PCIe while
+    this step computes.  Every step still moves its own inputs and result."""
+
+    def __init__(self, nslots):
+        self.h2d, self.comp, self.d2h = (torch.cuda.Stream() for _ in range(3))
+        self.used = [None] * nslots  # compute done with the slot's device buffers
+        self.read = [None] * nslots  # D2H done with the slot's result
+
+    def begin(self):
+        ev = torch.cuda.Event()
+        ev.record()
+        for st in (self.h2d, self.comp, self.d2h):
+            st.wait_event(ev)
+
+    def step(self, slot, h2d, compute, d2h):
+        with torch.cuda.stream(self.h2d):
+            if self.used[slot] is not None:
+                self.h2d.wait_event(self.used[slot])
+            h2d()
+            ev_in = torch.cuda.Event()
+            ev_in.record()
+        with torch.cuda.stream(self.comp):
+            self.comp.wait_event(ev_in)
+            if self.read[slot] is not None:
+                self.comp.wait_event(self.read[slot])
+            res = compute()
+            ev_c = torch.cuda.Event()
+            ev_c.record()
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(ev_c)
+            d2h(res)
+            ev_r = torch.cuda.Event()
+            ev_r.record()
+        self.used[slot], self.read[slot] = ev_c, ev_r
+
+    def join(self):
+        cur = torch.cuda.current_stream()
+        for st in (self.h2d, self.comp, self.d2h):
+            cur.wait_stream(st)
+
+
 class QuantizeWorkload:
     name = "quantize"
     metric = "NVFP4 quantize GB/s per B200, % of HBM roofline"
@@ -203,13 +247,18 @@ class QuantizeWorkload:
         self._full(i % self.nsets)
 
     def e2e_step(self, i):
-        """Public API, host buffers: H2D input, quantize, D2H codes + scales."""
+        """Public API, host buffers: H2D input, quantize, D2H codes + scales (pipelined over steps)."""
         from fp4_attn_b200 import quant
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(self.nsets)
         i %= self.nsets
-        self.xs[i].copy_(self.x_host, non_blocking=True)
-        t = quant.quantize(self.xs[i], "tensor", 2688.0)
-        self.codes_host.copy_(t.codes, non_blocking=True)
-        self.scales_host.copy_(t.scales, non_blocking=True)
+
+        def d2h(t):
+            self.codes_host.copy_(t.codes, non_blocking=True)
+            self.scales_host.copy_(t.scales, non_blocking=True)
+
+        self.pipe.step(i, lambda: self.xs[i].copy_(self.x_host, non_blocking=True),
+                       lambda: quant.quantize(self.xs[i], "tensor", 2688.0), d2h)
 
     e2e_h2d = property(lambda self: self.elems * 2)
     e2e_d2h = property(lambda self: self.elems // 2 + self.elems // 16)
@@ -268,7 +317,7 @@ class AttentionWorkload:
         units = shard.attention_shard(world, self.Hq, self.Hkv, world, rank)
         assert all(u.b == rank for u in units) and len(units) == self.Hkv
         self.config = {"workload": "NVFP4 attention fwd, Llama-3-8B shape: B=1, Hq=32, Hkv=8, D=128, T=4096, "
-                                   "causal, single-slice Q/P quantization",
+                                   "causal, single-slice Q/P quantization, bf16 output",
                        "flops_per_step": self.flops, "global_batch": world,
                        "shard": "batch row r (its 8 (batch, kv-head) units) on rank r, seed 1 + r"}
         if cpu_only:
@@ -282,8 +331,10 @@ class AttentionWorkload:
         self.nsets = max(2, int(2 * L2_BYTES // per_set) + 1)
         self.sets = [tuple(t.to(dev) for t in (q, k, v)) for _ in range(self.nsets)]
         self.ws = [A.AttentionWorkspace(self.B, self.Hq, self.Hkv, self.T, self.D, dev) for _ in range(self.nsets)]
-        self.out = [torch.empty(self.B, self.T, self.Hq, self.D, device=dev) for _ in range(self.nsets)]
-        self.out_host = torch.empty(self.B, self.T, self.Hq, self.D).pin_memory()
+        self.out = [torch.empty(self.B, self.T, self.Hq, self.D, device=dev, dtype=torch.bfloat16)
+                    for _ in range(self.nsets)]
+        self.out_bf16 = self.out
+        self.out_host = torch.empty(self.B, self.T, self.Hq, self.D, dtype=torch.bfloat16).pin_memory()
         self.config["l2"] = f"rotating {self.nsets} input sets (> L2)"
 
     use_graph = True  # each step (one C ABI call, several launches on forked streams) is a CUDA graph replay
@@ -294,32 +345,39 @@ class AttentionWorkload:
         i %= self.nsets
         q, k, v = self.sets[i]
         ws = self.ws[i]
-        _lib.call("fp4attn_forward", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], self.B,
+        _lib.call("fp4attn_forward_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], self.B,
                   self.Hq, self.Hkv, self.T, self.D, q.stride(0), q.stride(1), q.stride(2), k.stride(0),
                   k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), 1, self.D ** -0.5,
-                  self.out[i].data_ptr(), ws.ptr(), ws.nbytes, _lib.stream_of(q))
+                  self.A.OUT_BF16, self.out[i].data_ptr(), ws.ptr(), ws.nbytes, _lib.stream_of(q))
 
     def kernel(self, i):
         """The attention kernel alone on the operands step(i) prepared."""
         from fp4_attn_b200 import _lib
         i %= self.nsets
         ws = self.ws[i]
-        _lib.call("fp4attn_fwd_packed", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), ws.kc.data_ptr(),
-                  ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), self.out[i].data_ptr(),
-                  self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, 1, self.D ** -0.5, 0,
-                  _lib.stream_of(self.sets[i][0]))
+        _lib.call("fp4attn_fwd_packed_dual", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), None, None, None,
+                  ws.kc.data_ptr(), ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(),
+                  self.out[i].data_ptr(), self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, 1, self.D ** -0.5,
+                  self.A.OUT_BF16, 0, _lib.stream_of(self.sets[i][0]))
 
     def e2e_step(self, i):
-        """Public API, host buffers: H2D q/k/v, fp4_attention_fwd, D2H the output."""
+        """Public API, host buffers: H2D q/k/v, fp4_attention_fwd (bf16 out, the reference's output
+        dtype), D2H the output; steps pipelined over copy and compute streams."""
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(self.nsets)
         i %= self.nsets
         q, k, v = self.sets[i]
-        for d, h in zip((q, k, v), self.host):
-            d.copy_(h, non_blocking=True)
-        o = self.A.fp4_attention_fwd(q, k, v, causal=True, workspace=self.ws[i], out=self.out[i])
-        self.out_host.copy_(o, non_blocking=True)
+
+        def h2d():
+            for d, h in zip((q, k, v), self.host):
+                d.copy_(h, non_blocking=True)
+
+        self.pipe.step(i, h2d, lambda: self.A.fp4_attention_fwd(q, k, v, causal=True, workspace=self.ws[i],
+                                                                 out=self.out_bf16[i], out_dtype=torch.bfloat16),
+                       lambda o: self.out_host.copy_(o, non_blocking=True))
 
     e2e_h2d = property(lambda self: sum(t.numel() * 2 for t in self.host))
-    e2e_d2h = property(lambda self: self.out_host.numel() * 4)
+    e2e_d2h = property(lambda self: self.out_host.numel() * 2)
 
     def value(self, seconds_per_step, world):
         return world * self.flops / seconds_per_step / 1e12
@@ -459,8 +517,12 @@ def run_ours(args, world, rank, local):
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    if hasattr(wl, "pipe"):
+        wl.pipe.begin()
     for i in range(K):
         wl.e2e_step(i)
+    if hasattr(wl, "pipe"):
+        wl.pipe.join()
     e1.record()
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)

@@ -20,7 +20,7 @@ import torch
 from . import _lib
 
 HEAD_DIM = 128
-DUAL_Q, DUAL_P = 1, 2  # fp4attn_forward_ex flags
+DUAL_Q, DUAL_P, OUT_BF16 = 1, 2, 4  # fp4attn_forward_ex flags
 
 
 class AttentionWorkspace:
@@ -99,8 +99,12 @@ def prepare_v(v: torch.Tensor, vhi, vlo, Tp: int, vhat=None, g=None) -> None:
 def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
                       scaling: float | None = None, out: torch.Tensor | None = None,
                       workspace: AttentionWorkspace | None = None, num_ctas: int = 0,
-                      dual_q: bool = False, dual_p: bool = False) -> torch.Tensor:
-    """NVFP4 attention forward.  q [B,Hq,T,D], k/v [B,Hkv,T,D] (CUDA) -> fp32 [B,T,Hq,D].
+                      dual_q: bool = False, dual_p: bool = False,
+                      out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """NVFP4 attention forward.  q [B,Hq,T,D], k/v [B,Hkv,T,D] (CUDA) -> [B,T,Hq,D] in out_dtype.
+
+    out_dtype fp32 or bf16 (the reference's output dtype for bf16 inputs,
+    llama_patch.py:102-103: the kernel rounds its fp32 result once).
 
     One call of the C ABI's fp4attn_forward_ex (quantize Q/K, prepare V-hat,
     attention) with the packed operands in ``workspace``.  dual_q / dual_p
@@ -126,12 +130,14 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
         raise ValueError(f"workspace made for {ws.shape}, called with {(B, Hq, Hkv, T, D)}")
     if dual_q and not ws.dual_q:
         raise ValueError("dual_q needs a workspace made with dual_q=True")
-    if num_ctas and (dual_q or dual_p):
-        raise ValueError("num_ctas is a single-slice profiling option")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
+    if num_ctas and (dual_q or dual_p or out_dtype != torch.float32):
+        raise ValueError("num_ctas is a single-slice fp32-output profiling option")
     if out is None:
-        out = torch.empty(B, T, Hq, D, dtype=torch.float32, device=q.device)
-    elif out.shape != (B, T, Hq, D) or out.dtype != torch.float32 or not out.is_contiguous():
-        raise ValueError("out must be a contiguous fp32 [B, T, Hq, D] tensor")
+        out = torch.empty(B, T, Hq, D, dtype=out_dtype, device=q.device)
+    elif out.shape != (B, T, Hq, D) or out.dtype != out_dtype or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {out_dtype} [B, T, Hq, D] tensor")
     if num_ctas:
         quantize_qk(q, ws.qc, ws.qs, ws.gq, ws.Tp)
         quantize_qk(k, ws.kc, ws.ks, ws.gk, ws.Tp)
@@ -140,7 +146,7 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
                   ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), out.data_ptr(), B, Hq,
                   Hkv, T, ws.Tp, D, 1 if causal else 0, float(scaling), int(num_ctas), _lib.stream_of(q))
         return out
-    flags = (DUAL_Q if dual_q else 0) | (DUAL_P if dual_p else 0)
+    flags = (DUAL_Q if dual_q else 0) | (DUAL_P if dual_p else 0) | (OUT_BF16 if out_dtype == torch.bfloat16 else 0)
     _lib.call("fp4attn_forward_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], B, Hq, Hkv, T,
               D, q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0),
               v.stride(1), v.stride(2), 1 if causal else 0, float(scaling), flags, out.data_ptr(), ws.ptr(),

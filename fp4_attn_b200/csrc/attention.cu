@@ -33,11 +33,13 @@
 // warp has loaded S(j); P-hat has its own TMEM buffer, freed by PV's commit.
 // Every wait is bounded (sm100.cuh).
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include <type_traits>
 
 #include "common.cuh"
 #include "attn_softmax.cuh"
+#include "fp4attn.h"
 #include "sm100.cuh"
 #include "status.h"
 #include "tmap.h"
@@ -81,7 +83,8 @@ struct AttnArgs {
   const float* gq_lo;
   const uint8_t* ksf;
   const float* gk;
-  float* out;  // [B, T, Hq, HD] fp32
+  void* out;    // [B, T, Hq, HD], fp32 or (out_bf16) bf16
+  int out_bf16;
   int B, Hq, Hkv, T, Tp;
   int causal;
   float scale_log2;  // scaling * log2(e)
@@ -399,11 +402,26 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       tmem_ld32(tmem + lane_base + T_O + col0, a);
       tmem_ld_wait();
       if (pend_off >= 0) {
-        float4* d4 = reinterpret_cast<float4*>(p.out + pend_off);
+        if (p.out_bf16) {  // rounded to bf16 as the reference's bf16 matmul output is
+          uint4* d4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + pend_off);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          d4[i] = make_float4(__uint_as_float(a[4 * i]) * pend_rl, __uint_as_float(a[4 * i + 1]) * pend_rl,
-                              __uint_as_float(a[4 * i + 2]) * pend_rl, __uint_as_float(a[4 * i + 3]) * pend_rl);
+          for (int i = 0; i < 4; ++i) {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(a[8 * i + 2 * k]) * pend_rl,
+                                                             __uint_as_float(a[8 * i + 2 * k + 1]) * pend_rl);
+              w[k] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        } else {
+          float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + pend_off);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(__uint_as_float(a[4 * i]) * pend_rl, __uint_as_float(a[4 * i + 1]) * pend_rl,
+                                __uint_as_float(a[4 * i + 2]) * pend_rl, __uint_as_float(a[4 * i + 3]) * pend_rl);
+        }
       }
       tc_fence_before();
       named_bar(1 + NWG, NWG * 128);
@@ -894,8 +912,8 @@ extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, in
 extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
                                        const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
                                        const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
-                                       const uint16_t* v_hi, const uint16_t* v_lo, float* out, int B, int Hq,
-                                       int Hkv, int T, int Tp, int D, int causal, float scaling, int dual_p,
+                                       const uint16_t* v_hi, const uint16_t* v_lo, void* out, int B, int Hq,
+                                       int Hkv, int T, int Tp, int D, int causal, float scaling, int flags,
                                        int num_ctas, void* stream) {
   using namespace attn;
   clear_error();
@@ -905,6 +923,8 @@ extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_
   if (!q_codes || !q_scales || !q_g || !k_codes || !k_scales || !k_g || !v_hi || !v_lo || !out)
     return set_error(FP4ATTN_ERR_ARG, "null pointer");
   const bool dq = q_codes_lo != nullptr;
+  if (flags & ~(FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16)) return set_error(FP4ATTN_ERR_ARG, "bad flags");
+  const bool dual_p = (flags & FP4ATTN_DUAL_P) != 0;
   if (dq && (!q_scales_lo || !q_g_lo)) return set_error(FP4ATTN_ERR_ARG, "null pointer (residual Q slice)");
   if (((uintptr_t)q_codes | (uintptr_t)k_codes | (uintptr_t)v_hi | (uintptr_t)v_lo | (uintptr_t)q_scales |
        (uintptr_t)k_scales | (uintptr_t)q_g | (uintptr_t)k_g | (uintptr_t)out | (uintptr_t)q_codes_lo |
@@ -938,6 +958,7 @@ extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_
   a.ksf = k_scales;
   a.gk = k_g;
   a.out = out;
+  a.out_bf16 = (flags & FP4ATTN_OUT_BF16) ? 1 : 0;
   a.B = B;
   a.Hq = Hq;
   a.Hkv = Hkv;

@@ -28,7 +28,7 @@ int64_t align_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 // Q - hi.  Returns the total size, or -1 for a bad shape.
 int64_t layout(int B, int Hq, int Hkv, int T, int D, int flags, int64_t* offsets) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0 || D <= 0 || D % 64 != 0 || Hq % Hkv != 0) return -1;
-  if (flags & ~(FP4ATTN_DUAL_Q | FP4ATTN_DUAL_P)) return -1;
+  if (flags & ~(FP4ATTN_DUAL_Q | FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16)) return -1;
   const int64_t Tp = ((int64_t)T + 127) / 128 * 128;
   const int64_t rows = (int64_t)B * Tp;
   const int64_t dq = (flags & FP4ATTN_DUAL_Q) ? 1 : 0;
@@ -137,7 +137,7 @@ extern "C" int64_t fp4attn_workspace_layout(int B, int Hq, int Hkv, int T, int D
 extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv,
                                   int T, int D, int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH,
                                   int64_t k_sT, int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling,
-                                  int flags, float* out, void* workspace, int64_t workspace_bytes, void* stream) {
+                                  int flags, void* out, void* workspace, int64_t workspace_bytes, void* stream) {
   using namespace fp4;
   clear_error();
   if (!q || !k || !v || !out || !workspace) return set_error(FP4ATTN_ERR_ARG, "null pointer");
@@ -216,7 +216,7 @@ extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, i
       return set_error(FP4ATTN_ERR_CUDA, "stream join: %s", cudaGetErrorString(cudaGetLastError()));
   }
   return fp4attn_fwd_packed_dual(qc, qs, gq, qc_lo, qs_lo, gq_lo, kc, ks, gk, vhi, vlo, out, B, Hq, Hkv, T, Tp, D,
-                                 causal, scaling, (flags & FP4ATTN_DUAL_P) ? 1 : 0, 0, stream);
+                                 causal, scaling, flags & (FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16), 0, stream);
 }
 
 extern "C" int fp4attn_forward(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv,

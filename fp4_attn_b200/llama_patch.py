@@ -75,8 +75,10 @@ def fp4_eager_attention(module, query, key, value, attention_mask, scaling, drop
     if S != T:
         raise NotImplementedError(f"prefill only: query length {T} != key length {S}")
     _check_mask(attention_mask, T, S)
+    out_dtype = torch.bfloat16 if query.dtype == torch.bfloat16 else torch.float32
     out = fp4_attention_fwd(query, key, value, causal=True, scaling=float(scaling),
-                            dual_q=dual_enabled("FP4_USE_DUAL_QUANT_Q"), dual_p=dual_enabled("FP4_USE_DUAL_QUANT_ATTN"))
+                            dual_q=dual_enabled("FP4_USE_DUAL_QUANT_Q"), dual_p=dual_enabled("FP4_USE_DUAL_QUANT_ATTN"),
+                            out_dtype=out_dtype)
     return out.to(query.dtype), None
 
 

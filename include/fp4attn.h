@@ -167,14 +167,16 @@ int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const fl
  * llama_patch.py:183-189 and FP4_USE_DUAL_QUANT_ATTN at llama_patch.py:84-95,
  * both default true in the reference).  q_codes_lo / q_scales_lo / q_g_lo:
  * the second (residual) Q slice, the same quantizer on Q - dequant(first
- * slice), same layouts; NULL = single-slice Q.  dual_p != 0: P-hat = hi + lo
- * with lo the row-aligned NVFP4 fake-quant of P - hi (one more pass over the
- * keys finds each row's residual scale). */
+ * slice), same layouts; NULL = single-slice Q.  flags: FP4ATTN_DUAL_P for
+ * P-hat = hi + lo with lo the row-aligned NVFP4 fake-quant of P - hi (one
+ * more pass over the keys finds each row's residual scale); FP4ATTN_OUT_BF16
+ * for a bf16 out (the reference's output dtype, llama_patch.py:102-103),
+ * else fp32. */
 int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
                             const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
                             const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g, const uint16_t* v_hi,
-                            const uint16_t* v_lo, float* out, int B, int Hq, int Hkv, int T, int Tp, int D,
-                            int causal, float scaling, int dual_p, int num_ctas, void* stream);
+                            const uint16_t* v_lo, void* out, int B, int Hq, int Hkv, int T, int Tp, int D,
+                            int causal, float scaling, int flags, int num_ctas, void* stream);
 
 /* Workspace of fp4attn_forward for a shape: writes the byte offsets of its
  * eight pieces -- Q codes, Q scale atoms, Q g, K codes, K scale atoms, K g,
@@ -187,6 +189,7 @@ int64_t fp4attn_workspace_layout(int B, int Hq, int Hkv, int T, int D, int64_t* 
 /* Flags of fp4attn_forward_ex / fp4attn_workspace_layout_ex. */
 #define FP4ATTN_DUAL_Q 1 /* dual-slice Q (FP4_USE_DUAL_QUANT_Q=true) */
 #define FP4ATTN_DUAL_P 2 /* dual-slice P (FP4_USE_DUAL_QUANT_ATTN=true) */
+#define FP4ATTN_OUT_BF16 4 /* out is bf16 [B,T,Hq,D] (the reference's output dtype), not fp32 */
 
 /* fp4attn_workspace_layout with flags: offsets[0..11], the eight pieces
  * above, then (FP4ATTN_DUAL_Q only; empty otherwise) the residual Q slice's
@@ -210,7 +213,7 @@ int fp4attn_forward(const void* q, const void* k, const void* v, int in_dtype, i
  * the fp32 residual Q - dequant(first slice), bit-exact to dual_nvfp4. */
 int fp4attn_forward_ex(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv, int T, int D,
                        int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH, int64_t k_sT,
-                       int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling, int flags, float* out,
+                       int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling, int flags, void* out,
                        void* workspace, int64_t workspace_bytes, void* stream);
 
 /* fp4attn_forward without a caller workspace; allocates no device memory.

@@ -177,3 +177,19 @@ def test_dual_q_slices_bit_exact(strided):
         np.testing.assert_array_equal(qs.cpu().numpy()[off], scales)
     pad = np.setdiff1d(np.arange(B * Tp), rows)  # padding rows read as zeros
     assert (ws.qc_lo.cpu().numpy()[pad] == 0).all() and (ws.gq_lo.cpu().numpy()[pad] == 0).all()
+
+
+def test_bf16_output_is_the_fp32_result_rounded():
+    """out_dtype=bf16 (the reference's output dtype) stores the fp32 result rounded to bf16, nothing else."""
+    from fp4_attn_b200.attention import fp4_attention_fwd
+    from fp4_attn_b200.gemm import device_status
+    g = torch.Generator().manual_seed(23)
+    dev = torch.device("cuda", 0)
+    q = torch.randn(2, 4, 300, 128, generator=g).bfloat16().to(dev)
+    k = torch.randn(2, 2, 300, 128, generator=g).bfloat16().to(dev)
+    v = torch.randn(2, 2, 300, 128, generator=g).bfloat16().to(dev)
+    for dual in (False, True):
+        o32 = fp4_attention_fwd(q, k, v, causal=True, dual_q=dual, dual_p=dual)
+        o16 = fp4_attention_fwd(q, k, v, causal=True, dual_q=dual, dual_p=dual, out_dtype=torch.bfloat16)
+        assert device_status() == 0
+        assert o16.dtype == torch.bfloat16 and torch.equal(o16, o32.bfloat16())

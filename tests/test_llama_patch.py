@@ -46,7 +46,7 @@ def test_patched_model_reaches_the_kernel_with_dual_defaults(monkeypatch):
     ids = torch.randint(0, 64, (1, 8))
     seen = []
 
-    def fake(q, k, v, causal=True, scaling=None, dual_q=False, dual_p=False):
+    def fake(q, k, v, causal=True, scaling=None, dual_q=False, dual_p=False, out_dtype=None):
         seen.append((dual_q, dual_p))
         raise RuntimeError("stop before the GPU")
 

@@ -33,6 +33,7 @@ SIGNATURES = {
     "fp4attn_fwd_packed": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P], _I),
     "fp4attn_workspace_layout": ([_I, _I, _I, _I, _I, _P], _L),
     "fp4q_quantize_dual": ([_P, _I, _I, _I, _I, _I, _L, _L, _L, _I, _P, _L, _P, _I, _L, _P, _P, _P, _P, _P], _I),
+    "fp4qkv_rope_quant": ([_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P], _I),
     "fp4attn_workspace_layout_ex": ([_I, _I, _I, _I, _I, _I, _P], _L),
     "fp4attn_fwd_packed_dual": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                                  _P], _I),

@@ -23,7 +23,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
           "-I", CSRC, "-I", os.path.join(ROOT, "include")]
 # Files whose arithmetic must round exactly like the reference: no FMA contraction.
-EXACT = {"quant.cu", "quant_f32.cu", "quant_bf16.cu", "quant_f16.cu", "quant_fused.cu", "nvfp4sim_compat.cu"}
+EXACT = {"quant.cu", "quant_f32.cu", "quant_bf16.cu", "quant_f16.cu", "quant_fused.cu", "nvfp4sim_compat.cu",
+         "qkv_quant.cu"}
 
 
 def _nvcc() -> str:

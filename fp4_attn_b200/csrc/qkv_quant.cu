@@ -1,0 +1,381 @@
+// qkv_quant.cu -- a Q or K projection fused with RoPE and the NVFP4 row
+// quantizer: packed attention operands straight from the hidden states.
+//
+// The reference's patched attention runs q_proj / k_proj (bf16 linear,
+// llama_patch.py:147-149), quantizes the 2-D views [B*T, H*D] row-wise with a
+// per-token global scale (llama_patch.py:167-194) and applies RoPE
+// (llama_patch.py:210).  This path applies RoPE first and quantizes the
+// rotated values (the FP4 tensor cores need FP4 operands after the rotation):
+//
+//   y   = bf16(x W^T)                                   (fp32 accumulate)
+//   z   = bf16(bf16(y cos) + bf16(rotate_half(y) sin))  (HF apply_rotary_pos_emb
+//                                                         in bf16, op for op)
+//   codes, E4M3 scales, g = the row quantizer on z      (g = max_row |z|,
+//                                                         fp4_quant_utils.py:118-169)
+//
+// written in the layout the attention kernel loads: codes [M][H*D/2], scales
+// in tcgen05 atoms, g [M] (M = B*T tokens, T a multiple of 128).
+//
+// A CTA computes 128 tokens x hpc heads (hpc = 4, or H when H < 4; up to 512
+// fp32 TMEM columns) with tcgen05 kind::f16 (bf16 operands staged by TMA, 64B
+// swizzle, 4-stage ring).  The per-token global scale spans all H heads, so
+// the H/hpc CTAs of one 128-token
+// block form a thread-block cluster: each CTA stages its rotated bf16 values
+// in shared memory, publishes its row maxima, reads the others' through
+// distributed shared memory, and quantizes its own columns.  No bf16 Q/K
+// tensor goes to HBM.  Every mbarrier wait is bounded; a CTA whose wait gave
+// up still takes part in both cluster barriers.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "fp4attn.h"
+#include "sm100.cuh"
+#include "status.h"
+#include "tmap.h"
+
+namespace fp4 {
+
+FP4_DEFINE_STATUS_READER(qkv_status)
+
+namespace {
+namespace qkv {
+constexpr int BM = 128, HD = 128, HPC = 4, BN = HPC * HD, BK = 32;  // BK: bf16 elements = 64 bytes per row
+constexpr int STAGES = 4;
+constexpr int X_BYTES = BM * BK * 2;             // 8 KB
+constexpr int W_BYTES = BN * BK * 2;             // 32 KB
+constexpr int STAGE_BYTES = X_BYTES + W_BYTES;   // 40 KB
+constexpr int RING_BYTES = STAGES * STAGE_BYTES;  // 160 KB
+constexpr int E_LD = BN * 2 + 16;  // staged row (bytes): 16 bytes of padding spread the rows over the banks
+constexpr int E_BYTES = BM * E_LD;
+static_assert(E_BYTES <= RING_BYTES, "the staged rows reuse the ring");
+constexpr int AUX_BYTES = 2048;  // barriers, TMEM slot, row maxima, reciprocal table
+constexpr int SMEM_BYTES = RING_BYTES + AUX_BYTES + 1024;
+constexpr int THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue (one TMEM lane quarter each)
+constexpr int MAX_CLUSTER = 16;
+constexpr uint32_t TMEM_COLS = 512;
+}  // namespace qkv
+
+struct QkvArgs {
+  const __nv_bfloat16* cos;  // [M][HD]
+  const __nv_bfloat16* sin;  // [M][HD]
+  uint8_t* codes;            // [M][H*HD/2]
+  uint8_t* scales;           // tcgen05 atoms, nkb4 groups per 128-row block
+  float* g;                  // [M]
+  int M, K, H;
+  int nkb4;  // H*HD/64
+  int hpc;   // heads per CTA: 1, 2 or 4
+};
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, f32 accumulate, M=128, K=16.
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f16 instruction descriptor with bf16 A/B (format 1 at [7,10) and [10,13)), f32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// A float in the shared memory of cluster CTA `rank` at this CTA's address `p`.
+__device__ __forceinline__ float ld_dsmem_f32(const float* p, uint32_t rank) {
+  uint32_t a = smem_u32(p), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Wait for a bulk copy to land, whatever the failure flag says (bounded).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > kWaitNs) return;
+}
+
+__global__ void __launch_bounds__(qkv::THREADS, 1)
+    qkv_rope_quant_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                          QkvArgs p) {
+  using namespace qkv;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + RING_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  float* rmax = reinterpret_cast<float*>(sm + RING_BYTES + 256);  // [BM]
+  float* rcp_tab = rmax + BM;                                     // [128]
+  const int warp = threadIdx.x / 32;
+  const int m0 = blockIdx.x * BM;
+  const int ncols = p.hpc * HD;             // output columns of this CTA
+  const int n0 = blockIdx.y * ncols;        // first output column: heads hpc*blockIdx.y ..
+  const int nrows_w = ncols < 256 ? ncols : 256;  // W rows per TMA box and per MMA (N)
+  const int nw = ncols / nrows_w;                 // W boxes (and MMAs per K step)
+  const uint32_t stage_tx = (uint32_t)(X_BYTES + ncols * BK * 2);
+  const int ksteps = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 128) {
+    // correctly rounded 1/s for every non-negative E4M3 scale byte (0 -> 0, get_reciprocal)
+    const float s = e4m3_to_f32((uint8_t)threadIdx.x);
+    rcp_tab[threadIdx.x] = s == 0.0f ? 0.0f : __frcp_rn(s);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------- producer: X and W tiles
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmX);
+      tma_prefetch_desc(&tmW);
+      int issued = 0;
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int s = ks % STAGES;
+        if (ks >= STAGES && !mbar_wait(&empty[s], ((ks / STAGES) - 1) & 1, 0x601)) break;
+        uint8_t* st = sm + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], stage_tx);
+        tma_load_2d(st, &tmX, &full[s], ks * BK, m0);
+        for (int i = 0; i < nw; ++i) tma_load_2d(st + X_BYTES + i * nrows_w * BK * 2, &tmW, &full[s], ks * BK, n0 + i * nrows_w);
+        issued = ks + 1;
+      }
+      // nothing of the ring may still be in flight when it is reused or the CTA exits
+      for (int ks = issued > STAGES ? issued - STAGES : 0; ks < issued; ++ks)
+        mbar_drain(&full[ks % STAGES], (ks / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issue
+    if (elect_one_lane()) {
+      const uint32_t idesc = idesc_bf16(BM, nrows_w);
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const int s = ks % STAGES;
+        if (!mbar_wait(&full[s], (ks / STAGES) & 1, 0x602)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + s * STAGE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = smem_desc(st + kk * 32, 16, 512, kSwizzle64B);
+          for (int i = 0; i < nw; ++i) {
+            const uint64_t bd = smem_desc(st + X_BYTES + i * nrows_w * BK * 2 + kk * 32, 16, 512, kSwizzle64B);
+            mma_bf16_ss(tmem + i * nrows_w, ad, bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------ epilogue: RoPE, row max
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + (threadIdx.x & 31);  // tile row == TMEM lane
+    const int m = m0 + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    mbar_wait(acc_full, 0, 0x603);
+    tc_fence_after();
+    uint8_t* erow = sm + r * E_LD;
+    const __nv_bfloat16* crow = p.cos + (int64_t)m * HD;
+    const __nv_bfloat16* srow = p.sin + (int64_t)m * HD;
+    float mx = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {  // dims 32c..32c+31 and their RoPE partners 64+32c..
+      float c1[32], s1[32], c2[32], s2[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const uint4 a = *reinterpret_cast<const uint4*>(crow + 32 * c + i);
+        const uint4 b = *reinterpret_cast<const uint4*>(srow + 32 * c + i);
+        const uint4 a2 = *reinterpret_cast<const uint4*>(crow + 64 + 32 * c + i);
+        const uint4 b2 = *reinterpret_cast<const uint4*>(srow + 64 + 32 * c + i);
+        const __nv_bfloat16* ea = reinterpret_cast<const __nv_bfloat16*>(&a);
+        const __nv_bfloat16* eb = reinterpret_cast<const __nv_bfloat16*>(&b);
+        const __nv_bfloat16* ea2 = reinterpret_cast<const __nv_bfloat16*>(&a2);
+        const __nv_bfloat16* eb2 = reinterpret_cast<const __nv_bfloat16*>(&b2);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          c1[i + k] = __bfloat162float(ea[k]);
+          s1[i + k] = __bfloat162float(eb[k]);
+          c2[i + k] = __bfloat162float(ea2[k]);
+          s2[i + k] = __bfloat162float(eb2[k]);
+        }
+      }
+#pragma unroll 1
+      for (int j = 0; j < p.hpc; ++j) {
+        uint32_t x1[32], x2[32];
+        tmem_ld32(tmem + lane_base + j * HD + 32 * c, x1);
+        tmem_ld32(tmem + lane_base + j * HD + 64 + 32 * c, x2);
+        tmem_ld_wait();
+        uint32_t o1[16], o2[16];  // bf16 pairs
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float z1[2], z2[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const float a1 = bf16r(__uint_as_float(x1[i + k]));  // y = bf16(x W^T)
+            const float a2 = bf16r(__uint_as_float(x2[i + k]));
+            // rotate_half(y) = [-y2, y1]; z = bf16(bf16(y cos) + bf16(rotate_half(y) sin))
+            z1[k] = bf16r(__fadd_rn(bf16r(__fmul_rn(a1, c1[i + k])), bf16r(__fmul_rn(-a2, s1[i + k]))));
+            z2[k] = bf16r(__fadd_rn(bf16r(__fmul_rn(a2, c2[i + k])), bf16r(__fmul_rn(a1, s2[i + k]))));
+          }
+          mx = nanmax(mx, nanmax(absmax3(z1[0], z1[1], z2[0]), fabsf(z2[1])));
+          const __nv_bfloat162 h1 = __floats2bfloat162_rn(z1[0], z1[1]);
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(z2[0], z2[1]);
+          o1[i / 2] = *reinterpret_cast<const uint32_t*>(&h1);
+          o2[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        uint4* e1 = reinterpret_cast<uint4*>(erow + (j * HD + 32 * c) * 2);
+        uint4* e2 = reinterpret_cast<uint4*>(erow + (j * HD + 64 + 32 * c) * 2);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          e1[q] = make_uint4(o1[4 * q], o1[4 * q + 1], o1[4 * q + 2], o1[4 * q + 3]);
+          e2[q] = make_uint4(o2[4 * q], o2[4 * q + 1], o2[4 * q + 2], o2[4 * q + 3]);
+        }
+      }
+    }
+    rmax[r] = mx;
+  }
+  // ---- per-token global scale over all H heads: the cluster's row maxima
+  __syncwarp();
+  cluster_sync_all();  // every CTA's rmax is written
+  const uint32_t nrank = cluster_nctarank();
+  float gtok = 0.0f;
+  if (warp >= 2) {
+    const int r = (warp & 3) * 32 + (threadIdx.x & 31);
+    for (uint32_t k = 0; k < nrank; ++k) gtok = nanmax(gtok, ld_dsmem_f32(&rmax[r], k));
+  }
+  cluster_sync_all();  // no CTA reuses or leaves its shared memory while another reads it
+  if (warp >= 2) {
+    // ---- NVFP4 row quantizer on this CTA's 512 columns (fp4_quant_utils.py:118-169, fp32 arithmetic)
+    const int r = (warp & 3) * 32 + (threadIdx.x & 31);
+    const int64_t m = m0 + r;
+    const uint8_t* erow = sm + r * E_LD;
+    const float g = gtok;  // global_scale_aligned: g = rowmax, no division by global_sf_max
+    const float rg = g == 0.0f ? 0.0f : __frcp_rn(g);
+    const float r6 = __frcp_rn(6.0f);
+    if (p.g && cluster_ctarank() == 0) p.g[m] = g;
+    uint4* crow = reinterpret_cast<uint4*>(p.codes + m * (int64_t)(p.H * HD / 2) + n0 / 2);
+#pragma unroll 1
+    for (int kb4 = 0; kb4 < ncols / 64; ++kb4) {  // 4 blocks of 16 = one scale word, 32 code bytes
+      uint32_t words[8], sw = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int kb = 4 * kb4 + b;
+        const uint4 u0 = *reinterpret_cast<const uint4*>(erow + kb * 32);
+        const uint4 u1 = *reinterpret_cast<const uint4*>(erow + kb * 32 + 16);
+        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          v[2 * k] = __fmul_rn(__uint_as_float(w[k] << 16), rg);
+          v[2 * k + 1] = __fmul_rn(__uint_as_float(w[k] & 0xFFFF0000u), rg);
+        }
+        float am = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 16; k += 4) am = nanmax(am, nanmax(absmax3(v[k], v[k + 1], v[k + 2]), fabsf(v[k + 3])));
+        const uint8_t sb = e4m3_torch(__fmul_rn(am, r6));
+        const float rs = rcp_tab[sb & 0x7F];
+        const bool nan_block = (sb & 0x7F) == 0x7F;
+#pragma unroll
+        for (int k = 0; k < 16; k += 2) {
+          // x * recip(s) + 0: one rounding; + 0 turns -0.0 into +0.0 (torch.sign(-0.0) == 0)
+          const uint32_t byte = nan_block ? 0u : e2m1x2(__fmaf_rn(v[k], rs, 0.0f), __fmaf_rn(v[k + 1], rs, 0.0f));
+          if (k % 8 == 0) words[2 * b + k / 8] = 0u;
+          words[2 * b + k / 8] |= byte << (8 * ((k / 2) % 4));
+        }
+        sw |= (uint32_t)sb << (8 * b);
+      }
+      crow[2 * kb4] = make_uint4(words[0], words[1], words[2], words[3]);
+      crow[2 * kb4 + 1] = make_uint4(words[4], words[5], words[6], words[7]);
+      const int kbg = n0 / 16 + 4 * kb4;  // first of the four global blocks (multiple of 4)
+      *reinterpret_cast<uint32_t*>(p.scales + sf_tcgen05_offset(m, kbg, p.nkb4)) = sw;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace
+}  // namespace fp4
+
+using namespace fp4;
+
+extern "C" int fp4qkv_rope_quant(const void* x, const void* w, const void* cos, const void* sin, int M, int K, int H,
+                                 int T, uint8_t* codes, uint8_t* scales, float* g, void* stream) {
+  using namespace qkv;
+  clear_error();
+  if (!x || !w || !cos || !sin || !codes || !scales || !g) return set_error(FP4ATTN_ERR_ARG, "null pointer");
+  if (M <= 0 || K <= 0 || H <= 0 || T <= 0) return set_error(FP4ATTN_ERR_ARG, "bad shape");
+  if (T % BM || M % T) return set_error(FP4ATTN_ERR_UNSUPPORTED, "T must be a multiple of %d and divide M", BM);
+  if (K % BK) return set_error(FP4ATTN_ERR_UNSUPPORTED, "the hidden size must be a multiple of %d", BK);
+  const int hpc = H >= HPC ? HPC : H;
+  if (H % hpc || hpc == 3 || H / hpc > MAX_CLUSTER)
+    return set_error(FP4ATTN_ERR_UNSUPPORTED, "heads must be 1, 2 or a multiple of %d, at most %d", HPC,
+                     HPC * MAX_CLUSTER);
+  if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)cos | (uintptr_t)sin | (uintptr_t)codes | (uintptr_t)scales |
+       (uintptr_t)g) % 16)
+    return set_error(FP4ATTN_ERR_ARG, "buffers must be 16-byte aligned");
+  CUtensorMap mx, mw;
+  if (int e = encode_tiled_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK,
+                              BM, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  const int nrows_w = hpc * HD < 256 ? hpc * HD : 256;
+  if (int e = encode_tiled_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, (uint64_t)K, (uint64_t)H * HD, (uint64_t)K * 2,
+                              BK, nrows_w, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  QkvArgs a{reinterpret_cast<const __nv_bfloat16*>(cos), reinterpret_cast<const __nv_bfloat16*>(sin), codes, scales,
+            g, M, K, H, H * HD / 64, hpc};
+  const int csize = H / hpc;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(qkv_rope_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(qkv_rope_quant_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(M / BM), (unsigned)csize, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = (unsigned)csize;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, qkv_rope_quant_kernel, mx, mw, a) != cudaSuccess)
+    return check_launch("qkv_rope_quant_kernel");
+  return check_launch("qkv_rope_quant_kernel");
+}

@@ -39,8 +39,9 @@ extern "C" int fp4attn_version(void) { return 1; }
 // bounded wait inside a kernel gave up: (site << 16) | (CTA index + 1).
 extern "C" unsigned int fp4attn_device_status(int reset) {
   // first non-zero status of the kernels with bounded waits; every word is read (and reset if asked)
-  const unsigned int s[4] = {fp4::gemm_status(reset != 0), fp4::attn_status(reset != 0),
-                             fp4::quant_status(reset != 0), fp4::decode_status(reset != 0)};
+  const unsigned int s[5] = {fp4::gemm_status(reset != 0), fp4::attn_status(reset != 0),
+                             fp4::quant_status(reset != 0), fp4::decode_status(reset != 0),
+                             fp4::qkv_status(reset != 0)};
   for (unsigned int v : s)
     if (v) return v;
   return 0;

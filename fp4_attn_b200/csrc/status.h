@@ -21,4 +21,5 @@ unsigned int gemm_status(bool reset);
 unsigned int attn_status(bool reset);
 unsigned int quant_status(bool reset);
 unsigned int decode_status(bool reset);
+unsigned int qkv_status(bool reset);
 }  // namespace fp4

@@ -233,6 +233,22 @@ int fp4attn_forward_noalloc(const void* q, const void* k, const void* v, int in_
                             void* stream);
 
 /* ------------------------------------------------------------------------
+ * Q or K projection fused with RoPE and the NVFP4 row quantizer: the packed
+ * attention operand straight from the hidden states.  Replaces q_proj/k_proj
+ * (llama_patch.py:147-149), the row-wise fake-quant of the [B*T, H*D] view
+ * (llama_patch.py:167-194) and the rotation (llama_patch.py:210), with the
+ * rotation applied before the quantization (HF apply_rotary_pos_emb in bf16,
+ * op for op).  x: bf16 [M][K] hidden states (M = B*T tokens), w: bf16
+ * [H*128][K] (the nn.Linear weight), cos / sin: bf16 [M][128] per token.
+ * Writes codes [M][H*64], E4M3 scales in tcgen05 atoms (H*2 groups per
+ * 128-row block, the layout fp4attn_fwd_packed reads) and g [M].  T % 128 ==
+ * 0, M % T == 0, K % 32 == 0, H = 1, 2 or a multiple of 4 up to 64; 16-byte
+ * aligned buffers.  One launch, thread-block clusters of H/4 CTAs (one CTA
+ * for H <= 4). */
+int fp4qkv_rope_quant(const void* x, const void* w, const void* cos, const void* sin, int M, int K, int H, int T,
+                      uint8_t* codes, uint8_t* scales, float* g, void* stream);
+
+/* ------------------------------------------------------------------------
  * Decode: one new query token per sequence over an NVFP4 KV cache.  The
  * reference appends each call's fake-quantized K/V to the HF cache
  * (llama_patch.py:167-215) and attends over every cached key with P

@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the NVFP4 hot path on B200s; prints ONE JSON line (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attention|quantize]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attention|quantize|decode|qkv]
                     [--impl ours|reference]
 
 For N > 1 launch one rank per GPU with torch.distributed.run; ranks shard the
@@ -19,6 +19,16 @@ configurations; no dataset is read):
   0, 0.1% of entries x50) with a per-tensor scale amax/(448*6).  Metric:
   GB/s of algorithmic traffic, 2.5625 B per element (2 B read, 0.5 B codes,
   1/16 B scales).
+* decode -- one decode step over an NVFP4 KV cache: B=8, 32 query / 8 KV
+  heads, D=128, 32768 cached tokens (N(0,1) bf16 K/V appended in calls of
+  4096 tokens, seed 2 + rank).  Metric: GB/s of cache bytes read per step.
+* qkv -- the Q and K projections of one Llama-3-8B layer fused with RoPE and
+  the NVFP4 quantizer: T=4096 tokens, hidden 4096, 32 + 8 heads (hidden
+  N(0,1), weights N(0,0.02), seed 3 + rank).  Metric: TFLOP/s of the two
+  projections, 2*T*hidden*(Hq+Hkv)*128.
+
+decode and qkv measure the rows that extend the path (the NVFP4 KV cache,
+the fused projection); attention is the default.
 
 L2 (126 MB) is defeated by rotating through input/output buffer sets larger
 than L2 in total, so every step reads HBM.
@@ -51,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["attention", "quantize"], default=None)
+    ap.add_argument("--workload", choices=["attention", "quantize", "decode", "qkv"], default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -577,6 +587,203 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+class DecodeWorkload:
+    name = "decode"
+    metric = "NVFP4 KV-cache decode attention GB/s per B200 (cache bytes read per step)"
+    unit = "GB/s"
+    dtype = "nvfp4 K/V cache, mma.sync fp16-exact QK^T, fp32 P-hat x V"
+    B, Hq, Hkv, T, D = 8, 32, 8, 32768, 128
+    use_graph = True
+
+    def __init__(self, dev, cpu_only=False, rank=0, world=1):
+        self.cache_bytes = self.B * self.Hkv * self.T * (64 + 8 + 64 + 128) + 2 * self.B * self.T * 4
+        self.config = {"workload": "NVFP4 KV-cache decode: B=8, Hq=32, Hkv=8, D=128, 32768 cached tokens "
+                                   "(appended in calls of 4096), one new query token per sequence",
+                       "cache_bytes": self.cache_bytes, "global_batch": world * self.B,
+                       "shard": "batch rows 8r..8r+7 on rank r (own cache, seed 2 + r)",
+                       "l2": "cache 556 MB > L2"}
+        if cpu_only:
+            return
+        from fp4_attn_b200 import _lib
+        from fp4_attn_b200.kv_cache import NVFP4KVCache
+        self.lib = _lib
+        self.dev = dev
+        g = torch.Generator().manual_seed(2 + rank)
+        self.cache = NVFP4KVCache(self.B, self.Hkv, self.T, self.D, dev)
+        for _ in range(self.T // 4096):
+            k = torch.randn(self.B, self.Hkv, 4096, self.D, generator=g).bfloat16().to(dev)
+            v = torch.randn(self.B, self.Hkv, 4096, self.D, generator=g).bfloat16().to(dev)
+            self.cache.append(k, v)
+        self.nsets = 4
+        self.q_host = torch.randn(self.B, self.Hq, 1, self.D, generator=g).bfloat16().pin_memory()
+        self.qs = [torch.randn(self.B, self.Hq, 1, self.D, generator=g).bfloat16().to(dev) for _ in range(self.nsets)]
+        self.ws = torch.empty(_lib.load().fp4attn_decode_workspace_size(self.B, self.Hq, self.T), dtype=torch.uint8,
+                              device=dev)
+        self.out_host = torch.empty(self.B, 1, self.Hq, self.D).pin_memory()
+
+    def step(self, i, ev=None):
+        from fp4_attn_b200.kv_cache import decode_attention
+        decode_attention(self.qs[i % self.nsets], self.cache, workspace=self.ws)
+
+    def kernel(self, i):
+        self.step(i)
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D the new query tokens, decode, D2H the output."""
+        from fp4_attn_b200.kv_cache import decode_attention
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(self.nsets)
+        i %= self.nsets
+        self.pipe.step(i, lambda: self.qs[i].copy_(self.q_host, non_blocking=True),
+                       lambda: decode_attention(self.qs[i], self.cache, workspace=self.ws),
+                       lambda o: self.out_host.copy_(o, non_blocking=True))
+
+    e2e_h2d = property(lambda self: self.q_host.numel() * 2)
+    e2e_d2h = property(lambda self: self.out_host.numel() * 4)
+
+    def value(self, seconds_per_step, world):
+        return world * self.cache_bytes / seconds_per_step / 1e9
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        achieved = self.cache_bytes / kernel_s / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "kernel": "decode step (query quantize, scores, pv, combine)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_src} copy bandwidth", "algorithmic_bytes_per_launch": self.cache_bytes,
+                "traffic": profile_traffic("decode_pv_kernel_B8_T32768"),
+                "traffic_source": "profiles/decode_pv_kernel_B8_T32768.md: ncu dram bytes of decode_pv_kernel"}
+
+    def cpu_sample(self, reps=None):
+        """The reference's CPU path (torch ops): one sequence, one KV-head group, 4096 cached keys."""
+        from oracle import torch_port as tp
+        g = torch.Generator().manual_seed(2)
+        L = 4096
+        q = torch.randn(1, 4, 1, self.D, generator=g).bfloat16()
+        k = torch.randn(1, 1, L, self.D, generator=g).bfloat16()
+        v = torch.randn(1, 1, L, self.D, generator=g).bfloat16()
+        # the cache's values: K row mode, V along tokens (column mode on the transposed view)
+        Kf = tp.fused_qdq(k.reshape(L, self.D).float()).view(1, 1, L, self.D)
+        Vf = tp.fused_qdq(v.reshape(L, self.D).float().T, aligned=False).T.reshape(1, 1, L, self.D)
+        sample_bytes = L * (64 + 8 + 64 + 128 + 8)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            Qf = tp.fused_qdq(q.reshape(1, -1).float()).view(1, 4, 1, self.D)
+            tp.eager_attention(Qf, Kf, Vf, False, self.D ** -0.5)
+            n += 1
+            el = time.perf_counter() - t0
+            if (reps and n >= reps) or (not reps and (el > 10.0 or n >= 200)):
+                break
+        return sample_bytes * n / el / 1e9, f"1 sequence x 1 KV-head group (4 query heads) x 4096 keys, x{n}"
+
+
+class QkvWorkload:
+    name = "qkv"
+    metric = "Q/K projection + RoPE + NVFP4 quantize TFLOP/s per B200"
+    unit = "TFLOP/s"
+    dtype = "bf16 projection (tcgen05 kind::f16, fp32 accumulate) -> bf16 RoPE -> nvfp4"
+    T, K, Hq, Hkv, D = 4096, 4096, 32, 8, 128
+    use_graph = True
+
+    def __init__(self, dev, cpu_only=False, rank=0, world=1):
+        self.flops = 2 * self.T * self.K * (self.Hq + self.Hkv) * self.D
+        self.config = {"workload": "Llama-3-8B layer Q/K projections fused with RoPE and NVFP4 quantize: "
+                                   "T=4096 tokens, hidden 4096, 32 + 8 heads of 128",
+                       "flops_per_step": self.flops, "global_batch": world,
+                       "shard": "one sequence of 4096 tokens per rank (seed 3 + r)"}
+        if cpu_only:
+            return
+        self.dev = dev
+        g = torch.Generator().manual_seed(3 + rank)
+        per_set = self.T * self.K * 2
+        self.nsets = max(2, int(2 * L2_BYTES // per_set) + 1)
+        self.x_host = torch.randn(self.T, self.K, generator=g).bfloat16().pin_memory()
+        self.xs = [self.x_host.to(dev) for _ in range(self.nsets)]
+        self.wq = (torch.randn(self.Hq * self.D, self.K, generator=g) * 0.02).bfloat16().to(dev)
+        self.wk = (torch.randn(self.Hkv * self.D, self.K, generator=g) * 0.02).bfloat16().to(dev)
+        inv = 1.0 / (10000.0 ** (torch.arange(0, self.D, 2, dtype=torch.float32) / self.D))
+        ang = torch.arange(self.T, dtype=torch.float32)[:, None] * inv[None, :]
+        emb = torch.cat((ang, ang), -1)
+        self.cos, self.sin = emb.cos().bfloat16().to(dev), emb.sin().bfloat16().to(dev)
+        self.qbuf = [self._bufs(self.Hq) for _ in range(self.nsets)]
+        self.kbuf = [self._bufs(self.Hkv) for _ in range(self.nsets)]
+        self.codes_host = torch.empty(self.T, self.Hq * self.D // 2, dtype=torch.uint8).pin_memory()
+        self.config["l2"] = f"rotating {self.nsets} hidden-state sets (> L2)"
+
+    def _bufs(self, H):
+        d = self.dev
+        return (torch.empty(self.T, H * self.D // 2, dtype=torch.uint8, device=d),
+                torch.empty(self.T // 128 * H * 2 * 512, dtype=torch.uint8, device=d),
+                torch.empty(self.T, dtype=torch.float32, device=d))
+
+    def step(self, i, ev=None):
+        from fp4_attn_b200.qkv import rope_quant_projection
+        i %= self.nsets
+        rope_quant_projection(self.xs[i], self.wq, self.cos, self.sin, self.T, *self.qbuf[i])
+        rope_quant_projection(self.xs[i], self.wk, self.cos, self.sin, self.T, *self.kbuf[i])
+
+    def kernel(self, i):
+        from fp4_attn_b200.qkv import rope_quant_projection
+        i %= self.nsets
+        rope_quant_projection(self.xs[i], self.wq, self.cos, self.sin, self.T, *self.qbuf[i])
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D the hidden states, both projections, D2H the packed Q codes."""
+        from fp4_attn_b200.qkv import rope_quant_projection
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(self.nsets)
+        i %= self.nsets
+
+        def compute():
+            rope_quant_projection(self.xs[i], self.wk, self.cos, self.sin, self.T, *self.kbuf[i])
+            return rope_quant_projection(self.xs[i], self.wq, self.cos, self.sin, self.T, *self.qbuf[i])
+
+        self.pipe.step(i, lambda: self.xs[i].copy_(self.x_host, non_blocking=True), compute,
+                       lambda r: self.codes_host.copy_(r[0], non_blocking=True))
+
+    e2e_h2d = property(lambda self: self.x_host.numel() * 2)
+    e2e_d2h = property(lambda self: self.codes_host.numel())
+
+    def value(self, seconds_per_step, world):
+        return world * self.flops / seconds_per_step / 1e12
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        fl = 2 * self.T * self.K * self.Hq * self.D
+        achieved = fl / kernel_s / 1e12
+        peak = peaks["bf16_tflops"]
+        return {"bound": "tensor", "kernel": "qkv_rope_quant_kernel (Q projection, 32 heads)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_src} dense bf16", "algorithmic_flops_per_launch": fl,
+                "traffic": profile_traffic("qkv_rope_quant_kernel_T4096_hidden4096_Hq32"),
+                "traffic_source": "profiles/qkv_rope_quant_kernel_T4096_hidden4096_Hq32.md: ncu dram bytes"}
+
+    def cpu_sample(self, reps=None):
+        """The reference's CPU path (torch ops): projection, bf16 RoPE and the quantizer on 256 tokens."""
+        from oracle import torch_port as tp
+        g = torch.Generator().manual_seed(3)
+        n_tok = 256
+        x = torch.randn(n_tok, self.K, generator=g).bfloat16()
+        w = (torch.randn((self.Hq + self.Hkv) * self.D, self.K, generator=g) * 0.02).bfloat16()
+        inv = 1.0 / (10000.0 ** (torch.arange(0, self.D, 2, dtype=torch.float32) / self.D))
+        ang = torch.arange(n_tok, dtype=torch.float32)[:, None] * inv[None, :]
+        emb = torch.cat((ang, ang), -1)
+        cos, sin = emb.cos().bfloat16()[:, None], emb.sin().bfloat16()[:, None]
+        fl = 2 * n_tok * self.K * (self.Hq + self.Hkv) * self.D
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            y = torch.nn.functional.linear(x, w).view(n_tok, -1, self.D)
+            rot = torch.cat((-y[..., 64:], y[..., :64]), -1)
+            z = (y * cos) + (rot * sin)
+            tp.fused_qdq(z[:, :self.Hq].reshape(n_tok, -1).float())
+            tp.fused_qdq(z[:, self.Hq:].reshape(n_tok, -1).float())
+            n += 1
+            el = time.perf_counter() - t0
+            if (reps and n >= reps) or (not reps and (el > 10.0 or n >= 20)):
+                break
+        return fl * n / el / 1e12, f"256 tokens (of 4096), both projections x{n}, torch bf16 ops + fp32 quantizer"
+
+
 def default_workload():
     return "attention"
 
@@ -590,6 +797,10 @@ def make_workload(name, dev, cpu_only=False, rank=0, world=1):
             w.config = {"workload": "quantize bf16 [4096,4096], per-tensor scale amax/2688, block 16"}
             return w
         return QuantizeWorkload(dev, rank, world)
+    if name == "decode":
+        return DecodeWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
+    if name == "qkv":
+        return QkvWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
     return AttentionWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
 
 

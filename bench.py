@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the NVFP4 hot path on B200s; prints ONE JSON line (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attention|quantize|decode|qkv]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload attention|quantize|decode|qkv|prefill|weights|llama]
                     [--impl ours|reference]
 
 For N > 1 launch one rank per GPU with torch.distributed.run; ranks shard the
@@ -26,9 +27,23 @@ configurations; no dataset is read):
   the NVFP4 quantizer: T=4096 tokens, hidden 4096, 32 + 8 heads (hidden
   N(0,1), weights N(0,0.02), seed 3 + rank).  Metric: TFLOP/s of the two
   projections, 2*T*hidden*(Hq+Hkv)*128.
+* prefill -- long-context prefill: B=4, 64 query / 8 KV heads, D=128,
+  T=32768, causal, q/k/v N(0,1)*0.5 with a per-(kv-head, channel) N(0,2)
+  bias on k (seed 2).  Strong scaling: the 32 (batch, KV-head) units are
+  split over the ranks in contiguous blocks (1, 2, 4 or 8 ranks).  Metric:
+  TFLOP/s of the whole job, 70.37 TFLOP per step.
+* weights -- per-tensor NVFP4 quantize of the linear weights of a
+  Llama-3-70B-shaped stack (q/o 8192x8192, k/v 1024x8192, gate/up
+  28672x8192, down 8192x28672; bf16 N(0,0.02), tensor t from seed 4 + t).
+  Weak scaling by whole layers: 10 layers per rank, so 8 ranks quantize the
+  80-layer stack.  Metric: GB/s of algorithmic traffic (2.5625 B/element).
+* llama -- one forward of a Llama-2-7B-shaped model (random bf16 weights
+  N(0,0.02), seed 3) with the FP4 attention patch installed, batch 8 x 2048
+  token ids; strong scaling over the batch.  Metric: tokens/s.
 
 decode and qkv measure the rows that extend the path (the NVFP4 KV cache,
-the fused projection); attention is the default.
+the fused projection); prefill and weights the long-context and weight
+configurations, llama the patched model; attention is the default.
 
 L2 (126 MB) is defeated by rotating through input/output buffer sets larger
 than L2 in total, so every step reads HBM.
@@ -61,8 +76,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["attention", "quantize", "decode", "qkv"], default=None)
+    ap.add_argument("--workload", choices=["attention", "quantize", "decode", "qkv", "prefill", "weights",
+                                                     "llama"],
+                    default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=10,
+                    help="weights workload: layers per rank (10 = the 80-layer stack at 8 ranks)")
     return ap.parse_args()
 
 
@@ -451,7 +470,7 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     wl_name = args.workload or default_workload()
-    wl = make_workload(wl_name, dev, rank=rank, world=world)
+    wl = make_workload(wl_name, dev, rank=rank, world=world, layers=args.layers)
     peaks, peak_src = measured_peaks()
     K, W = args.steps, args.warmup
     for i in range(W):
@@ -547,7 +566,8 @@ def run_ours(args, world, rank, local):
     line = {
         "metric": wl.metric, "value": round(wl.value(sec_per_step, world), 3), "unit": wl.unit,
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
+        "dtype": wl.dtype,
         "data": "synthetic (seeded; shapes/distributions of the named configuration)",
         "config": dict(wl.config, parallelism=f"{world} independent shard(s), no data-path collective",
                        timing="CUDA graph replay per step" if getattr(wl, "use_graph", False) else "stream launches"),
@@ -567,7 +587,7 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     wl_name = args.workload or default_workload()
-    wl = make_workload(wl_name, None, cpu_only=True)
+    wl = make_workload(wl_name, None, cpu_only=True, layers=args.layers)
     torch.set_num_threads(os.cpu_count() or 1)
     for _ in range(args.warmup):
         wl.cpu_sample(reps=1)
@@ -578,7 +598,8 @@ def run_reference(args, world, rank):
     v = statistics.median(vals)
     line = {
         "metric": wl.metric, "value": round(v, 5), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
+        "vs_baseline": None,
         "dtype": wl.dtype, "data": "synthetic", "config": wl.config, "impl": "reference",
         "cpu_baseline": {"value": round(v, 5), "unit": wl.unit, "kind": "port", "cores": torch.get_num_threads(),
                          "sample": sample},
@@ -784,11 +805,360 @@ class QkvWorkload:
         return fl * n / el / 1e12, f"256 tokens (of 4096), both projections x{n}, torch bf16 ops + fp32 quantizer"
 
 
+class PrefillWorkload(AttentionWorkload):
+    """Long-context prefill, strong scaling: the fixed job of 4 x 8 (batch, KV-head) units is split
+    over the ranks in contiguous blocks (fp4_attn_b200.shard.attention_shard)."""
+    name = "prefill"
+    metric = "NVFP4 attention forward TFLOP/s (long-context prefill), % of dense FP4 tensor peak"
+    scaling = "strong"
+    B_JOB, Hq_JOB, Hkv_JOB, T, D = 4, 64, 8, 32768, 128
+
+    def __init__(self, dev, cpu_only=False, rank=0, world=1):
+        from fp4_attn_b200 import shard
+        units = shard.attention_shard(self.B_JOB, self.Hq_JOB, self.Hkv_JOB, world, rank)
+        bs, hs = sorted({u.b for u in units}), sorted({u.hk for u in units})
+        if len(units) != len(bs) * len(hs) or bs != list(range(bs[0], bs[-1] + 1)) or \
+                hs != list(range(hs[0], hs[-1] + 1)):
+            raise ValueError(f"{world} ranks do not split the 32 prefill units into (batch x kv-head) blocks")
+        G = self.Hq_JOB // self.Hkv_JOB
+        self.b0, self.b1, self.h0, self.h1 = bs[0], bs[-1] + 1, hs[0], hs[-1] + 1
+        self.B, self.Hkv, self.Hq = self.b1 - self.b0, self.h1 - self.h0, (self.h1 - self.h0) * G
+        self.flops = 4 * self.B * self.Hq * self.T * self.T * self.D / 2  # causal, this rank's units
+        self.config = {"workload": "NVFP4 attention fwd, long-context prefill: B=4, Hq=64, Hkv=8, D=128, T=32768, "
+                                   "causal, q/k/v N(0,1)*0.5 with a per-(kv-head, channel) N(0,2) bias on k, "
+                                   "single-slice Q/P quantization, bf16 output",
+                       "flops_job": 4 * self.B_JOB * self.Hq_JOB * self.T * self.T * self.D / 2,
+                       "global_batch": self.B_JOB,
+                       "shard": f"units (b {self.b0}..{self.b1 - 1}) x (kv-head {self.h0}..{self.h1 - 1}) on rank "
+                                f"{rank}; a rank holding part of a batch row quantizes Q/K per token over its "
+                                f"own heads"}
+        if cpu_only:
+            return
+        from fp4_attn_b200 import attention as A
+        self.A = A
+        self.dev = dev
+        g = torch.Generator(dev).manual_seed(2)  # the whole job's inputs on every rank, then this rank's block
+        q = torch.randn(self.B_JOB, self.Hq_JOB, self.T, self.D, device=dev, generator=g) * 0.5
+        q = q[self.b0:self.b1, self.h0 * G:self.h1 * G].bfloat16()
+        k = torch.randn(self.B_JOB, self.Hkv_JOB, self.T, self.D, device=dev, generator=g) * 0.5
+        bias = torch.randn(self.Hkv_JOB, self.D, device=dev, generator=g) * 2.0
+        k = (k + bias[None, :, None, :])[self.b0:self.b1, self.h0:self.h1].bfloat16()
+        v = (torch.randn(self.B_JOB, self.Hkv_JOB, self.T, self.D, device=dev, generator=g) * 0.5)
+        v = v[self.b0:self.b1, self.h0:self.h1].bfloat16()
+        self.host = [t.cpu().pin_memory() for t in (q, k, v)]
+        self.nsets = 2  # inputs (2.7 GB at one rank) are far larger than L2; two sets let e2e copies overlap
+        self.sets = [(q, k, v)] + [tuple(t.clone() for t in (q, k, v)) for _ in range(self.nsets - 1)]
+        del q, k, v
+        self.ws = [A.AttentionWorkspace(self.B, self.Hq, self.Hkv, self.T, self.D, dev) for _ in range(self.nsets)]
+        self.out = [torch.empty(self.B, self.T, self.Hq, self.D, device=dev, dtype=torch.bfloat16)
+                    for _ in range(self.nsets)]
+        self.out_bf16 = self.out
+        self.out_host = torch.empty(self.B, self.T, self.Hq, self.D, dtype=torch.bfloat16).pin_memory()
+        self.config["l2"] = "inputs 2.7 GB per set > L2"
+
+    def value(self, seconds_per_step, world):
+        return world * self.flops / seconds_per_step / 1e12
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        r = super().kernel_roofline(kernel_s, peaks, peak_src)
+        r["traffic"], r["traffic_source"] = None, "not captured at this shape"
+        return r
+
+    def cpu_sample(self, reps=None):
+        """The reference's CPU path (torch ops) on the last 256 query rows of one KV-head group (8 query
+        heads) of batch row 0 against all 32768 keys; that head's K/V fake-quant runs in every repetition."""
+        from oracle import torch_port as tp
+        L, rows, G, D = self.T, 256, self.Hq_JOB // self.Hkv_JOB, self.D
+        g = torch.Generator().manual_seed(2)
+        q = (torch.randn(rows, G * D, generator=g) * 0.5).bfloat16()
+        k = (torch.randn(L, D, generator=g) * 0.5 + torch.randn(D, generator=g) * 2.0).bfloat16()
+        v = (torch.randn(L, D, generator=g) * 0.5).bfloat16()
+        flops = 4 * D * G * sum(t + 1 for t in range(L - rows, L))
+        Qf = torch.zeros(1, G, L, D)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            Qf[0, :, L - rows:] = tp.fused_qdq(q.float()).view(rows, G, D).transpose(0, 1)
+            Kf = tp.fused_qdq(k.float()).view(1, 1, L, D)
+            Vf = tp.fused_qdq(v.float().T, aligned=False).T.reshape(1, 1, L, D)
+            tp.eager_attention(Qf, Kf, Vf, True, D ** -0.5, q_rows=slice(L - rows, L))
+            n += 1
+            el = time.perf_counter() - t0
+            if (reps and n >= reps) or (not reps and (el > 10.0 or n >= 5)):
+                break
+        return flops * n / el / 1e12, f"1 KV-head group (8 query heads), last {rows} of 32768 query rows x{n}"
+
+
+LAYER_70B = [("q", 8192, 8192), ("k", 1024, 8192), ("v", 1024, 8192), ("o", 8192, 8192),
+             ("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672)]
+
+
+class WeightsWorkload:
+    """Per-tensor NVFP4 quantization of the linear weights of a Llama-3-70B-shaped stack.  Weak
+    scaling by whole layers: rank r quantizes layers 10r..10r+9, so 8 ranks cover the 80 layers
+    with no exchange (each tensor's max is reduced on the rank that holds it)."""
+    name = "weights"
+    metric = "NVFP4 weight quantize GB/s per B200 (Llama-3-70B-shaped stack), % of HBM roofline"
+    unit = "GB/s"
+    dtype = "bf16->nvfp4 (fp32 arithmetic)"
+    LAYERS_PER_RANK = 10
+    use_graph = True
+
+    def __init__(self, dev, cpu_only=False, rank=0, world=1, layers=10):
+        self.LAYERS_PER_RANK = layers
+        per_layer = sum(m * n for _, m, n in LAYER_70B)
+        self.elems = self.LAYERS_PER_RANK * per_layer
+        self.algo_bytes = self.elems * (2 + 0.5 + 1 / 16)
+        l0 = rank * self.LAYERS_PER_RANK
+        self.config = {"workload": "NVFP4 quantize of the linear weights of Llama-3-70B layers (q/o 8192x8192, "
+                                   "k/v 1024x8192, gate/up 28672x8192, down 8192x28672), bf16 N(0,0.02), "
+                                   "per-tensor scale amax/2688, block 16",
+                       "elements": self.elems, "layers": f"{l0}..{l0 + self.LAYERS_PER_RANK - 1}",
+                       "global_batch": world * self.LAYERS_PER_RANK,
+                       "shard": f"{layers} whole layers per rank (10 per rank at 8 ranks = the 80-layer stack), "
+                                f"tensor t from seed 4 + t",
+                       "l2": f"{layers * 1.71:.1f} GB of weights per rank > L2"}
+        if cpu_only:
+            return
+        from fp4_attn_b200 import _lib
+        self.lib = _lib
+        self.dev = dev
+        self.nsets = 1
+        self.t = []  # (weight, codes, scales, g) per tensor
+        for l in range(l0, l0 + self.LAYERS_PER_RANK):
+            for idx, (_, m, n) in enumerate(LAYER_70B):
+                gen = torch.Generator(dev).manual_seed(4 + 7 * l + idx)
+                w = (torch.randn(m, n, device=dev, generator=gen) * 0.02).bfloat16()
+                self.t.append((w, torch.empty(m, n // 2, dtype=torch.uint8, device=dev),
+                               torch.empty(m, n // 16, dtype=torch.uint8, device=dev),
+                               torch.empty(1, dtype=torch.float32, device=dev)))
+        self.stream = torch.cuda.current_stream(dev).cuda_stream
+        # e2e: one layer's tensors in pinned host memory, copied into every layer's device buffers
+        self.host = [w.cpu().pin_memory() for w, *_ in self.t[:len(LAYER_70B)]]
+        self.codes_host = [c.cpu().pin_memory() for _, c, *_ in self.t[:len(LAYER_70B)]]
+        self.scales_host = [s.cpu().pin_memory() for _, _, s, _ in self.t[:len(LAYER_70B)]]
+
+    def _quantize(self, w, codes, scales, g, gmode=3):
+        m, n = w.shape
+        self.lib.call("fp4q_quantize", w.data_ptr(), 1, 1, m, 1, n, 0, n, 0, m, gmode, 0, 2688.0, codes.data_ptr(),
+                      n // 2, scales.data_ptr(), 0, n // 16, g.data_ptr(), None, 0, 0, self.stream)
+
+    def step(self, i, ev=None):
+        for w, c, s, g in self.t:
+            self._quantize(w, c, s, g)
+
+    def kernel(self, i):
+        """The row kernel alone on one gate weight [28672, 8192] (its per-tensor g already reduced)."""
+        self._quantize(*self.t[4], gmode=3 | 0x10)
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D every weight, quant.quantize per tensor, D2H codes + scales."""
+        from fp4_attn_b200 import quant
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(1)
+        nl = len(LAYER_70B)
+
+        def h2d():
+            for j, (w, *_) in enumerate(self.t):
+                w.copy_(self.host[j % nl], non_blocking=True)
+
+        def compute():
+            return [quant.quantize(w, "tensor", 2688.0) for w, *_ in self.t]
+
+        def d2h(res):
+            for j, pk in enumerate(res):
+                self.codes_host[j % nl].copy_(pk.codes, non_blocking=True)
+                self.scales_host[j % nl].copy_(pk.scales, non_blocking=True)
+
+        self.pipe.step(0, h2d, compute, d2h)
+
+    e2e_h2d = property(lambda self: self.elems * 2)
+    e2e_d2h = property(lambda self: self.elems // 2 + self.elems // 16)
+
+    def value(self, seconds_per_step, world):
+        return world * self.algo_bytes / seconds_per_step / 1e9
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        m, n = LAYER_70B[4][1:]
+        algo = m * n * (2 + 0.5 + 1 / 16)
+        achieved = algo / kernel_s / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "kernel": "quant_rows_vec_kernel on a [28672, 8192] weight (g given)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_src} copy bandwidth", "algorithmic_bytes_per_launch": algo,
+                "traffic": profile_traffic("quant_rows_vec_kernel_28672x8192_tensor"),
+                "traffic_source": "profiles/quant_rows_vec_kernel_28672x8192_tensor.md: ncu dram bytes per launch"}
+
+    def cpu_sample(self, reps=None):
+        """The reference's CPU path (torch ops) on the k weight [1024, 8192] of layer 0, per-tensor scale."""
+        from oracle import torch_port as tp
+        g = torch.Generator().manual_seed(4 + 1)
+        w = (torch.randn(1024, 8192, generator=g) * 0.02).bfloat16()
+        one = torch.tensor(1.0)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            gs = w.abs().max().float() * (one / torch.tensor(2688.0))
+            tp.fused_qdq(w.float() * (one / gs), aligned=True, global_sf_max=None) * gs
+            n += 1
+            el = time.perf_counter() - t0
+            if (reps and n >= reps) or (not reps and (el > 10.0 or n >= 30)):
+                break
+        return w.numel() * (2 + 0.5 + 1 / 16) * n / el / 1e9, f"k weight [1024, 8192] of layer 0 x{n} (torch ops)"
+
+
+def llama2_7b_config():
+    from transformers import LlamaConfig
+    return LlamaConfig(hidden_size=4096, intermediate_size=11008, num_hidden_layers=32, num_attention_heads=32,
+                       num_key_value_heads=32, head_dim=128, vocab_size=32000, max_position_embeddings=4096,
+                       rope_theta=10000.0, rms_norm_eps=1e-5, attn_implementation="eager")
+
+
+class LlamaWorkload:
+    """One forward pass of a Llama-2-7B-shaped model with the FP4 attention patch installed
+    (fp4_attn_b200.llama_patch.install, as eval.py installs the reference's).  Strong scaling:
+    the batch of 8 sequences is split over the ranks."""
+    name = "llama"
+    metric = "Llama-2-7B forward tokens/s per B200 with the NVFP4 attention patch"
+    unit = "tokens/s"
+    dtype = "bf16 model (torch GEMMs), NVFP4 attention (tcgen05), single-slice Q/P"
+    scaling = "strong"
+    B_JOB, T = 8, 2048
+    use_graph = False  # the patched forward checks the mask and NaNs on the host every layer
+
+    def __init__(self, dev, cpu_only=False, rank=0, world=1):
+        if self.B_JOB % world:
+            raise ValueError(f"{world} ranks do not split a batch of {self.B_JOB}")
+        self.B = self.B_JOB // world
+        self.b0 = rank * self.B
+        self.attn_flops = 4 * self.B * 32 * self.T * self.T * 128 / 2  # one layer, causal
+        self.config = {"workload": "Llama-2-7B (32 layers, hidden 4096, 32 heads MHA, SwiGLU 11008, vocab 32000), "
+                                   "random bf16 weights N(0,0.02) from seed 3, FP4 attention patch, one forward "
+                                   "of batch 8 x 2048 token ids (seed 3), use_cache=False",
+                       "global_batch": self.B_JOB, "seq_len": self.T,
+                       "shard": f"sequences {self.b0}..{self.b0 + self.B - 1} on rank {rank}",
+                       "quant": "FP4_USE_DUAL_QUANT_Q=false, FP4_USE_DUAL_QUANT_ATTN=false"}
+        os.environ["FP4_USE_DUAL_QUANT_Q"] = "false"
+        os.environ["FP4_USE_DUAL_QUANT_ATTN"] = "false"
+        if cpu_only:
+            return
+        from transformers import LlamaForCausalLM
+        from fp4_attn_b200 import llama_patch as lp
+        self.dev = dev
+        self.lp = lp
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            with torch.device(dev):
+                self.model = LlamaForCausalLM(llama2_7b_config())
+        finally:
+            torch.set_default_dtype(torch.float32)
+        gen = torch.Generator(dev).manual_seed(3)
+        with torch.no_grad():
+            for prm in self.model.parameters():
+                prm.normal_(0.0, 0.02, generator=gen)
+        self.model.eval()
+        ids = torch.randint(0, 32000, (self.B_JOB, self.T), generator=torch.Generator().manual_seed(3))
+        self.ids_host = ids[self.b0:self.b0 + self.B].contiguous().pin_memory()
+        self.ids = self.ids_host.to(dev)
+        self.out_host = torch.empty(self.B, 32000, dtype=torch.bfloat16).pin_memory()
+        self._ev = None
+
+        def timed(module, *a, **kw):  # layer 0's attention call between the step's events
+            if self._ev is not None and module.layer_idx == 0:
+                self._ev[0].record()
+                r = lp.fp4_eager_attention(module, *a, **kw)
+                self._ev[1].record()
+                return r
+            return lp.fp4_eager_attention(module, *a, **kw)
+
+        lp.attention_interface = timed
+        lp.install()
+        self.nsets = 1
+        self.config["l2"] = "13.5 GB of weights per forward > L2"
+
+    def _forward(self, ids):
+        with torch.no_grad():
+            return self.model(input_ids=ids, use_cache=False).logits
+
+    def step(self, i, ev=None):
+        self._ev = ev
+        self._forward(self.ids)
+        self._ev = None
+
+    def kernel(self, i):
+        self.step(i)
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D the token ids, the patched forward, D2H the last position's logits."""
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(1)
+        self.pipe.step(0, lambda: self.ids.copy_(self.ids_host, non_blocking=True),
+                       lambda: self._forward(self.ids)[:, -1], lambda o: self.out_host.copy_(o, non_blocking=True))
+
+    e2e_h2d = property(lambda self: self.ids_host.numel() * 8)
+    e2e_d2h = property(lambda self: self.out_host.numel() * 2)
+
+    def value(self, seconds_per_step, world):
+        return world * self.B * self.T / seconds_per_step
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        achieved = self.attn_flops / kernel_s / 1e12
+        peak = 4 * peaks["bf16_tflops"]
+        return {"bound": "tensor", "kernel": "layer 0's FP4 attention call (Q/K quantize, V-hat prep, fp4_attn_kernel)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
+                "algorithmic_flops_per_launch": self.attn_flops, "traffic": None,
+                "traffic_source": "not captured at this shape"}
+
+    def cpu_sample(self, reps=None):
+        """The reference's CPU path: one decoder layer (torch ops, FP4 attention simulated with the
+        reference's fake-quant) on one 2048-token sequence, plus the LM head; x32 layers."""
+        from transformers.models.llama.modeling_llama import LlamaDecoderLayer, LlamaRotaryEmbedding
+        from fp4_attn_b200 import llama_patch as lp
+        from oracle import torch_port as tp
+        cfg = llama2_7b_config()
+        torch.manual_seed(3)
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            layer = LlamaDecoderLayer(cfg, layer_idx=0).eval()
+            head = torch.nn.Linear(4096, 32000, bias=False)
+        finally:
+            torch.set_default_dtype(torch.float32)
+        rot = LlamaRotaryEmbedding(cfg)
+        h = (torch.randn(1, self.T, 4096) * 0.02).bfloat16()
+        pe = rot(h, torch.arange(self.T)[None])
+
+        def cpu_attn(module, q, k, v, mask, scaling, dropout=0.0, **kw):
+            return tp.attention(q, k, v, True, float(scaling)).to(q.dtype), None
+
+        saved = lp.attention_interface
+        lp.attention_interface = cpu_attn
+        lp.install()
+        try:
+            t0 = time.perf_counter()
+            n = 0
+            with torch.no_grad():
+                while True:
+                    t1 = time.perf_counter()
+                    layer(h, position_embeddings=pe)
+                    t2 = time.perf_counter()
+                    head(h)
+                    t3 = time.perf_counter()
+                    n += 1
+                    if reps and n >= reps or not reps and (t3 - t0 > 10.0 or n >= 3):
+                        break
+        finally:
+            lp.uninstall()
+            lp.attention_interface = saved
+        return self.T / (32 * (t2 - t1) + (t3 - t2)), \
+            f"1 decoder layer + LM head on 1 x 2048 tokens (last of x{n}), layer time x32"
+
+
 def default_workload():
     return "attention"
 
 
-def make_workload(name, dev, cpu_only=False, rank=0, world=1):
+def make_workload(name, dev, cpu_only=False, rank=0, world=1, layers=10):
     if name == "quantize":
         if cpu_only:
             w = QuantizeWorkload.__new__(QuantizeWorkload)
@@ -801,6 +1171,12 @@ def make_workload(name, dev, cpu_only=False, rank=0, world=1):
         return DecodeWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
     if name == "qkv":
         return QkvWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
+    if name == "prefill":
+        return PrefillWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
+    if name == "weights":
+        return WeightsWorkload(dev, cpu_only=cpu_only, rank=rank, world=world, layers=layers)
+    if name == "llama":
+        return LlamaWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
     return AttentionWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
 
 

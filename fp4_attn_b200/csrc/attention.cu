@@ -50,7 +50,10 @@ FP4_DEFINE_STATUS_READER(attn_status)
 
 namespace attn {
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int NK = 4;   // K stages (codes + scale atoms + g)
+#ifndef FP4ATTN_K_STAGES
+#define FP4ATTN_K_STAGES 4
+#endif
+constexpr int NK = FP4ATTN_K_STAGES;  // K stages (codes + scale atoms + g)
 constexpr int NV = 2;   // V-hat stages, one 128-key tile each (hi and lo planes)
 constexpr int NWG = 4;  // softmax warpgroups; warpgroup q owns key columns 32q .. 32q+31
 constexpr int THREADS = 128 + NWG * 128;
@@ -71,9 +74,11 @@ constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 // TMEM columns: S0, S1, O, P (fp16, single-buffered; warpgroup q writes columns
 // 16q..16q+15), Q scale atoms, K scale atoms per stage, the residual Q
-// slice's scale atoms (496 of 512 columns).  With dual-slice Q, S0 and S1
+// slice's scale atoms (456 + 8 * (NK + 1) of 512 columns).  With dual-slice Q, S0 and S1
 // hold the two slices' products of the same key tile (S single-buffered).
-constexpr uint32_t T_S = 0, T_O = 256, T_P = 384, T_SFA = 448, T_SFB = 456, T_SFA_LO = 488;
+constexpr uint32_t T_S = 0, T_O = 256, T_P = 384, T_SFA = 448, T_SFB = 456, T_SFA_LO = T_SFB + 8 * NK;
+static_assert(T_SFA_LO + 8 <= TMEM_COLS, "K scale atoms of every stage must fit in TMEM");
+static_assert(SMEM_BYTES <= 232448, "shared memory map exceeds the 227 KB a CTA can have");
 }  // namespace attn
 
 struct AttnArgs {
@@ -169,17 +174,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bar + 0;
   uint64_t* q_empty = bar + 1;
-  uint64_t* k_full = bar + 2;    // [NK]
-  uint64_t* k_empty = bar + 6;   // [NK]
-  uint64_t* v_full = bar + 10;   // [NV]
-  uint64_t* v_empty = bar + 14;  // [NV]
-  uint64_t* s_full = bar + 18;   // [2] S buffer written (MMA commit)
-  uint64_t* s_free = bar + 20;   // [2] S buffer read by every softmax warp
-  uint64_t* p_full = bar + 22;   // P written by every softmax warp
-  uint64_t* p_free = bar + 23;   // PV has read P (PV thread's commit)
-  uint64_t* o_full = bar + 30;
-  uint64_t* o_free = bar + 31;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 32);
+  uint64_t* k_full = bar + 2;          // [NK]
+  uint64_t* k_empty = k_full + NK;     // [NK]
+  uint64_t* v_full = k_empty + NK;     // [NV]
+  uint64_t* v_empty = v_full + NV;     // [NV]
+  uint64_t* s_full = v_empty + NV;     // [2] S buffer written (MMA commit)
+  uint64_t* s_free = s_full + 2;       // [2] S buffer read by every softmax warp
+  uint64_t* p_full = s_free + 2;       // P written by every softmax warp
+  uint64_t* p_free = p_full + 1;       // PV has read P (PV thread's commit)
+  uint64_t* o_full = p_free + 1;
+  uint64_t* o_free = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 1);
+  static_assert(2 + 2 * NK + 2 * NV + 8 + 1 <= 64, "barriers exceed their 512-byte slot");
 
   const int warp = threadIdx.x / 32;
   const int nkb4q = p.Hq * 2, nkb4k = p.Hkv * 2;

@@ -13,6 +13,9 @@ kernels:
   (transformers 5.x signature): projections, RoPE, the KV-cache update,
   ``fp4_eager_attention``, o_proj.
 * ``install()`` / ``uninstall()`` swap it in and out like eval.py does.
+* Single- or dual-slice Q and P follow FP4_USE_DUAL_QUANT_Q and
+  FP4_USE_DUAL_QUANT_ATTN as the reference reads them (llama_patch.py:84,183:
+  unset means dual).
 
 Semantics that differ from the reference, by design:
 
@@ -20,9 +23,6 @@ Semantics that differ from the reference, by design:
   (llama_patch.py:167-210) and applies RoPE to the dequantized values, which
   leaves them off the FP4 grid; QK^T on FP4 tensor cores needs FP4
   operands, so the native path quantizes the rotated Q and K.
-* Single-slice Q and P.  The reference reads FP4_USE_DUAL_QUANT_Q and
-  FP4_USE_DUAL_QUANT_ATTN (default true, llama_patch.py:84,183); here an
-  unset variable means single, and "true" raises NotImplementedError.
 * The quantizer arithmetic is fp32 (the FP4Quantizer default) whatever the
   model dtype; the reference uses the weight dtype (llama_patch.py:126-134).
 * Prefill only: query and key lengths must match (a non-empty KV cache,

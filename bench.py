@@ -986,8 +986,9 @@ class WeightsWorkload:
         return {"bound": "hbm", "kernel": "quant_rows_vec_kernel on a [28672, 8192] weight (g given)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"{peak_src} copy bandwidth", "algorithmic_bytes_per_launch": algo,
-                "traffic": profile_traffic("quant_rows_vec_kernel_28672x8192_tensor"),
-                "traffic_source": "profiles/quant_rows_vec_kernel_28672x8192_tensor.md: ncu dram bytes per launch"}
+                "traffic": profile_traffic("quant_rows_vec_kernel_llama3-70b_weights"),
+                "traffic_source": "profiles/quant_rows_vec_kernel_llama3-70b_weights.md: ncu dram bytes of an "
+                                  "[8192, 8192] launch x 3.5"}
 
     def cpu_sample(self, reps=None):
         """The reference's CPU path (torch ops) on the k weight [1024, 8192] of layer 0, per-tensor scale."""

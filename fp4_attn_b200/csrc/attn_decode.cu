@@ -23,8 +23,9 @@
 //    each row's maximum into an order-free atomic maximum;
 //  * pv: the same ring over V and S; the exact row max, e = exp2((S - m)
 //    log2 e), the NVFP4 fake-quant of e per 16 keys (as the prefill kernel
-//    does), then O-partial = (P-hat * g_v) (code*scale)_v on CUDA cores with
-//    packed fp32x2 FMAs (V's per-token g_v is not exact in fp16);
+//    does), then O-partial^T = (code*scale)_v^T (P-hat * g_v)^T on mma.sync
+//    m16n8k16 (V-hat exact in fp16; P-hat * g_v as fp16 hi + lo, since V's
+//    per-token g_v is not exact in fp16), fp32 accumulate;
 //  * combine: O = sum O-partial / sum l over the chunks, in a fixed order.
 #include <stdint.h>
 
@@ -58,17 +59,20 @@ constexpr uint32_t PV_VC = DK_KEYS * DK_D / 2;
 constexpr uint32_t PV_VS = DK_KEYS * DK_D;
 constexpr uint32_t PV_VG = DK_KEYS * 4;
 constexpr uint32_t PV_S1 = DK_KEYS * 4;  // S of one head
-// MG bounds the query heads per KV head; AG heads are accumulated at a time.
-// Dynamic shared memory: the ring, then P-hat * g_v [MG][DK_KEYS], then the
-// cross-warp partial sums [4][AG][DK_D].
+// MG bounds the query heads per KV head (NT = MG/8 rounded up MMA n-tiles of
+// 8 heads).  Dynamic shared memory: the ring, then P-hat * g_v * 2^E as fp16
+// hi and lo rows [2*MG][PV_PH_LD] (keys in MMA k order), then each warp's
+// partial O [DK_WARPS][MG][PV_PART_LD] (dim 16g + c at position c*8 + g).
+constexpr int PV_PART_LD = 132;  // 4 mod 16 floats: the fragment stores hit 32 distinct banks
+constexpr int PV_PH_LD = DK_KEYS + 8;  // fp16 P-hat row: 132 words, so the 8 heads of a B load hit 32 banks
 template <int MG>
 struct PvCfg {
-  static constexpr int AG = MG < 8 ? MG : 8;
+  static constexpr int NT = (MG + 7) / 8;
   static constexpr int STAGES = MG <= 8 ? 3 : 2;
   static constexpr uint32_t STAGE = PV_VC + PV_VS + PV_VG + MG * PV_S1;
   static constexpr uint32_t RING = STAGES * STAGE;
-  static constexpr uint32_t PH = MG * DK_KEYS * 4;
-  static constexpr uint32_t PART = 4 * AG * DK_D * 4;
+  static constexpr uint32_t PH = 2 * MG * PV_PH_LD * 2;
+  static constexpr uint32_t PART = DK_WARPS * MG * PV_PART_LD * 4;
   static constexpr uint32_t SMEM = RING + PH + PART;
 };
 
@@ -112,17 +116,6 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
-__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
-// acc += {a, a} * {x, y}, one packed fp32x2 FMA (two IEEE fp32 FMAs)
-__device__ __forceinline__ void fma2(float& acc0, float& acc1, float a, float x, float y) {
-  unsigned long long A, X, C;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a), "f"(a));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(X) : "f"(x), "f"(y));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(C) : "f"(acc0), "f"(acc1));
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(C) : "l"(A), "l"(X));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(acc0), "=f"(acc1) : "l"(C));
 }
 // order-preserving float maximum on the bit pattern (exact, order-free)
 __device__ __forceinline__ void atomic_max_f32(unsigned int* a, float v) {
@@ -282,24 +275,55 @@ __global__ void __launch_bounds__(DK_THREADS) decode_scores_kernel(DecodeArgs p)
 }
 
 // -------------------------------------------------------------------- pv
-// Phase e: thread t handles key t of the item.  Accumulation: thread (oct,
-// slot) sums dims 8*oct..+7 over keys 16*slot..+15, for AG heads at a time.
+// Phase e: thread t handles key t of the item (e, the per-16-key NVFP4
+// fake-quant of e, P-hat * g_v), as the prefill kernel quantizes P.
+//
+// PV on mma.sync m16n8k16 (fp16 operands, fp32 accumulate), transposed:
+// O^T[dim][head] += V-hat^T[dim][key] * (P-hat g_v)^T[key][head].  Warp w owns
+// keys 32w..32w+31 of the item -- the keys its own phase-e threads produced,
+// so no CTA barrier sits between the phases -- as two k-steps of 16 keys.
+//  * A = V-hat = code * scale, exact in fp16 (E2M1 x E4M3 has at most five
+//    significant bits and lies in [2^-10, 2688]).  M index: m-tile mt, row g
+//    (g = lane/4) is dim 16g + 2mt, row g+8 dim 16g + 2mt + 1, so a lane's
+//    dims are one 8-byte run of codes and one 16-byte run of scales per key.
+//  * K index within a k-step: k = 8h + 2t + j (t = lane%4) is key 8h + 4j + t,
+//    so lane t's keys are t, t+4, t+8, t+12 and each load instruction reads
+//    four consecutive key rows (no bank conflicts).  The code nibbles of keys
+//    t and t+4 are merged into (key t, key t+4) bytes, which convert to the
+//    A register pairs directly.
+//  * B = P-hat * g_v as fp16 hi + lo (22 significant bits; g_v varies along
+//    the keys, so it cannot be factored out), scaled by a per-warp power of
+//    two 2^E that keeps the largest value below 2^15 (P-hat <= 1.03125 and
+//    g_v < 2^(e+1)); the partial O is scaled back by 2^-E, exactly.
+//  * N index: head 8nt + g (heads >= G are zero).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
 template <int MG>
 __global__ void __launch_bounds__(DK_THREADS) decode_pv_kernel(DecodeArgs p) {
   using C = PvCfg<MG>;
-  constexpr int AG = C::AG;
+  constexpr int NT = C::NT;
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES];
   __shared__ float lred[DK_WARPS][MG];
-  float(*ph)[DK_KEYS] = reinterpret_cast<float(*)[DK_KEYS]>(ring + C::RING);           // P-hat * g_v
-  float(*part)[AG][DK_D] = reinterpret_cast<float(*)[AG][DK_D]>(ring + C::RING + C::PH);  // partial sums
+  __shared__ float rcp_tab[128];  // correctly rounded 1/s of every non-negative E4M3 scale byte (0 -> 0)
+  __half(*ph)[PV_PH_LD] = reinterpret_cast<__half(*)[PV_PH_LD]>(ring + C::RING);  // hi rows [0,MG), lo rows [MG,2MG)
+  float(*part)[MG][PV_PART_LD] = reinterpret_cast<float(*)[MG][PV_PART_LD]>(ring + C::RING + C::PH);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, t = threadIdx.x;
+  const int g8 = lane >> 2, t4 = lane & 3;
   const int G = p.Hq / p.Hkv;
   int i0, i1;
   item_range(p.nsplit * p.B * p.Hkv, i0, i1);
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], DK_WARPS);
     fence_barrier_init();
+  }
+  if (threadIdx.x < 128) {
+    const float sv = e4m3_to_f32((uint8_t)threadIdx.x);
+    rcp_tab[threadIdx.x] = sv == 0.0f ? 0.0f : __frcp_rn(sv);
   }
   __syncthreads();
   if (warp == DK_WARPS) {
@@ -319,7 +343,9 @@ __global__ void __launch_bounds__(DK_THREADS) decode_pv_kernel(DecodeArgs p) {
     return;
   }
   const float log2e = 1.4426950408889634f, r6 = __frcp_rn(6.0f);
-  const int oct = t % 16, slot = t / 16;
+  // this thread's key t sits at MMA k position kpos within its 16-key step
+  const int kr = t & 15;
+  const int kpos = (t & ~15) + (kr & 8) + 2 * (kr & 3) + ((kr >> 2) & 1);
   int cur = -1;
   float m[MG];
 #pragma unroll
@@ -339,18 +365,24 @@ __global__ void __launch_bounds__(DK_THREADS) decode_pv_kernel(DecodeArgs p) {
     const bool landed = mbar_wait(&full[s], (it / C::STAGES) & 1, 0x412);
     uint8_t* st = ring + (size_t)s * C::STAGE;
     const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
-    if (nlive < DK_KEYS) {
-      // keys past len: whatever the cache holds there becomes V = 0 (P-hat is 0 there too)
-      uint4* vc = reinterpret_cast<uint4*>(st);
-      uint4* vs = reinterpret_cast<uint4*>(st + PV_VC);
-      for (int i = nlive * (DK_D / 2 / 16) + t; i < DK_KEYS * (DK_D / 2 / 16); i += DK_WARPS * 32)
-        vc[i] = make_uint4(0u, 0u, 0u, 0u);
-      for (int i = nlive * (DK_D / 16) + t; i < DK_KEYS * (DK_D / 16); i += DK_WARPS * 32)
-        vs[i] = make_uint4(0u, 0u, 0u, 0u);
+    const bool live = t < nlive;
+    if (!live) {
+      // key t is past len: whatever the cache holds there becomes V = 0 (P-hat is 0 there too)
+      uint4* vc = reinterpret_cast<uint4*>(st + t * (DK_D / 2));
+      uint4* vs = reinterpret_cast<uint4*>(st + PV_VC + t * DK_D);
+#pragma unroll
+      for (int i = 0; i < DK_D / 2 / 16; ++i) vc[i] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int i = 0; i < DK_D / 16; ++i) vs[i] = make_uint4(0u, 0u, 0u, 0u);
     }
+    const float gv = live ? reinterpret_cast<const float*>(st + PV_VC + PV_VS)[t] : 0.0f;
+    float gmax = gv;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
+    int E = 0;
+    if (gmax > 0.0f) E = max(-100, min(100, 13 - (((__float_as_int(gmax) >> 23) & 0xFF) - 127)));
+    const float up = __int_as_float((E + 127) << 23), down = __int_as_float((127 - E) << 23);
     {
-      const bool live = t < nlive;
-      const float gv = live ? reinterpret_cast<const float*>(st + PV_VC + PV_VS)[t] : 0.0f;
       const float* Ss = reinterpret_cast<const float*>(st + PV_VC + PV_VS + PV_VG);
 #pragma unroll
       for (int g = 0; g < MG; ++g) {
@@ -359,110 +391,162 @@ __global__ void __launch_bounds__(DK_THREADS) decode_pv_kernel(DecodeArgs p) {
         float am = e;  // block of 16 keys = 16 consecutive lanes
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-        const uint8_t sb = e4m3_satfinite(__fmul_rn(am, r6));
+        const uint8_t sb = e4m3_satfinite(__fmul_rn(am, r6));  // e >= 0: sb < 0x80
         const float sf = e4m3_to_f32(sb);
-        const float rs = sf == 0.0f ? 0.0f : __frcp_rn(sf);
+        const float rs = rcp_tab[sb & 0x7F];
         const uint32_t byte = e2m1x2(__fmaf_rn(e, rs, 0.0f), 0.0f);
-        ph[g][t] = live ? __fmul_rn(__fmul_rn(e2m1_value(byte & 15u), sf), gv) : 0.0f;
+        const float code = __half2float(__ushort_as_half((unsigned short)(cvt_e2m1x2_f16x2(byte) & 0xFFFFu)));
+        const float x = live ? __fmul_rn(__fmul_rn(__fmul_rn(code, sf), gv), up) : 0.0f;
+        const __half hi = __float2half_rn(x);
+        ph[g][kpos] = hi;
+        ph[MG + g][kpos] = __float2half_rn(x - __half2float(hi));
         float l = e;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         if (lane == 0) lred[warp][g] = l;
       }
     }
-    if (!consumers_all(landed)) break;  // ph, lred and the zeroed V are visible
+    __syncwarp();
+    float acc[NT][8][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][mt][i] = 0.0f;
+#pragma unroll
+    for (int kstep = 0; kstep < 2; ++kstep) {
+      const int kb = 32 * warp + 16 * kstep;
+      uint2 cw[4];
+      uint4 sw[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int key = kb + t4 + 4 * i;
+        cw[i] = *reinterpret_cast<const uint2*>(st + key * (DK_D / 2) + 8 * g8);
+        sw[i] = *reinterpret_cast<const uint4*>(st + PV_VC + key * DK_D + 16 * g8);
+      }
+      uint32_t bhi[NT][2], blo[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int h = 8 * nt + g8;
+        const bool on = h < G;
+        bhi[nt][0] = on ? *reinterpret_cast<const uint32_t*>(&ph[h][kb + 2 * t4]) : 0u;
+        bhi[nt][1] = on ? *reinterpret_cast<const uint32_t*>(&ph[h][kb + 2 * t4 + 8]) : 0u;
+        blo[nt][0] = on ? *reinterpret_cast<const uint32_t*>(&ph[MG + h][kb + 2 * t4]) : 0u;
+        blo[nt][1] = on ? *reinterpret_cast<const uint32_t*>(&ph[MG + h][kb + 2 * t4 + 8]) : 0u;
+      }
+      // code bytes of key pairs (t, t+4) and (t+8, t+12): even dims in E, odd dims in O,
+      // the first key of the pair in the low nibble
+      uint32_t ev[2][2], od[2][2];
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr)
+#pragma unroll
+        for (int wd = 0; wd < 2; ++wd) {
+          const uint32_t x = wd ? cw[2 * pr].y : cw[2 * pr].x, y = wd ? cw[2 * pr + 1].y : cw[2 * pr + 1].x;
+          ev[pr][wd] = (x & 0x0F0F0F0Fu) | ((y << 4) & 0xF0F0F0F0u);
+          od[pr][wd] = ((x >> 4) & 0x0F0F0F0Fu) | (y & 0xF0F0F0F0u);
+        }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int wd = mt >> 2, sh = 8 * (mt & 3);
+        const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
+        uint32_t a[4];
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const uint32_t sx = (mt >> 1) == 0 ? sw[2 * pr].x : (mt >> 1) == 1 ? sw[2 * pr].y
+                            : (mt >> 1) == 2 ? sw[2 * pr].z : sw[2 * pr].w;
+          const uint32_t sy = (mt >> 1) == 0 ? sw[2 * pr + 1].x : (mt >> 1) == 1 ? sw[2 * pr + 1].y
+                            : (mt >> 1) == 2 ? sw[2 * pr + 1].z : sw[2 * pr + 1].w;
+          const uint32_t sc = prmt(sx, sy, sel);  // {s_x, s_y} of dim 2mt (low half), of dim 2mt+1 (high half)
+          a[2 * pr] = hmul2u(cvt_e2m1x2_f16x2((ev[pr][wd] >> sh) & 0xFFu), cvt_e4m3x2_f16x2(sc & 0xFFFFu));
+          a[2 * pr + 1] = hmul2u(cvt_e2m1x2_f16x2((od[pr][wd] >> sh) & 0xFFu), cvt_e4m3x2_f16x2(sc >> 16));
+        }
+        // fragment order: a0 rows g / k 0-7, a1 rows g+8 / k 0-7, a2 rows g / k 8-15, a3 rows g+8 / k 8-15
+        const uint32_t fr[4] = {a[0], a[1], a[2], a[3]};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma16816(acc[nt][mt], fr, bhi[nt][0], bhi[nt][1]);
+          mma16816(acc[nt][mt], fr, blo[nt][0], blo[nt][1]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp's V rows and scores are no longer read
+    // acc[nt][mt]: (dim 16g+2mt, head 8nt+2t), (dim, head+1), (dim+1, head), (dim+1, head+1)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int h = 8 * nt + 2 * t4, c = 2 * mt;
+        if (h < G) {
+          part[warp][h][c * 8 + g8] = acc[nt][mt][0] * down;
+          part[warp][h][(c + 1) * 8 + g8] = acc[nt][mt][2] * down;
+        }
+        if (h + 1 < G) {
+          part[warp][h + 1][c * 8 + g8] = acc[nt][mt][1] * down;
+          part[warp][h + 1][(c + 1) * 8 + g8] = acc[nt][mt][3] * down;
+        }
+      }
+    if (!consumers_all(landed)) break;  // part and lred are complete
     if (t < G) {
       float l = 0.0f;
       for (int w = 0; w < DK_WARPS; ++w) l += lred[w][t];
       p.lpart[(bh0 + t) * p.nsplit + split] = l;
     }
-    for (int g0 = 0; g0 < G; g0 += AG) {
-      float acc[AG][8];
-#pragma unroll
-      for (int g = 0; g < AG; ++g)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[g][i] = 0.0f;
-#pragma unroll
-      for (int u4 = 0; u4 < 4; ++u4) {
-        float v[4][8];  // code * scale of 4 keys, 8 dims each
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int key = slot * 16 + u4 * 4 + u;
-          const uint32_t cw = *reinterpret_cast<const uint32_t*>(st + key * (DK_D / 2) + 4 * oct);
-          const uint2 sw = *reinterpret_cast<const uint2*>(st + PV_VC + key * DK_D + 8 * oct);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t sc = ((i < 2 ? sw.x : sw.y) >> (16 * (i & 1))) & 0xFFFFu;
-            const uint32_t w = hmul2u(cvt_e2m1x2_f16x2((cw >> (8 * i)) & 0xFFu), cvt_e4m3x2_f16x2(sc));
-            v[u][2 * i] = half_lo(w);
-            v[u][2 * i + 1] = half_hi(w);
-          }
-        }
-#pragma unroll
-        for (int g = 0; g < AG; ++g)
-          if (g0 + g < G) {
-            const float4 pg = *reinterpret_cast<const float4*>(&ph[g0 + g][slot * 16 + u4 * 4]);
-            const float pa[4] = {pg.x, pg.y, pg.z, pg.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                fma2(acc[g][2 * i], acc[g][2 * i + 1], pa[u], v[u][2 * i], v[u][2 * i + 1]);
-          }
-      }
-      if (g0 + AG >= G) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // the stage is no longer read
-      }
-      // slots 2w and 2w+1 share a warp: fold lane l + 16 into lane l
-#pragma unroll
-      for (int g = 0; g < AG; ++g)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[g][i] += __shfl_xor_sync(0xffffffffu, acc[g][i], 16);
-      if (warp >= 4 && lane < 16) {
-#pragma unroll
-        for (int g = 0; g < AG; ++g)
-          if (g0 + g < G)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) part[warp - 4][g][8 * oct + i] = acc[g][i];
-      }
-      consumers_sync();
-      if (warp < 4 && lane < 16) {
-#pragma unroll
-        for (int g = 0; g < AG; ++g)
-          if (g0 + g < G)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) part[warp][g][8 * oct + i] += acc[g][i];
-      }
-      consumers_sync();
-      // ((w0 + w4) + (w2 + w6)) + ((w1 + w5) + (w3 + w7)), in a fixed order
-      const int ng = min(AG, G - g0);
-      for (int i = t; i < ng * DK_D; i += DK_WARPS * 32) {
-        const int g = i / DK_D, dd = i % DK_D;
-        p.opart[((bh0 + g0 + g) * p.nsplit + split) * DK_D + dd] =
-            (part[0][g][dd] + part[2][g][dd]) + (part[1][g][dd] + part[3][g][dd]);
-      }
-      if (g0 + AG < G) consumers_sync();  // part is rewritten by the next head group
+    for (int i = t; i < G * DK_D; i += DK_WARPS * 32) {
+      // consecutive threads read consecutive positions (no bank conflicts); pos c*8 + g holds dim 16g + c
+      const int g = i / DK_D, pos = i % DK_D, d = 16 * (pos & 7) + (pos >> 3);
+      // ((w0 + w1) + (w2 + w3)) + ((w4 + w5) + (w6 + w7)), in a fixed order
+      const float o = ((part[0][g][pos] + part[1][g][pos]) + (part[2][g][pos] + part[3][g][pos])) +
+                      ((part[4][g][pos] + part[5][g][pos]) + (part[6][g][pos] + part[7][g][pos]));
+      p.opart[((bh0 + g) * p.nsplit + split) * DK_D + d] = o;
     }
+    consumers_sync();  // part and lred are rewritten by the next item
   }
 }
 
-// O = sum over chunks of O-partial / sum of l, four interleaved partial sums in a fixed order.
-__global__ void __launch_bounds__(DK_D) decode_combine_kernel(DecodeArgs p) {
-  const int bh = blockIdx.x, d = threadIdx.x;
-  const float* op = p.opart + (int64_t)bh * p.nsplit * DK_D + d;
+// O = sum over chunks of O-partial / sum of l.  One CTA per (b, query head):
+// group r of 32 threads sums chunks r, r + 8, r + 16, ... (4 dims per thread,
+// 16-byte loads, every load of the group issued before the adds), then the
+// eight group sums are added in a fixed order.
+constexpr int CB_GROUPS = 8;
+__global__ void __launch_bounds__(CB_GROUPS * 32) decode_combine_kernel(DecodeArgs p) {
+  __shared__ float4 osum[CB_GROUPS][DK_D / 4];
+  __shared__ float lsum[CB_GROUPS];
+  const int bh = blockIdx.x, r = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const float4* op = reinterpret_cast<const float4*>(p.opart + (int64_t)bh * p.nsplit * DK_D) + lane;
   const float* lp = p.lpart + (int64_t)bh * p.nsplit;
-  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f}, l[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  int s = 0;
-  for (; s + 8 <= p.nsplit; s += 8) {
-    float ov[8], lv[8];
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float l = 0.0f;
+  int s = r;
+  for (; s + 3 * CB_GROUPS < p.nsplit; s += 4 * CB_GROUPS) {
+    float4 v[4];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) ov[u] = op[(int64_t)(s + u) * DK_D], lv[u] = lp[s + u];
+    for (int u = 0; u < 4; ++u) v[u] = op[(int64_t)(s + u * CB_GROUPS) * (DK_D / 4)];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) o[u & 3] += ov[u], l[u & 3] += lv[u];
+    for (int u = 0; u < 4; ++u) {
+      o.x += v[u].x, o.y += v[u].y, o.z += v[u].z, o.w += v[u].w;
+      if (lane == 0) l += lp[s + u * CB_GROUPS];
+    }
   }
-  for (; s < p.nsplit; ++s) o[0] += op[(int64_t)s * DK_D], l[0] += lp[s];
-  p.out[(int64_t)bh * DK_D + d] = ((o[0] + o[1]) + (o[2] + o[3])) / ((l[0] + l[1]) + (l[2] + l[3]));
+  for (; s < p.nsplit; s += CB_GROUPS) {
+    const float4 v = op[(int64_t)s * (DK_D / 4)];
+    o.x += v.x, o.y += v.y, o.z += v.z, o.w += v.w;
+    if (lane == 0) l += lp[s];
+  }
+  osum[r][lane] = o;
+  if (lane == 0) lsum[r] = l;
+  __syncthreads();
+  if (threadIdx.x < DK_D) {
+    const int d = threadIdx.x;
+    const float* os = reinterpret_cast<const float*>(osum);
+    float v[CB_GROUPS];
+#pragma unroll
+    for (int g = 0; g < CB_GROUPS; ++g) v[g] = os[g * DK_D + d];
+    const float on = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    const float ln = ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3])) + ((lsum[4] + lsum[5]) + (lsum[6] + lsum[7]));
+    p.out[(int64_t)bh * DK_D + d] = on / ln;
+  }
 }
 
 // Persistent grid: as many CTAs as are resident at once, at most one per item.
@@ -546,6 +630,6 @@ extern "C" int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, c
   const int G = Hq / Hkv;
   const int e = G <= 4 ? launch_pv<4>(a, items, st) : G <= 8 ? launch_pv<8>(a, items, st) : launch_pv<16>(a, items, st);
   if (e) return e;
-  decode_combine_kernel<<<(unsigned)bh, DK_D, 0, st>>>(a);
+  decode_combine_kernel<<<(unsigned)bh, CB_GROUPS * 32, 0, st>>>(a);
   return check_launch("decode_combine_kernel");
 }

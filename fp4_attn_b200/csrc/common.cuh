@@ -47,6 +47,14 @@ __device__ __forceinline__ float recip(float v) {
   return v == 0.0f ? 0.0f : rnd<A>(__frcp_rn(v));
 }
 
+// recip<A>(6.0f) as a compile-time constant: 1.0f / 6.0f is folded with IEEE
+// round-to-nearest, the rounding rcp.rn gives, so no reciprocal runs per block.
+template <int A>
+__device__ __forceinline__ float recip6() {
+  constexpr float kSixth = 1.0f / 6.0f;
+  return rnd<A>(kSixth);
+}
+
 // NaN-propagating maximum (torch.max semantics).
 __device__ __forceinline__ float nanmax(float a, float b) {
   float r;

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(QF_THREADS, 1) quant_tensor_fused_kernel(QFArg
   if (!s_ok) return;
   // ---- quantize from shared memory: lanes 2i and 2i+1 hold the two halves of a block;
   // each thread takes two halves per step (independent chains the scheduler interleaves)
-  const float rg = s_rg, r6 = recip<A>(6.0f);
+  const float rg = s_rg, r6 = recip6<A>();
   const int64_t b0 = e0 / 16;  // first block of the slice
   const int nhalf = (int)(cnt / 8);
   const float2 rg2 = make_float2(rg, rg), zero2 = make_float2(0.0f, 0.0f);

@@ -164,7 +164,7 @@ __device__ __forceinline__ uint32_t e2m1x8(const float* v) {
 template <int A, int ODT, bool COLG, bool OUT>
 __device__ __forceinline__ void quant_block(float v[16], const QuantArgs& p, int64_t orow, int kb, float g, float rg,
                                             const float* rcp_tab, uint32_t* wout = nullptr, float* sout = nullptr) {
-  const float r6 = recip<A>(6.0f);
+  const float r6 = recip6<A>();
   if constexpr (COLG) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = mul<A>(v[j], recip<A>(p.g_in[kb * 16 + j]));
@@ -492,6 +492,9 @@ __global__ void __launch_bounds__(kVecThreads, 3) quant_rows_vec_kernel(QuantArg
       t = (int)((uint32_t)orow - (uint32_t)b * tpad);
     }
   };
+  // tensor mode: the one global scale and its reciprocal, read and computed once
+  const float g_tensor = p.gmode == 3 ? p.g_in[0] : 1.0f;
+  const float rg_tensor = p.gmode == 3 ? recip<A>(g_tensor) : 1.0f;
   RawBlock<DT> cur[2], nxt[2];
   uint32_t whi[2][2] = {{0u, 0u}, {0u, 0u}};  // DUAL: first-slice codes and scales of this thread's blocks
   float shi[2] = {0.0f, 0.0f};
@@ -546,7 +549,7 @@ __global__ void __launch_bounds__(kVecThreads, 3) quant_rows_vec_kernel(QuantArg
       g = m;  // rowmax, no division by global_sf_max (fp4_quant_utils.py:134,139)
       if (p.g_row && lane == 0 && live) p.g_row[orow] = pad_row ? 0.0f : g;
     } else if (p.gmode == 3) {
-      g = p.g_in[0];
+      g = g_tensor;
     }
     if (live) {
       if (pad_row) {
@@ -556,7 +559,7 @@ __global__ void __launch_bounds__(kVecThreads, 3) quant_rows_vec_kernel(QuantArg
             p.scales[p.scale_layout ? sf_tcgen05_offset(orow, kb, p.scales_ld) : orow * p.scales_ld + kb] = 0;
         }
       } else {
-        const float rg = p.gmode == 0 ? 1.0f : recip<A>(g);
+        const float rg = p.gmode == 0 ? 1.0f : p.gmode == 3 ? rg_tensor : recip<A>(g);
 #pragma unroll
         for (int i = 0; i < 2; ++i)
           if (i < nmine) {

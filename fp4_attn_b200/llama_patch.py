@@ -31,6 +31,7 @@ Semantics that differ from the reference, by design:
 from __future__ import annotations
 
 import os
+import weakref
 
 import torch
 
@@ -45,8 +46,17 @@ def dual_enabled(name: str) -> bool:
     return os.getenv(name, "true").lower() == "true"
 
 
+# The last mask found to be plain causal: (weak reference to the tensor, its version counter, T, S).
+# A model passes one mask object to every layer, so it is checked once per forward.
+_CHECKED = (None, -1, 0, 0)
+
+
 def _check_mask(mask: torch.Tensor | None, T: int, S: int) -> None:
+    global _CHECKED
     if mask is None:
+        return
+    ref, version, t0, s0 = _CHECKED
+    if ref is not None and ref() is mask and mask._version == version and (t0, s0) == (T, S):
         return
     if mask.dim() != 4 or mask.shape[-2] != T or mask.shape[-1] < S:
         raise ValueError(f"attention mask of shape {tuple(mask.shape)} does not match T={T}, S={S}")
@@ -58,6 +68,7 @@ def _check_mask(mask: torch.Tensor | None, T: int, S: int) -> None:
     causal = torch.ones(T, S, dtype=torch.bool, device=m.device).tril()
     if not bool((allowed == causal).all()):
         raise NotImplementedError("the FP4 attention kernel supports a plain causal mask (no padding)")
+    _CHECKED = (weakref.ref(mask), mask._version, T, S)
 
 
 def fp4_eager_attention(module, query, key, value, attention_mask, scaling, dropout=0.0, **kwargs):
@@ -102,7 +113,8 @@ def llama_fp4_attention_forward(self, hidden_states, position_embeddings=None, a
     q, k = apply_rotary_pos_emb(q, k, cos, sin)
     if past_key_values is not None:
         k, v = past_key_values.update(k, v, self.layer_idx)
-    if torch.isnan(q).any() or torch.isnan(k).any() or torch.isnan(v).any():  # llama_patch.py:228-232
+    # llama_patch.py:228-232 (one host read for the three tensors)
+    if bool(torch.isnan(q).any() | torch.isnan(k).any() | torch.isnan(v).any()):
         raise FloatingPointError("NaN in the attention inputs")
     out, weights = attention_interface(self, q, k, v, attention_mask, scaling=self.scaling,
                                        dropout=0.0 if not self.training else self.attention_dropout)

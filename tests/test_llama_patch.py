@@ -92,6 +92,13 @@ def test_mask_check():
         lp._check_mask(padded, T, T)
     with pytest.raises(ValueError):
         lp._check_mask(causal[..., :4, :], T, T)
+    # a mask already found causal is not re-read, unless it was changed in place since
+    m = causal.clone()
+    lp._check_mask(m, T, T)
+    lp._check_mask(m, T, T)
+    m[..., :, 0] = torch.finfo(torch.float32).min
+    with pytest.raises(NotImplementedError):
+        lp._check_mask(m, T, T)
 
 
 def test_nvfp4sim_new_exports_refuse_unimplemented_modes():

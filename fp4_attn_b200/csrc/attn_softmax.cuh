@@ -85,9 +85,14 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&a)[32], const float*
 #pragma unroll
     for (int i = 0; i < 32; ++i) z[i] = (col0 + i > lim) ? -INFINITY : z[i];
   }
+  // a tree (depth 4) instead of a chain of 16 dependent maxima
+  float t[11];
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) m = max3f(m, z[i], z[i + 1]);
-  return m;
+  for (int i = 0; i < 10; ++i) t[i] = max3f(z[3 * i], z[3 * i + 1], z[3 * i + 2]);
+  t[10] = fmaxf(z[30], z[31]);
+  const float b0 = max3f(t[0], t[1], t[2]), b1 = max3f(t[3], t[4], t[5]), b2 = max3f(t[6], t[7], t[8]);
+  const float b3 = max3f(t[9], t[10], m);
+  return fmaxf(max3f(b0, b1, b2), b3);
 }
 
 // exp2 of four scores: e = exp2(acc * gk * u - m * u).

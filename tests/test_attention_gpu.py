@@ -60,7 +60,7 @@ def test_prepare_v_bit_exact():
 
 @pytest.mark.parametrize("B,Hq,Hkv,T,causal", [
     (1, 2, 1, 256, True), (2, 4, 2, 200, True), (1, 2, 2, 384, False), (1, 8, 2, 512, True),
-    (1, 4, 4, 130, False), (3, 2, 1, 64, True)])
+    (1, 4, 4, 130, False), (3, 2, 1, 64, True), (1, 2, 1, 1, True), (2, 4, 1, 17, False)])
 def test_attention_small(B, Hq, Hkv, T, causal):
     g = torch.Generator().manual_seed(B * 1000 + Hq * 100 + T)
     q = torch.randn(B, Hq, T, 128, generator=g).bfloat16()

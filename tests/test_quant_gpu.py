@@ -254,3 +254,16 @@ def test_nvfp4sim_packed_exports(dev):
         np.testing.assert_array_equal(canon(y.cpu().numpy()), canon(ref_out), err_msg=name)
         d = nvfp4sim.dequantize_nvfp4(codes, scales, g, xt.shape, "row")
         np.testing.assert_array_equal(canon(d.cpu().numpy()), canon(ref_out), err_msg=name)
+
+
+@pytest.mark.parametrize("mode", ["row", "tensor", "none"])
+def test_empty_rows(dev, mode):
+    """Zero rows quantize to empty outputs without a launch error (in row mode the reference's
+    single_nvfp4_quant_dequant_fused returns an empty tensor too)."""
+    from fp4_attn_b200 import quant
+    x = torch.zeros(0, 64, dtype=torch.bfloat16, device=dev)
+    pk = quant.quantize(x, mode, 2688.0 if mode == "tensor" else 1536.0)
+    torch.cuda.synchronize()
+    assert pk.codes.shape == (0, 32) and pk.scales.numel() == 0
+    out = quant.qdq(x, mode, 2688.0 if mode == "tensor" else 1536.0, torch.float32)
+    assert out.shape == (0, 64)

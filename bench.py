@@ -2,7 +2,7 @@
 """Benchmark of the NVFP4 hot path on B200s; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload attention|quantize|decode|qkv|prefill|weights|llama]
+                    [--workload attention|quantize|decode|qkv|prefill|weights|llama|gemm]
                     [--impl ours|reference]
 
 For N > 1 launch one rank per GPU with torch.distributed.run; ranks shard the
@@ -40,6 +40,9 @@ configurations; no dataset is read):
 * llama -- one forward of a Llama-2-7B-shaped model (random bf16 weights
   N(0,0.02), seed 3) with the FP4 attention patch installed, batch 8 x 2048
   token ids; strong scaling over the batch.  Metric: tokens/s.
+* gemm -- an FP4 linear layer: 8192 tokens of bf16 activations quantized
+  per token and multiplied by layer 0's per-tensor NVFP4 gate weight of the
+  70B stack (8192 -> 28672) on tcgen05.  Metric: TFLOP/s, 2*M*N*K.
 
 decode and qkv measure the rows that extend the path (the NVFP4 KV cache,
 the fused projection); prefill and weights the long-context and weight
@@ -77,7 +80,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["attention", "quantize", "decode", "qkv", "prefill", "weights",
-                                                     "llama"],
+                                                     "llama", "gemm"],
                     default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=10,
@@ -1008,6 +1011,111 @@ class WeightsWorkload:
         return w.numel() * (2 + 0.5 + 1 / 16) * n / el / 1e9, f"k weight [1024, 8192] of layer 0 x{n} (torch ops)"
 
 
+class GemmWorkload:
+    """An FP4 linear layer: the activations quantized to NVFP4 (row mode) and multiplied by a
+    per-tensor NVFP4 weight on tcgen05, Y = X W^T in fp32.  The weight is layer 0's gate
+    projection of the Llama-3-70B-shaped stack (quantized once, as weights are)."""
+    name = "gemm"
+    metric = "NVFP4 GEMM TFLOP/s per B200 (Llama-3-70B gate projection), % of dense FP4 tensor peak"
+    unit = "TFLOP/s"
+    dtype = "nvfp4 x nvfp4 (tcgen05 kind::mxf4nvf4), fp32 accumulate and output"
+    M, N, K = 8192, 28672, 8192
+    use_graph = True
+
+    def __init__(self, dev, cpu_only=False, rank=0, world=1):
+        self.flops = 2 * self.M * self.N * self.K
+        self.config = {"workload": "NVFP4 GEMM Y[8192, 28672] = X[8192, 8192] W^T: X bf16 N(0,1) quantized per "
+                                   "token (row mode), W the gate weight of layer 0 (bf16 N(0,0.02), seed 4 + 4, "
+                                   "per-tensor scale amax/2688), fp32 output",
+                       "flops_per_step": self.flops, "global_batch": world,
+                       "shard": "8192 tokens per rank (seed 40 + r), the weight on every rank"}
+        if cpu_only:
+            return
+        from fp4_attn_b200 import _lib, quant
+        self.lib, self.quant, self.dev = _lib, quant, dev
+        gen = torch.Generator(dev).manual_seed(4 + 4)
+        w = (torch.randn(self.N, self.K, device=dev, generator=gen) * 0.02).bfloat16()
+        self.wq = quant.quantize(w, "tensor", 2688.0, scale_layout="tcgen05")
+        self.gw = self.wq.g.expand(self.N).contiguous()
+        del w
+        gx = torch.Generator(dev).manual_seed(40 + rank)
+        self.nsets = 2
+        self.xs = [torch.randn(self.M, self.K, device=dev, generator=gx).bfloat16() for _ in range(self.nsets)]
+        self.xq = [quant.quantize(x, "row", 1536.0, scale_layout="tcgen05") for x in self.xs]
+        self.c = [torch.empty(self.M, self.N, device=dev) for _ in range(self.nsets)]
+        self.x_host = self.xs[0].cpu().pin_memory()
+        self.c_host = torch.empty(self.M, self.N).pin_memory()
+        self.stream = torch.cuda.current_stream(dev).cuda_stream
+        self.config["l2"] = f"weight codes 117 MB + {self.nsets} activation sets of 134 MB (> L2)"
+
+    def _gemm(self, i):
+        xq, wq = self.xq[i], self.wq
+        self.lib.call("fp4_gemm_nvf4", xq.codes.data_ptr(), xq.scales.data_ptr(), xq.g.data_ptr(),
+                      wq.codes.data_ptr(), wq.scales.data_ptr(), self.gw.data_ptr(), self.c[i].data_ptr(),
+                      self.M, self.N, self.K, xq.codes.stride(0), wq.codes.stride(0), self.c[i].stride(0),
+                      self.stream)
+
+    def step(self, i, ev=None):
+        """Quantize the activations (row mode, tcgen05 scale atoms) into their buffers, then the GEMM."""
+        i %= self.nsets
+        x, xq = self.xs[i], self.xq[i]
+        self.lib.call("fp4q_quantize", x.data_ptr(), 1, 1, self.M, 1, self.K, 0, self.K, 0, self.M, 1, 0, 1536.0,
+                      xq.codes.data_ptr(), self.K // 2, xq.scales.data_ptr(), 1, (self.K // 16 + 3) // 4,
+                      xq.g.data_ptr(), None, 0, 0, self.stream)
+        self._gemm(i)
+
+    def kernel(self, i):
+        self._gemm(i % self.nsets)
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D the bf16 activations, quant.quantize + gemm_nvf4, D2H Y."""
+        from fp4_attn_b200.gemm import gemm_nvf4
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(self.nsets)
+        i %= self.nsets
+        self.pipe.step(i, lambda: self.xs[i].copy_(self.x_host, non_blocking=True),
+                       lambda: gemm_nvf4(self.quant.quantize(self.xs[i], "row", 1536.0, scale_layout="tcgen05"),
+                                         self.wq),
+                       lambda y: self.c_host.copy_(y, non_blocking=True))
+
+    e2e_h2d = property(lambda self: self.M * self.K * 2)
+    e2e_d2h = property(lambda self: self.M * self.N * 4)
+
+    def value(self, seconds_per_step, world):
+        return world * self.flops / seconds_per_step / 1e12
+
+    def kernel_roofline(self, kernel_s, peaks, peak_src):
+        achieved = self.flops / kernel_s / 1e12
+        peak = 4 * peaks["bf16_tflops"]
+        return {"bound": "tensor", "kernel": "gemm_nvf4_kernel", "achieved": round(achieved, 1), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
+                "frac_of_nominal_fp4": round(achieved / 9000.0, 4), "algorithmic_flops_per_launch": self.flops,
+                "traffic": None, "traffic_source": "not captured at this shape"}
+
+    def cpu_sample(self, reps=None):
+        """The reference's way on the host cores: fake-quantized activations (torch ops) times the
+        dequantized weight in an fp32 matmul, for 256 of the 8192 tokens."""
+        from oracle import torch_port as tp
+        if getattr(self, "_wd", None) is None:  # the weight's fake-quant is offline: once, not timed
+            g = torch.Generator().manual_seed(4 + 4)
+            w = (torch.randn(self.N, self.K, generator=g) * 0.02).bfloat16().float()
+            one = torch.tensor(1.0)
+            gw = w.abs().max() * (one / torch.tensor(2688.0))
+            self._wd = tp.fused_qdq(w * (one / gw), aligned=True, global_sf_max=None) * gw
+        wd = self._wd
+        x = torch.randn(256, self.K, generator=torch.Generator().manual_seed(40)).bfloat16()
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            torch.matmul(tp.fused_qdq(x.float()), wd.T)
+            n += 1
+            el = time.perf_counter() - t0
+            if (reps and n >= reps) or (not reps and (el > 10.0 or n >= 20)):
+                break
+        return 2 * 256 * self.N * self.K * n / el / 1e12, f"256 of 8192 tokens x{n} (torch fp32 matmul)"
+
+
 def llama2_7b_config():
     from transformers import LlamaConfig
     return LlamaConfig(hidden_size=4096, intermediate_size=11008, num_hidden_layers=32, num_attention_heads=32,
@@ -1178,6 +1286,8 @@ def make_workload(name, dev, cpu_only=False, rank=0, world=1, layers=10):
         return WeightsWorkload(dev, cpu_only=cpu_only, rank=rank, world=world, layers=layers)
     if name == "llama":
         return LlamaWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
+    if name == "gemm":
+        return GemmWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
     return AttentionWorkload(dev, cpu_only=cpu_only, rank=rank, world=world)
 
 

@@ -9,7 +9,7 @@
 // its own for NVFP4 linear layers.
 //
 // One CTA per 128x128 output tile.  Warp 0 issues TMA (codes, 128B swizzle)
-// and bulk copies (scale atoms) into a 4-stage ring; warp 1 copies the scale
+// and bulk copies (scale atoms) into a 3-stage ring; warp 1 copies the scale
 // atoms into TMEM (tcgen05.cp) and issues tcgen05.mma kind::mxf4nvf4
 // (K = 64 per instruction, 4 per 256-wide stage) into a 128-column fp32 TMEM
 // accumulator; warps 2-5 drain TMEM, apply the global scales and store.
@@ -24,7 +24,7 @@ namespace fp4 {
 
 namespace gemm {
 constexpr int BM = 128, BN = 128, BK = 256;  // BK in elements (128 bytes of codes per row)
-constexpr int STAGES = 4;
+constexpr int STAGES = 3;  // 109 KB of ring: two CTAs per SM, so one's epilogue overlaps the other's main loop
 constexpr int A_BYTES = BM * BK / 2, B_BYTES = BN * BK / 2;
 constexpr int SF_BYTES = 4 * 512;  // 4 atoms of 128 rows x 4 scales
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * SF_BYTES;
@@ -44,7 +44,7 @@ struct GemmArgs {
   int nkb4;  // K / 64
 };
 
-__global__ void __launch_bounds__(gemm::THREADS, 1)
+__global__ void __launch_bounds__(gemm::THREADS, 2)
     gemm_nvf4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
   using namespace gemm;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     if (ok) {
       const int m = m0 + row;
       const float ga = (p.ga && m < p.M) ? p.ga[m] : 1.0f;
+      const bool vec_out = p.ldc % 4 == 0 && (uintptr_t)p.c % 16 == 0 && (uintptr_t)p.gb % 16 == 0;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -132,12 +133,27 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         tmem_ld_wait();
         if (m < p.M) {
           float* dst = p.c + (int64_t)m * p.ldc + n0 + c;
+          if (vec_out && n0 + c + 32 <= p.N) {
+            // 16-byte stores of the row's 32 columns (same products, same order)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + c + j;
-            if (n < p.N) {
-              const float gb = p.gb ? p.gb[n] : 1.0f;
-              dst[j] = __uint_as_float(r[j]) * ga * gb;
+            for (int j = 0; j < 32; j += 4) {
+              const float4 gb = p.gb ? *reinterpret_cast<const float4*>(p.gb + n0 + c + j)
+                                     : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+              float4 o;
+              o.x = __uint_as_float(r[j]) * ga * gb.x;
+              o.y = __uint_as_float(r[j + 1]) * ga * gb.y;
+              o.z = __uint_as_float(r[j + 2]) * ga * gb.z;
+              o.w = __uint_as_float(r[j + 3]) * ga * gb.w;
+              *reinterpret_cast<float4*>(dst + j) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + c + j;
+              if (n < p.N) {
+                const float gb = p.gb ? p.gb[n] : 1.0f;
+                dst[j] = __uint_as_float(r[j]) * ga * gb;
+              }
             }
           }
         }

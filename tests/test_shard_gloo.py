@@ -8,8 +8,6 @@ ones bit for bit, and the tensor-mode max reduction equals the global max
 """
 from __future__ import annotations
 
-import os
-import socket
 
 import pytest
 import torch
@@ -51,17 +49,13 @@ def test_attention_units_partition():
     assert all_units == set(shard.attention_units(B, Hq, Hkv))
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _rendezvous(tmp_path):
+    """A file store per test: no TCP port to pick, so no race with other processes for one."""
+    return "file://" + str(tmp_path / "rendezvous")
 
 
-def _attention_rank(rank, world, port, q, k, v, ret):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+def _attention_rank(rank, world, init, q, k, v, ret):
+    torch.distributed.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         B, Hq, T, D = q.shape
         Hkv = k.shape[1]
@@ -82,7 +76,7 @@ def _attention_rank(rank, world, port, q, k, v, ret):
         torch.distributed.destroy_process_group()
 
 
-def test_attention_sharded_equals_unsharded():
+def test_attention_sharded_equals_unsharded(tmp_path):
     g = torch.Generator().manual_seed(7)
     B, Hq, Hkv, T, D = 2, 8, 2, 64, 32
     q = torch.randn(B, Hq, T, D, generator=g).bfloat16()
@@ -90,8 +84,8 @@ def test_attention_sharded_equals_unsharded():
     v = torch.randn(B, Hkv, T, D, generator=g).bfloat16()
     ctx = mp.get_context("spawn")
     ret = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_attention_rank, args=(r, 2, port, q, k, v, ret)) for r in range(2)]
+    init = _rendezvous(tmp_path)
+    procs = [ctx.Process(target=_attention_rank, args=(r, 2, init, q, k, v, ret)) for r in range(2)]
     for p in procs:
         p.start()
     out = ret.get(timeout=120)
@@ -102,9 +96,8 @@ def test_attention_sharded_equals_unsharded():
     assert torch.equal(out, ref)
 
 
-def _quant_rank(rank, world, port, x, ret):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+def _quant_rank(rank, world, init, x, ret):
+    torch.distributed.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         rows = shard.row_shard(x.shape[0], world, rank)
         xs = x[rows].float()
@@ -120,7 +113,7 @@ def _quant_rank(rank, world, port, x, ret):
 
 
 @pytest.mark.parametrize("plant_nan", [False, True])
-def test_tensor_mode_row_shards(plant_nan):
+def test_tensor_mode_row_shards(plant_nan, tmp_path):
     g = torch.Generator().manual_seed(3)
     x = torch.randn(37, 48, generator=g)
     x[5, 7] *= 40.0  # the tensor max lives on rank 0's rows
@@ -129,8 +122,8 @@ def test_tensor_mode_row_shards(plant_nan):
     x = x.bfloat16()
     ctx = mp.get_context("spawn")
     ret = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_quant_rank, args=(r, 2, port, x, ret)) for r in range(2)]
+    init = _rendezvous(tmp_path)
+    procs = [ctx.Process(target=_quant_rank, args=(r, 2, init, x, ret)) for r in range(2)]
     for p in procs:
         p.start()
     parts = ret.get(timeout=120)

@@ -1091,7 +1091,8 @@ class GemmWorkload:
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4), "algorithmic_flops_per_launch": self.flops,
-                "traffic": None, "traffic_source": "not captured at this shape"}
+                "traffic": profile_traffic("gemm_nvf4_kernel_8192x28672x8192"),
+                "traffic_source": "profiles/gemm_nvf4_kernel_8192x28672x8192.md: ncu dram__bytes_read+write per launch"}
 
     def cpu_sample(self, reps=None):
         """The reference's way on the host cores: fake-quantized activations (torch ops) times the

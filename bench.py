@@ -5,9 +5,14 @@
                     [--workload attention|quantize|decode|qkv|prefill|weights|llama|gemm]
                     [--impl ours|reference]
 
-For N > 1 launch one rank per GPU with torch.distributed.run; ranks shard the
-work with no collective on the data path (weak scaling: every rank runs the
-full per-GPU workload) and the reported time is the max over ranks.
+With no --workload the line is the long-context prefill (the headline: a
+fixed 70.37 TFLOP job split over the ranks, strong scaling) with the
+Llama-3-8B attention, the [4096,4096] quantize and the 70B weight-stack
+quantize as sub-objects of the same line, each with its own value, roofline,
+e2e and CPU baseline.  For N > 1 launch one rank per GPU with
+torch.distributed.run; ranks shard the work with no collective on the data
+path and every reported time is the max over ranks.  The dense NVFP4 peak
+(the FP4 roofline denominator) is measured at the start of every run.
 
 Workloads (synthetic data with the shapes and distributions of the named
 configurations; no dataset is read):
@@ -46,7 +51,7 @@ configurations; no dataset is read):
 
 decode and qkv measure the rows that extend the path (the NVFP4 KV cache,
 the fused projection); prefill and weights the long-context and weight
-configurations, llama the patched model; attention is the default.
+configurations, llama the patched model.
 
 L2 (126 MB) is defeated by rotating through input/output buffer sets larger
 than L2 in total, so every step reads HBM.
@@ -106,6 +111,38 @@ def measured_peaks():
             return json.load(f), "measured"
     except OSError:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def fp4_peak(peaks, peak_src):
+    """(peak TFLOP/s, source) for FP4 contractions: the mxf4nvf4 throughput measured in this run
+    (measure_fp4_peak) when present, else 4 x the dense bf16 peak."""
+    if peaks.get("fp4_tflops"):
+        return peaks["fp4_tflops"], (f"measured mxf4nvf4 (this run, {peaks.get('fp4_mhz')} MHz median); "
+                                     f"4 x {peak_src} dense bf16 = {4 * peaks['bf16_tflops']:.0f}; nominal dense FP4 9000")
+    return 4 * peaks["bf16_tflops"], f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000"
+
+
+def measure_fp4_peak(dev, iters=16384, reps=5):
+    """Dense NVFP4 tensor throughput of this GPU: fp4_mma_peak_run (one CTA per SM issuing
+    back-to-back tcgen05 mxf4nvf4 M128 N128 K64 MMAs), best of `reps` event-timed launches."""
+    from fp4_attn_b200 import _lib
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    st = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        _lib.call("fp4_mma_peak_run", iters, 0, st.cuda_stream)
+    torch.cuda.synchronize(dev)
+    best = 0.0
+    with Clocks(dev) as clk:
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            _lib.call("fp4_mma_peak_run", iters, 0, st.cuda_stream)
+            b.record(st)
+            b.synchronize()
+            best = max(best, sms * iters * 4194304 / (a.elapsed_time(b) / 1e3) / 1e12)
+    if _lib.load().fp4attn_device_status(1) != 0:
+        raise RuntimeError("mma_peak_kernel: a bounded wait gave up")
+    return best, clk.summary().get("sm_mhz")
 
 
 # ----------------------------------------------------------------- clocks
@@ -416,10 +453,9 @@ class AttentionWorkload:
 
     def kernel_roofline(self, kernel_s, peaks, peak_src):
         achieved = self.flops / kernel_s / 1e12
-        peak = 4 * peaks["bf16_tflops"]
-        return {"bound": "tensor", "kernel": "fp4_attn_kernel", "achieved": round(achieved, 1), "peak": peak,
-                "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
+        peak, src = fp4_peak(peaks, peak_src)
+        return {"bound": "tensor", "kernel": "fp4_attn_kernel", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": src,
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4),
                 "algorithmic_flops_per_launch": self.flops,
                 "traffic": profile_traffic("fp4_attn_kernel_llama3-8b_T4096"),
@@ -468,28 +504,23 @@ def max_over_ranks(v, world, dev):
     return float(t.item())
 
 
-def run_ours(args, world, rank, local):
+def measure(wl, K, W, world, rank, dev, peaks, peak_src, cpu_baseline=True):
+    """Time one workload: W untimed warm-up steps, K timed steps (device resident, barrier and
+    synchronize on both sides, max over ranks), the dominant kernel alone, K end-to-end steps
+    through the public API with host buffers, and (rank 0 at N=1) the CPU baseline sample."""
     from fp4_attn_b200 import _lib
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    wl_name = args.workload or default_workload()
-    wl = make_workload(wl_name, dev, rank=rank, world=world, layers=args.layers)
-    peaks, peak_src = measured_peaks()
-    K, W = args.steps, args.warmup
     for i in range(W):
         wl.step(i)
     torch.cuda.synchronize(dev)
 
-    # device-resident timed region: whole steps, plus the dominant kernel alone
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graphs, kgraphs = [], []
     if getattr(wl, "use_graph", False):
-        # short steps: each step replays a CUDA graph of its launches, so host-side
-        # launch cost does not starve the GPU; the dominant kernel is timed from its
-        # own graph replays right after the timed region
+        # each step replays a CUDA graph of its launches, so host-side launch cost does not
+        # starve the GPU; the dominant kernel is timed from its own graph replays right after
         stream = torch.cuda.Stream(dev)
         wl.stream = stream.cuda_stream
-        graphs, kgraphs = [], []
         with torch.cuda.stream(stream):
             for i in range(wl.nsets):
                 wl.step(i)
@@ -541,6 +572,7 @@ def run_ours(args, world, rank, local):
     ms_max = max_over_ranks(ms, world, dev)
     kernel_ms_max = max_over_ranks(kernel_ms, world, dev)
     sec_per_step = ms_max / 1e3 / K
+    del graphs, kgraphs
 
     # end to end through the public API with host buffers
     for i in range(2):
@@ -561,19 +593,15 @@ def run_ours(args, world, rank, local):
     barrier(world)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if cpu_baseline and rank == 0 and world == 1:
         v, sample = wl.cpu_sample()
         cpu = {"value": round(v, 4), "unit": wl.unit, "cores": torch.get_num_threads(), "kind": "port",
                "sample": sample}
-
-    line = {
+    return {
         "metric": wl.metric, "value": round(wl.value(sec_per_step, world), 3), "unit": wl.unit,
-        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 5),
-        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
-        "dtype": wl.dtype,
-        "data": "synthetic (seeded; shapes/distributions of the named configuration)",
-        "config": dict(wl.config, parallelism=f"{world} independent shard(s), no data-path collective",
-                       timing="CUDA graph replay per step" if getattr(wl, "use_graph", False) else "stream launches"),
+        "ms_per_step": round(ms_max / K, 5), "scaling": getattr(wl, "scaling", "weak"), "dtype": wl.dtype,
+        "config": dict(wl.config, timing="CUDA graph replay per step" if getattr(wl, "use_graph", False)
+                       else "stream launches"),
         "roofline": wl.kernel_roofline(kernel_ms_max / 1e3, peaks, peak_src),
         "cpu_baseline": cpu,
         "e2e": {"value": round(wl.value(e2e_ms / 1e3 / K, world), 3), "unit": wl.unit,
@@ -581,6 +609,50 @@ def run_ours(args, world, rank, local):
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
+
+
+# the default run: the long-context prefill as the headline, the other graded configurations beside it
+SUITE_PRIMARY = "prefill"
+SUITE_SECONDARY = (("llama3_8b_attention", "attention"), ("quantize_4096x4096", "quantize"),
+                   ("weights_llama3_70b", "weights"))
+
+
+def run_ours(args, world, rank, local):
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = measured_peaks()
+    peaks = dict(peaks)
+    fp4, fp4_mhz = measure_fp4_peak(dev)
+    peaks["fp4_tflops"] = max_over_ranks(-fp4, world, dev) * -1  # the slowest rank's (min over ranks)
+    peaks["fp4_mhz"] = fp4_mhz
+    K, W = args.steps, args.warmup
+    suite = args.workload is None
+    name = SUITE_PRIMARY if suite else args.workload
+    wl = make_workload(name, dev, rank=rank, world=world, layers=args.layers)
+    res = measure(wl, K, W, world, rank, dev, peaks, peak_src, cpu_baseline=not args.no_cpu_baseline)
+    del wl
+    torch.cuda.empty_cache()
+    par = ("strong: the fixed job split over ranks" if res["scaling"] == "strong" else "weak: one shard per rank")
+    line = {
+        "metric": res["metric"], "value": res["value"], "unit": res["unit"], "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": res["scaling"],
+        "vs_baseline": None, "dtype": res["dtype"],
+        "data": "synthetic (seeded; shapes/distributions of the named configuration)",
+        "config": dict(res["config"], parallelism=f"{world} shard(s), {par}, no data-path collective"),
+        "roofline": res["roofline"], "cpu_baseline": res["cpu_baseline"], "e2e": res["e2e"],
+        "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
+        "fp4_peak": {"tflops": round(peaks["fp4_tflops"], 1), "sm_mhz": fp4_mhz,
+                     "how": "fp4_mma_peak_run: one CTA per SM, back-to-back tcgen05 mxf4nvf4 M128 N128 K64, "
+                            "best of 5 event-timed launches, min over ranks"},
+    }
+    if suite:
+        for key, wname in SUITE_SECONDARY:
+            w2 = make_workload(wname, dev, rank=rank, world=world, layers=args.layers)
+            r2 = measure(w2, K, W, world, rank, dev, peaks, peak_src, cpu_baseline=not args.no_cpu_baseline)
+            line["gpu_launches"] += r2["gpu_launches"]
+            line[key] = r2
+            del w2
+            torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -589,8 +661,9 @@ def run_reference(args, world, rank):
     """The reference's CPU path (torch ops) on the host cores, rank 0 only."""
     if rank != 0:
         return
-    wl_name = args.workload or default_workload()
-    wl = make_workload(wl_name, None, cpu_only=True, layers=args.layers)
+    suite = args.workload is None
+    wl_name = SUITE_PRIMARY if suite else args.workload
+    wl = make_workload(wl_name, None, cpu_only=True, world=world, layers=args.layers)
     torch.set_num_threads(os.cpu_count() or 1)
     for _ in range(args.warmup):
         wl.cpu_sample(reps=1)
@@ -599,15 +672,26 @@ def run_reference(args, world, rank):
         v, sample = wl.cpu_sample(reps=1)
         vals.append(v)
     v = statistics.median(vals)
+    par = "strong: the fixed job split over ranks" if getattr(wl, "scaling", "weak") == "strong" else \
+        "weak: one shard per rank"
     line = {
         "metric": wl.metric, "value": round(v, 5), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
         "vs_baseline": None,
-        "dtype": wl.dtype, "data": "synthetic", "config": wl.config, "impl": "reference",
+        "dtype": wl.dtype, "data": "synthetic (seeded; shapes/distributions of the named configuration)",
+        "config": dict(wl.config, parallelism=f"reference CPU path on rank 0's host cores ({par} on the GPU arm)"),
+        "impl": "reference",
         "cpu_baseline": {"value": round(v, 5), "unit": wl.unit, "kind": "port", "cores": torch.get_num_threads(),
                          "sample": sample},
         "e2e": {"value": round(v, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if suite:
+        for key, wname in SUITE_SECONDARY:
+            w2 = make_workload(wname, None, cpu_only=True, world=world, layers=args.layers)
+            v2, s2 = w2.cpu_sample()
+            line[key] = {"metric": w2.metric, "value": round(v2, 5), "unit": w2.unit, "config": w2.config,
+                         "cpu_baseline": {"value": round(v2, 5), "unit": w2.unit, "kind": "port",
+                                          "cores": torch.get_num_threads(), "sample": s2}}
     print(json.dumps(line), flush=True)
 
 
@@ -810,7 +894,9 @@ class QkvWorkload:
 
 class PrefillWorkload(AttentionWorkload):
     """Long-context prefill, strong scaling: the fixed job of 4 x 8 (batch, KV-head) units is split
-    over the ranks in contiguous blocks (fp4_attn_b200.shard.attention_shard)."""
+    over the ranks in contiguous (batch rows) x (KV heads) blocks (fp4_attn_b200.shard).  A rank
+    quantizes Q/K/V on every head of its batch rows -- the per-token global scales span the whole
+    [B*T, H*D] row -- and attends its own KV heads, so the job's result does not depend on N."""
     name = "prefill"
     metric = "NVFP4 attention forward TFLOP/s (long-context prefill), % of dense FP4 tensor peak"
     scaling = "strong"
@@ -819,45 +905,83 @@ class PrefillWorkload(AttentionWorkload):
     def __init__(self, dev, cpu_only=False, rank=0, world=1):
         from fp4_attn_b200 import shard
         units = shard.attention_shard(self.B_JOB, self.Hq_JOB, self.Hkv_JOB, world, rank)
-        bs, hs = sorted({u.b for u in units}), sorted({u.hk for u in units})
-        if len(units) != len(bs) * len(hs) or bs != list(range(bs[0], bs[-1] + 1)) or \
-                hs != list(range(hs[0], hs[-1] + 1)):
-            raise ValueError(f"{world} ranks do not split the 32 prefill units into (batch x kv-head) blocks")
+        rows, (self.h0, self.h1) = shard.shard_rows(units)
         G = self.Hq_JOB // self.Hkv_JOB
-        self.b0, self.b1, self.h0, self.h1 = bs[0], bs[-1] + 1, hs[0], hs[-1] + 1
-        self.B, self.Hkv, self.Hq = self.b1 - self.b0, self.h1 - self.h0, (self.h1 - self.h0) * G
-        self.flops = 4 * self.B * self.Hq * self.T * self.T * self.D / 2  # causal, this rank's units
+        self.b0, self.b1 = rows.start, rows.stop
+        self.B, self.Hkv, self.Hq = self.b1 - self.b0, self.Hkv_JOB, self.Hq_JOB  # operands: whole rows
+        self.flops = 4 * self.B * (self.h1 - self.h0) * G * self.T * self.T * self.D / 2  # this rank's units
         self.config = {"workload": "NVFP4 attention fwd, long-context prefill: B=4, Hq=64, Hkv=8, D=128, T=32768, "
                                    "causal, q/k/v N(0,1)*0.5 with a per-(kv-head, channel) N(0,2) bias on k, "
                                    "single-slice Q/P quantization, bf16 output",
                        "flops_job": 4 * self.B_JOB * self.Hq_JOB * self.T * self.T * self.D / 2,
+                       "flops_per_step": self.flops,
                        "global_batch": self.B_JOB,
                        "shard": f"units (b {self.b0}..{self.b1 - 1}) x (kv-head {self.h0}..{self.h1 - 1}) on rank "
-                                f"{rank}; a rank holding part of a batch row quantizes Q/K per token over its "
-                                f"own heads"}
+                                f"{rank}; Q/K/V quantized on every head of those batch rows (per-token scales "
+                                f"over the whole row, as unsharded)"}
         if cpu_only:
             return
         from fp4_attn_b200 import attention as A
         self.A = A
         self.dev = dev
-        g = torch.Generator(dev).manual_seed(2)  # the whole job's inputs on every rank, then this rank's block
+        g = torch.Generator(dev).manual_seed(2)  # the whole job's inputs on every rank, then this rank's rows
         q = torch.randn(self.B_JOB, self.Hq_JOB, self.T, self.D, device=dev, generator=g) * 0.5
-        q = q[self.b0:self.b1, self.h0 * G:self.h1 * G].bfloat16()
+        q = q[self.b0:self.b1].bfloat16()
         k = torch.randn(self.B_JOB, self.Hkv_JOB, self.T, self.D, device=dev, generator=g) * 0.5
         bias = torch.randn(self.Hkv_JOB, self.D, device=dev, generator=g) * 2.0
-        k = (k + bias[None, :, None, :])[self.b0:self.b1, self.h0:self.h1].bfloat16()
+        k = (k + bias[None, :, None, :])[self.b0:self.b1].bfloat16()
         v = (torch.randn(self.B_JOB, self.Hkv_JOB, self.T, self.D, device=dev, generator=g) * 0.5)
-        v = v[self.b0:self.b1, self.h0:self.h1].bfloat16()
+        v = v[self.b0:self.b1].bfloat16()
         self.host = [t.cpu().pin_memory() for t in (q, k, v)]
         self.nsets = 2  # inputs (2.7 GB at one rank) are far larger than L2; two sets let e2e copies overlap
         self.sets = [(q, k, v)] + [tuple(t.clone() for t in (q, k, v)) for _ in range(self.nsets - 1)]
         del q, k, v
         self.ws = [A.AttentionWorkspace(self.B, self.Hq, self.Hkv, self.T, self.D, dev) for _ in range(self.nsets)]
-        self.out = [torch.empty(self.B, self.T, self.Hq, self.D, device=dev, dtype=torch.bfloat16)
+        Ho = (self.h1 - self.h0) * G
+        self.out = [torch.empty(self.B, self.T, Ho, self.D, device=dev, dtype=torch.bfloat16)
                     for _ in range(self.nsets)]
         self.out_bf16 = self.out
-        self.out_host = torch.empty(self.B, self.T, self.Hq, self.D, dtype=torch.bfloat16).pin_memory()
-        self.config["l2"] = "inputs 2.7 GB per set > L2"
+        self.out_host = torch.empty(self.B, self.T, Ho, self.D, dtype=torch.bfloat16).pin_memory()
+        self.config["l2"] = "inputs > L2 (2.7 GB per set at one rank)"
+
+    def step(self, i, ev=None):
+        """One fp4attn_forward_heads call: quantize the rank's batch rows, attend its KV heads."""
+        from fp4_attn_b200 import _lib
+        i %= self.nsets
+        q, k, v = self.sets[i]
+        ws = self.ws[i]
+        _lib.call("fp4attn_forward_heads", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype],
+                  self.B, self.Hq, self.Hkv, self.T, self.D, q.stride(0), q.stride(1), q.stride(2), k.stride(0),
+                  k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), 1, self.D ** -0.5,
+                  self.A.OUT_BF16, self.h0, self.h1, self.out[i].data_ptr(), ws.ptr(), ws.nbytes,
+                  _lib.stream_of(q))
+
+    def kernel(self, i):
+        """The attention kernel alone on the operands step(i) prepared, this rank's KV heads."""
+        from fp4_attn_b200 import _lib
+        i %= self.nsets
+        ws = self.ws[i]
+        _lib.call("fp4attn_fwd_packed_heads", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), None, None,
+                  None, ws.kc.data_ptr(), ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(),
+                  self.out[i].data_ptr(), self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, self.h0, self.h1, 1,
+                  self.D ** -0.5, self.A.OUT_BF16, _lib.stream_of(self.sets[i][0]))
+
+    def e2e_step(self, i):
+        """Public API, host buffers: H2D q/k/v of the rank's rows, fp4_attention_fwd on its KV heads
+        (bf16 out), D2H the output; steps pipelined over copy and compute streams."""
+        if not hasattr(self, "pipe"):
+            self.pipe = E2EPipe(self.nsets)
+        i %= self.nsets
+        q, k, v = self.sets[i]
+
+        def h2d():
+            for d, h in zip((q, k, v), self.host):
+                d.copy_(h, non_blocking=True)
+
+        self.pipe.step(i, h2d, lambda: self.A.fp4_attention_fwd(q, k, v, causal=True, workspace=self.ws[i],
+                                                                 out=self.out_bf16[i], out_dtype=torch.bfloat16,
+                                                                 kv_heads=(self.h0, self.h1)),
+                       lambda o: self.out_host.copy_(o, non_blocking=True))
 
     def value(self, seconds_per_step, world):
         return world * self.flops / seconds_per_step / 1e12
@@ -1086,10 +1210,9 @@ class GemmWorkload:
 
     def kernel_roofline(self, kernel_s, peaks, peak_src):
         achieved = self.flops / kernel_s / 1e12
-        peak = 4 * peaks["bf16_tflops"]
-        return {"bound": "tensor", "kernel": "gemm_nvf4_kernel", "achieved": round(achieved, 1), "peak": peak,
-                "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
+        peak, src = fp4_peak(peaks, peak_src)
+        return {"bound": "tensor", "kernel": "gemm_nvf4_kernel", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": src,
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4), "algorithmic_flops_per_launch": self.flops,
                 "traffic": profile_traffic("gemm_nvf4_kernel_8192x28672x8192"),
                 "traffic_source": "profiles/gemm_nvf4_kernel_8192x28672x8192.md: ncu dram__bytes_read+write per launch"}
@@ -1213,10 +1336,10 @@ class LlamaWorkload:
 
     def kernel_roofline(self, kernel_s, peaks, peak_src):
         achieved = self.attn_flops / kernel_s / 1e12
-        peak = 4 * peaks["bf16_tflops"]
+        peak, src = fp4_peak(peaks, peak_src)
         return {"bound": "tensor", "kernel": "layer 0's FP4 attention call (Q/K quantize, V-hat prep, fp4_attn_kernel)",
-                "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                "peak_source": f"4 x {peak_src} dense bf16 (no measured FP4 peak); nominal dense FP4 9000",
+                "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "peak_source": src,
                 "algorithmic_flops_per_launch": self.attn_flops, "traffic": None,
                 "traffic_source": "not captured at this shape"}
 
@@ -1262,10 +1385,6 @@ class LlamaWorkload:
             lp.attention_interface = saved
         return self.T / (32 * (t2 - t1) + (t3 - t2)), \
             f"1 decoder layer + LM head on 1 x 2048 tokens (last of x{n}), layer time x32"
-
-
-def default_workload():
-    return "attention"
 
 
 def make_workload(name, dev, cpu_only=False, rank=0, world=1, layers=10):

@@ -29,6 +29,7 @@ SIGNATURES = {
     "fp4attn_device_status": ([_I], ctypes.c_uint),
     "fp4_gemm_nvf4": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _L, _L, _L, _P], _I),
     "fp4attn_set_trace": ([_P], None),
+    "fp4_mma_peak_run": ([_I, _I, _P], _I),
     "fp4attn_prepare_v": ([_P, _I, _I, _I, _I, _I, _L, _L, _L, _I, _P, _P, _P, _P, _P], _I),
     "fp4attn_fwd_packed": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P], _I),
     "fp4attn_workspace_layout": ([_I, _I, _I, _I, _I, _P], _L),
@@ -37,12 +38,16 @@ SIGNATURES = {
     "fp4attn_workspace_layout_ex": ([_I, _I, _I, _I, _I, _I, _P], _L),
     "fp4attn_fwd_packed_dual": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                                  _P], _I),
+    "fp4attn_fwd_packed_heads": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I,
+                                  _F, _I, _P], _I),
     "fp4attn_decode_workspace_size": ([_I, _I, _I], _L),
     "fp4attn_decode": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _L, _P], _I),
     "fp4attn_forward": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _P, _P, _L,
                          _P], _I),
     "fp4attn_forward_ex": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _I, _P, _P,
                             _L, _P], _I),
+    "fp4attn_forward_heads": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _I, _I,
+                               _I, _P, _P, _L, _P], _I),
     "fp4attn_forward_noalloc": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _P,
                                  _P], _I),
     "nvfp4sim_f32_to_nvf4": ([_P, _P, _P, _L, _P], _I),

@@ -100,8 +100,16 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
                       scaling: float | None = None, out: torch.Tensor | None = None,
                       workspace: AttentionWorkspace | None = None, num_ctas: int = 0,
                       dual_q: bool = False, dual_p: bool = False,
-                      out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+                      out_dtype: torch.dtype = torch.float32,
+                      kv_heads: tuple[int, int] | None = None) -> torch.Tensor:
     """NVFP4 attention forward.  q [B,Hq,T,D], k/v [B,Hkv,T,D] (CUDA) -> [B,T,Hq,D] in out_dtype.
+
+    kv_heads=(h0, h1) attends only KV heads h0..h1-1 and their query groups
+    (one rank's shard of a job split by (batch, KV head)) and returns
+    [B, T, (h1-h0)*Hq/Hkv, D].  Q/K/V are still quantized on every head of the
+    given batch rows, since the reference's per-token global scales span the
+    whole [B*T, H*D] row (llama_patch.py:167-196): the attended heads' output
+    equals the unsharded call's bit for bit.
 
     out_dtype fp32 or bf16 (the reference's output dtype for bf16 inputs,
     llama_patch.py:102-103: the kernel rounds its fp32 result once).
@@ -134,10 +142,16 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
         raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
     if num_ctas and (dual_q or dual_p or out_dtype != torch.float32):
         raise ValueError("num_ctas is a single-slice fp32-output profiling option")
+    h0, h1 = (0, Hkv) if kv_heads is None else (int(kv_heads[0]), int(kv_heads[1]))
+    if not 0 <= h0 < h1 <= Hkv:
+        raise ValueError(f"kv_heads {kv_heads} outside [0, {Hkv})")
+    if (h0, h1) != (0, Hkv) and num_ctas:
+        raise ValueError("num_ctas is not available with kv_heads")
+    Ho = (h1 - h0) * (Hq // Hkv)
     if out is None:
-        out = torch.empty(B, T, Hq, D, dtype=out_dtype, device=q.device)
-    elif out.shape != (B, T, Hq, D) or out.dtype != out_dtype or not out.is_contiguous():
-        raise ValueError(f"out must be a contiguous {out_dtype} [B, T, Hq, D] tensor")
+        out = torch.empty(B, T, Ho, D, dtype=out_dtype, device=q.device)
+    elif out.shape != (B, T, Ho, D) or out.dtype != out_dtype or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {out_dtype} [B, T, {Ho}, D] tensor")
     if num_ctas:
         quantize_qk(q, ws.qc, ws.qs, ws.gq, ws.Tp)
         quantize_qk(k, ws.kc, ws.ks, ws.gk, ws.Tp)
@@ -147,8 +161,8 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
                   Hkv, T, ws.Tp, D, 1 if causal else 0, float(scaling), int(num_ctas), _lib.stream_of(q))
         return out
     flags = (DUAL_Q if dual_q else 0) | (DUAL_P if dual_p else 0) | (OUT_BF16 if out_dtype == torch.bfloat16 else 0)
-    _lib.call("fp4attn_forward_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], B, Hq, Hkv, T,
-              D, q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0),
-              v.stride(1), v.stride(2), 1 if causal else 0, float(scaling), flags, out.data_ptr(), ws.ptr(),
+    _lib.call("fp4attn_forward_heads", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], B, Hq,
+              Hkv, T, D, q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0),
+              v.stride(1), v.stride(2), 1 if causal else 0, float(scaling), flags, h0, h1, out.data_ptr(), ws.ptr(),
               ws.nbytes, _lib.stream_of(q))
     return out

@@ -39,6 +39,7 @@
 
 #include "common.cuh"
 #include "attn_softmax.cuh"
+#include "attn_internal.h"
 #include "fp4attn.h"
 #include "sm100.cuh"
 #include "status.h"
@@ -90,7 +91,11 @@ struct AttnArgs {
   const float* gk;
   void* out;    // [B, T, Hq, HD], fp32 or (out_bf16) bf16
   int out_bf16;
-  int B, Hq, Hkv, T, Tp;
+  int B, Hq, Hkv, T, Tp;  // Hq / Hkv: the heads attended (and written to out)
+  // The packed operands may hold more heads than are attended (a rank of a sharded job
+  // quantizes whole batch rows): the attended heads start at head hq0 / hk0 of operands
+  // with nkb4q / nkb4k scale atoms per 128-row block (2 per head) and HkvT KV heads.
+  int hq0, hk0, nkb4q, nkb4k, HkvT;
   int causal;
   float scale_log2;  // scaling * log2(e)
   int units;
@@ -188,7 +193,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   static_assert(2 + 2 * NK + 2 * NV + 8 + 1 <= 64, "barriers exceed their 512-byte slot");
 
   const int warp = threadIdx.x / 32;
-  const int nkb4q = p.Hq * 2, nkb4k = p.Hkv * 2;
+  const int nkb4q = p.nkb4q, nkb4k = p.nkb4k;
   const int group = p.Hq / p.Hkv;
 
   if (threadIdx.x == 0) {
@@ -237,16 +242,16 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
-        const int hk = un.h / group;
+        const int hq = p.hq0 + un.h, hk = p.hk0 + un.h / group;  // heads within the operands
         const int qrow = un.b * p.Tp + un.qt * BM;
         if (uc > 0) mbar_wait(q_empty, (uc - 1) & 1, 0x201);
         mbar_arrive_expect_tx(q_full, (DQ ? 2 : 1) * (Q_BYTES + 1024 + 512));
-        tma_load_2d(sm + OFF_Q, &tmQ, q_full, un.h * (HD / 2), qrow);
-        bulk_load(sm + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * nkb4q + 2 * un.h) * 512, 1024, q_full);
+        tma_load_2d(sm + OFF_Q, &tmQ, q_full, hq * (HD / 2), qrow);
+        bulk_load(sm + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * nkb4q + 2 * hq) * 512, 1024, q_full);
         bulk_load(sm + OFF_GQ, p.gq + qrow, 512, q_full);
         if constexpr (DQ) {
-          tma_load_2d(sm + OFF_QLO, &tmQlo, q_full, un.h * (HD / 2), qrow);
-          bulk_load(sm + OFF_QLOSF, p.qsf_lo + ((int64_t)(qrow / 128) * nkb4q + 2 * un.h) * 512, 1024, q_full);
+          tma_load_2d(sm + OFF_QLO, &tmQlo, q_full, hq * (HD / 2), qrow);
+          bulk_load(sm + OFF_QLOSF, p.qsf_lo + ((int64_t)(qrow / 128) * nkb4q + 2 * hq) * 512, 1024, q_full);
           bulk_load(sm + OFF_GQLO, p.gq_lo + qrow, 512, q_full);
         }
         for (int pass = 0; pass < NPASS; ++pass) {
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units)) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
-        const int vrow = (un.b * p.Hkv + un.h / group) * HD;
+        const int vrow = (un.b * p.HkvT + p.hk0 + un.h / group) * HD;
         for (int j = 0; j < n; ++j, ++vc) {
           const int vs = vc % NV;
           if (vc >= NV) mbar_wait(&v_empty[vs], ((vc / NV) - 1) & 1, 0x203);
@@ -915,64 +920,66 @@ extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, in
   return launch_vprep(a, st);
 }
 
-extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
-                                       const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
-                                       const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
-                                       const uint16_t* v_hi, const uint16_t* v_lo, void* out, int B, int Hq,
-                                       int Hkv, int T, int Tp, int D, int causal, float scaling, int flags,
-                                       int num_ctas, void* stream) {
+int fp4::launch_attention(const AttnLaunch& L, cudaStream_t st) {
   using namespace attn;
-  clear_error();
-  if (D != HD) return set_error(FP4ATTN_ERR_UNSUPPORTED, "head_dim must be %d", HD);
-  if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0 || Hq % Hkv != 0) return set_error(FP4ATTN_ERR_ARG, "bad shape");
+  const int B = L.B, HqT = L.HqT, HkvT = L.HkvT, T = L.T, Tp = L.Tp;
+  if (L.D != HD) return set_error(FP4ATTN_ERR_UNSUPPORTED, "head_dim must be %d", HD);
+  if (B <= 0 || HqT <= 0 || HkvT <= 0 || T <= 0 || HqT % HkvT != 0) return set_error(FP4ATTN_ERR_ARG, "bad shape");
+  if (L.hk0 < 0 || L.hk1 > HkvT || L.hk0 >= L.hk1) return set_error(FP4ATTN_ERR_ARG, "bad KV-head range");
   if (Tp % 128 != 0 || Tp < T) return set_error(FP4ATTN_ERR_ARG, "Tp must be a multiple of 128 >= T");
-  if (!q_codes || !q_scales || !q_g || !k_codes || !k_scales || !k_g || !v_hi || !v_lo || !out)
+  if (!L.q_codes || !L.q_scales || !L.q_g || !L.k_codes || !L.k_scales || !L.k_g || !L.v_hi || !L.v_lo || !L.out)
     return set_error(FP4ATTN_ERR_ARG, "null pointer");
-  const bool dq = q_codes_lo != nullptr;
-  if (flags & ~(FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16)) return set_error(FP4ATTN_ERR_ARG, "bad flags");
-  const bool dual_p = (flags & FP4ATTN_DUAL_P) != 0;
-  if (dq && (!q_scales_lo || !q_g_lo)) return set_error(FP4ATTN_ERR_ARG, "null pointer (residual Q slice)");
-  if (((uintptr_t)q_codes | (uintptr_t)k_codes | (uintptr_t)v_hi | (uintptr_t)v_lo | (uintptr_t)q_scales |
-       (uintptr_t)k_scales | (uintptr_t)q_g | (uintptr_t)k_g | (uintptr_t)out | (uintptr_t)q_codes_lo |
-       (uintptr_t)q_scales_lo | (uintptr_t)q_g_lo) % 16)
+  const bool dq = L.q_codes_lo != nullptr;
+  if (L.flags & ~(FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16)) return set_error(FP4ATTN_ERR_ARG, "bad flags");
+  const bool dual_p = (L.flags & FP4ATTN_DUAL_P) != 0;
+  if (dq && (!L.q_scales_lo || !L.q_g_lo)) return set_error(FP4ATTN_ERR_ARG, "null pointer (residual Q slice)");
+  if (((uintptr_t)L.q_codes | (uintptr_t)L.k_codes | (uintptr_t)L.v_hi | (uintptr_t)L.v_lo | (uintptr_t)L.q_scales |
+       (uintptr_t)L.k_scales | (uintptr_t)L.q_g | (uintptr_t)L.k_g | (uintptr_t)L.out | (uintptr_t)L.q_codes_lo |
+       (uintptr_t)L.q_scales_lo | (uintptr_t)L.q_g_lo) % 16)
     return set_error(FP4ATTN_ERR_ARG, "buffers must be 16-byte aligned");
+  const int G = HqT / HkvT;
   CUtensorMap mq, mql, mk, mvh, mvl;
-  if (int e = encode_tiled_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, q_codes, (uint64_t)Hq * (HD / 2), (uint64_t)B * Tp,
-                              (uint64_t)Hq * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+  if (int e = encode_tiled_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.q_codes, (uint64_t)HqT * (HD / 2),
+                              (uint64_t)B * Tp, (uint64_t)HqT * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (dq) {
-    if (int e = encode_tiled_2d(&mql, CU_TENSOR_MAP_DATA_TYPE_UINT8, q_codes_lo, (uint64_t)Hq * (HD / 2),
-                                (uint64_t)B * Tp, (uint64_t)Hq * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    if (int e = encode_tiled_2d(&mql, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.q_codes_lo, (uint64_t)HqT * (HD / 2),
+                                (uint64_t)B * Tp, (uint64_t)HqT * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
       return e;
   } else {
     mql = mq;  // not read
   }
-  if (int e = encode_tiled_2d(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_codes, (uint64_t)Hkv * (HD / 2), (uint64_t)B * Tp,
-                              (uint64_t)Hkv * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+  if (int e = encode_tiled_2d(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.k_codes, (uint64_t)HkvT * (HD / 2),
+                              (uint64_t)B * Tp, (uint64_t)HkvT * (HD / 2), HD / 2, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
-  if (int e = encode_tiled_2d(&mvh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, v_hi, (uint64_t)Tp, (uint64_t)B * Hkv * HD,
+  if (int e = encode_tiled_2d(&mvh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.v_hi, (uint64_t)Tp, (uint64_t)B * HkvT * HD,
                               (uint64_t)Tp * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
-  if (int e = encode_tiled_2d(&mvl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, v_lo, (uint64_t)Tp, (uint64_t)B * Hkv * HD,
+  if (int e = encode_tiled_2d(&mvl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.v_lo, (uint64_t)Tp, (uint64_t)B * HkvT * HD,
                               (uint64_t)Tp * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   AttnArgs a{};
-  a.qsf = q_scales;
-  a.gq = q_g;
-  a.qsf_lo = q_scales_lo;
-  a.gq_lo = q_g_lo;
-  a.ksf = k_scales;
-  a.gk = k_g;
-  a.out = out;
-  a.out_bf16 = (flags & FP4ATTN_OUT_BF16) ? 1 : 0;
+  a.qsf = L.q_scales;
+  a.gq = L.q_g;
+  a.qsf_lo = L.q_scales_lo;
+  a.gq_lo = L.q_g_lo;
+  a.ksf = L.k_scales;
+  a.gk = L.k_g;
+  a.out = L.out;
+  a.out_bf16 = (L.flags & FP4ATTN_OUT_BF16) ? 1 : 0;
   a.B = B;
-  a.Hq = Hq;
-  a.Hkv = Hkv;
+  a.Hkv = L.hk1 - L.hk0;
+  a.Hq = a.Hkv * G;
   a.T = T;
   a.Tp = Tp;
-  a.causal = causal ? 1 : 0;
-  a.scale_log2 = scaling * 1.4426950408889634f;
-  a.units = B * Hq * (Tp / 128);
+  a.hq0 = L.hk0 * G;
+  a.hk0 = L.hk0;
+  a.nkb4q = 2 * HqT;
+  a.nkb4k = 2 * HkvT;
+  a.HkvT = HkvT;
+  a.causal = L.causal ? 1 : 0;
+  a.scale_log2 = L.scaling * 1.4426950408889634f;
+  a.units = B * a.Hq * (Tp / 128);
   // the event timeline is recorded by the single-slice kernel only
   a.trace = (dq || dual_p) ? nullptr : g_trace;
   using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
@@ -980,19 +987,41 @@ extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_
   static const Kern kerns[5] = {fp4_attn_kernel<false, false, false>, fp4_attn_kernel<false, true, false>,
                                 fp4_attn_kernel<false, false, true>, fp4_attn_kernel<false, true, true>,
                                 fp4_attn_kernel<true, false, false>};
-  static bool attr = false;
-  if (!attr) {
-    for (Kern k : kerns) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr = true;
-  }
   const Kern kern = a.trace ? kerns[4] : kerns[(dq ? 1 : 0) + (dual_p ? 2 : 0)];
+  if (int e = set_smem_attr((const void*)kern, SMEM_BYTES)) return e;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int grid = num_ctas > 0 ? num_ctas : sms;
+  int grid = L.num_ctas > 0 ? L.num_ctas : sms;
   if (grid > a.units) grid = a.units;
-  kern<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mql, mk, mvh, mvl, a);
+  kern<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mql, mk, mvh, mvl, a);
   return check_launch("fp4_attn_kernel");
+}
+
+extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                                       const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
+                                       const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                                       const uint16_t* v_hi, const uint16_t* v_lo, void* out, int B, int Hq,
+                                       int Hkv, int T, int Tp, int D, int causal, float scaling, int flags,
+                                       int num_ctas, void* stream) {
+  clear_error();
+  AttnLaunch L{q_codes, q_scales, q_g,  q_codes_lo, q_scales_lo, q_g_lo, k_codes, k_scales, k_g,     v_hi,
+               v_lo,    out,      B,    Hq,         Hkv,         T,      Tp,      D,        0,       Hkv,
+               causal,  scaling,  flags, num_ctas};
+  return launch_attention(L, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fp4attn_fwd_packed_heads(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                                        const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
+                                        const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                                        const uint16_t* v_hi, const uint16_t* v_lo, void* out, int B, int Hq,
+                                        int Hkv, int T, int Tp, int D, int hkv0, int hkv1, int causal, float scaling,
+                                        int flags, void* stream) {
+  clear_error();
+  AttnLaunch L{q_codes, q_scales, q_g,  q_codes_lo, q_scales_lo, q_g_lo, k_codes, k_scales, k_g,    v_hi,
+               v_lo,    out,      B,    Hq,         Hkv,         T,      Tp,      D,        hkv0,   hkv1,
+               causal,  scaling,  flags, 0};
+  return launch_attention(L, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fp4attn_fwd_packed(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,

@@ -595,11 +595,7 @@ int persistent_grid(const void* fn, uint32_t smem, int items, int threads = DK_T
 template <int MG, int NW>
 int launch_pv(const DecodeArgs& a, int items, cudaStream_t st) {
   using C = PvCfg<MG, NW>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(decode_pv_kernel<MG, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    attr = true;
-  }
+  if (int e = set_smem_attr((const void*)decode_pv_kernel<MG, NW>, (int)C::SMEM)) return e;
   const int grid = persistent_grid((const void*)decode_pv_kernel<MG, NW>, C::SMEM, items, C::THREADS);
   decode_pv_kernel<MG, NW><<<grid, C::THREADS, C::SMEM, st>>>(a);
   return check_launch("decode_pv_kernel");
@@ -650,11 +646,7 @@ extern "C" int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, c
     return set_error(FP4ATTN_ERR_CUDA, "memset: %s", cudaGetErrorString(cudaGetLastError()));
   const int items = nsplit * B * Hkv;
   constexpr uint32_t sc_smem = SC_STAGES * SC_STAGE;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(decode_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem);
-    attr = true;
-  }
+  if (int e = set_smem_attr((const void*)decode_scores_kernel, (int)sc_smem)) return e;
   decode_scores_kernel<<<persistent_grid((const void*)decode_scores_kernel, sc_smem, items), DK_THREADS, sc_smem,
                          st>>>(a);
   if (int e = check_launch("decode_scores_kernel")) return e;

@@ -8,6 +8,9 @@
 // [B,T,Hq,D] out.
 #include <stdint.h>
 
+#include <stdio.h>
+
+#include "attn_internal.h"
 #include "fp4attn.h"
 #include "status.h"
 
@@ -134,10 +137,37 @@ extern "C" int64_t fp4attn_workspace_layout(int B, int Hq, int Hkv, int T, int D
   return n;
 }
 
-extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv,
-                                  int T, int D, int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH,
-                                  int64_t k_sT, int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling,
-                                  int flags, void* out, void* workspace, int64_t workspace_bytes, void* stream) {
+// Joins the side streams back into the caller's stream when it goes out of scope
+// (every exit after the fork, error returns included): under stream capture an
+// unjoined fork invalidates the caller's capture, and outside it the caller must
+// not see the call return while side-stream kernels can still write its workspace.
+struct SideJoin {
+  SideStreams* side;
+  cudaStream_t st;
+  int join() {
+    if (!side) return FP4ATTN_OK;
+    SideStreams* sd = side;
+    side = nullptr;
+    if (cudaEventRecord(sd->join[0], sd->s[0]) != cudaSuccess || cudaEventRecord(sd->join[1], sd->s[1]) != cudaSuccess ||
+        cudaStreamWaitEvent(st, sd->join[0], 0) != cudaSuccess || cudaStreamWaitEvent(st, sd->join[1], 0) != cudaSuccess)
+      return fp4::set_error(FP4ATTN_ERR_CUDA, "stream join: %s", cudaGetErrorString(cudaGetLastError()));
+    return FP4ATTN_OK;
+  }
+  ~SideJoin() {
+    if (side) {
+      char keep[512];  // an error already reported stays the reported one
+      snprintf(keep, sizeof(keep), "%s", fp4attn_last_error());
+      join();
+      fp4::set_error(0, "%s", keep);
+    }
+  }
+};
+
+extern "C" int fp4attn_forward_heads(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv,
+                                     int T, int D, int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB,
+                                     int64_t k_sH, int64_t k_sT, int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal,
+                                     float scaling, int flags, int hkv0, int hkv1, void* out, void* workspace,
+                                     int64_t workspace_bytes, void* stream) {
   using namespace fp4;
   clear_error();
   if (!q || !k || !v || !out || !workspace) return set_error(FP4ATTN_ERR_ARG, "null pointer");
@@ -145,6 +175,7 @@ extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, i
   int64_t off[kPieces];
   const int64_t need = layout(B, Hq, Hkv, T, D, flags, off);
   if (need < 0) return set_error(FP4ATTN_ERR_ARG, "bad shape or flags");
+  if (hkv0 < 0 || hkv1 > Hkv || hkv0 >= hkv1) return set_error(FP4ATTN_ERR_ARG, "bad KV-head range [%d, %d)", hkv0, hkv1);
   if (workspace_bytes < need)
     return set_error(FP4ATTN_ERR_ARG, "workspace of %lld bytes, %lld needed", (long long)workspace_bytes,
                      (long long)need);
@@ -167,7 +198,10 @@ extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, i
   const int64_t qld = (int64_t)Hq * D;
   // The three operand preparations are independent: K and V run on side streams
   // forked from and joined back to the caller's stream (capturable in a CUDA graph),
-  // so the latency-bound K and V kernels overlap the Q quantization.
+  // so the latency-bound K and V kernels overlap the Q quantization.  The Q/K/V
+  // quantization always covers every head of the batch rows: the per-token global
+  // scales span the whole [B*T, H*D] row (llama_patch.py:167-196), whatever heads
+  // this call attends.
   SideStreams* side = side_streams();
   void* k_stream = stream;
   void* v_stream = stream;
@@ -180,6 +214,7 @@ extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, i
     cudaGetLastError();
     side = nullptr;
   }
+  SideJoin joiner{side, st};
   if (int e = fp4q_quantize(k, in_dtype, B, T, Hkv, D, k_sB, k_sT, k_sH, Tp, 1, 0, 1536.0f, kc,
                             (int64_t)Hkv * D / 2, ks, 1, (int64_t)Hkv * D / 64, gk, nullptr, 0, 0, k_stream))
     return e;
@@ -209,14 +244,20 @@ extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, i
         return e;
     }
   }
-  if (side) {
-    if (cudaEventRecord(side->join[0], side->s[0]) != cudaSuccess ||
-        cudaEventRecord(side->join[1], side->s[1]) != cudaSuccess ||
-        cudaStreamWaitEvent(st, side->join[0], 0) != cudaSuccess || cudaStreamWaitEvent(st, side->join[1], 0) != cudaSuccess)
-      return set_error(FP4ATTN_ERR_CUDA, "stream join: %s", cudaGetErrorString(cudaGetLastError()));
-  }
-  return fp4attn_fwd_packed_dual(qc, qs, gq, qc_lo, qs_lo, gq_lo, kc, ks, gk, vhi, vlo, out, B, Hq, Hkv, T, Tp, D,
-                                 causal, scaling, flags & (FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16), 0, stream);
+  if (int e = joiner.join()) return e;
+  AttnLaunch L{qc,    qs,   gq,   qc_lo, qs_lo, gq_lo, kc,   ks,   gk,     vhi,    vlo,
+               out,   B,    Hq,   Hkv,   T,     Tp,    D,    hkv0, hkv1,   causal, scaling,
+               flags & (FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16), 0};
+  return launch_attention(L, st);
+}
+
+extern "C" int fp4attn_forward_ex(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv,
+                                  int T, int D, int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH,
+                                  int64_t k_sT, int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling,
+                                  int flags, void* out, void* workspace, int64_t workspace_bytes, void* stream) {
+  return fp4attn_forward_heads(q, k, v, in_dtype, B, Hq, Hkv, T, D, q_sB, q_sH, q_sT, k_sB, k_sH, k_sT, v_sB, v_sH,
+                               v_sT, causal, scaling, flags, 0, Hkv > 0 ? Hkv : 1, out, workspace, workspace_bytes,
+                               stream);
 }
 
 extern "C" int fp4attn_forward(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv,

@@ -7,7 +7,11 @@
 // memory pressure mid-request).  The workspace is a file-scope __device__
 // array of kNoAllocWorkspaceBytes; its address is looked up once per device
 // (cudaGetSymbolAddress) on the first call made with that device current, so
-// make that first call before any stream capture.
+// make that first call before any stream capture.  Every later call whose
+// stream is not capturing looks the address up again: a device reset
+// (cudaDeviceReset, or a reset of the primary context) reloads the module and
+// the array can move, so only a call made during a capture uses the address
+// the last call outside one found.
 //
 // Every call shares the one array: calls whose GPU work overlaps (different
 // streams without ordering between them) race on it and corrupt each other's
@@ -55,7 +59,17 @@ extern "C" int fp4attn_forward_noalloc(const void* q, const void* k, const void*
   if (cudaGetDevice(&dev) != cudaSuccess) return set_error(FP4ATTN_ERR_CUDA, "cudaGetDevice failed");
   if (dev < 0 || dev >= kMaxDevices) return set_error(FP4ATTN_ERR_UNSUPPORTED, "device index %d", dev);
   void* ws = g_ws_ptr[dev].load(std::memory_order_acquire);
-  if (!ws) {
+  // a stream whose capture state cannot be read is treated as capturing
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  bool capturing = false;
+  if (cudaStreamIsCapturing(reinterpret_cast<cudaStream_t>(stream), &cap) != cudaSuccess) {
+    cudaGetLastError();
+    capturing = true;
+  } else {
+    capturing = cap != cudaStreamCaptureStatusNone;
+  }
+  if (!ws || !capturing) {
+    ws = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&ws, g_noalloc_ws);
     if (e != cudaSuccess || !ws)
       return set_error(FP4ATTN_ERR_CUDA, "cudaGetSymbolAddress of the fixed workspace: %s", cudaGetErrorString(e));

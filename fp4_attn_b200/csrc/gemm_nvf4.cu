@@ -53,12 +53,17 @@ __global__ void __launch_bounds__(gemm::THREADS, 2)
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  // set by the MMA thread when a wait gave up: the accumulator is then partial and the
+  // epilogue stores nothing (the done commit is still issued, so no MMA is in flight
+  // when TMEM is released)
+  volatile uint32_t* mma_failed = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
   const int ksteps = p.K / BK;
 
   if (threadIdx.x == 0) {
+    *mma_failed = 0u;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -116,11 +121,15 @@ __global__ void __launch_bounds__(gemm::THREADS, 2)
       }
       tc_commit(&empty[s]);
     }
+    if (!ok) {
+      *mma_failed = 1u;
+      __threadfence_block();
+    }
     tc_commit(done);
   } else if (warp >= 2) {
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + (threadIdx.x & 31);
-    const bool ok = mbar_wait(done, 0, 0x103);
+    const bool ok = mbar_wait(done, 0, 0x103) && *mma_failed == 0u;
     tc_fence_after();
     if (ok) {
       const int m = m0 + row;
@@ -190,11 +199,7 @@ extern "C" int fp4_gemm_nvf4(const uint8_t* a_codes, const uint8_t* a_scales, co
   if (int e = make_codes_map(&ma, a_codes, M, K, lda)) return e;
   if (int e = make_codes_map(&mb, b_codes, N, K, ldb)) return e;
   GemmArgs p{a_scales, b_scales, a_g, b_g, c, M, N, K, ldc, K / 64};
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_nvf4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES);
-    attr_set = true;
-  }
+  if (int e = set_smem_attr((const void*)gemm_nvf4_kernel, gemm::SMEM_BYTES)) return e;
   dim3 grid((M + 127) / 128, (N + 127) / 128);
   gemm_nvf4_kernel<<<grid, gemm::THREADS, gemm::SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(ma, mb, p);
   return check_launch("gemm_nvf4_kernel");

@@ -357,12 +357,7 @@ extern "C" int fp4qkv_rope_quant(const void* x, const void* w, const void* cos, 
   QkvArgs a{reinterpret_cast<const __nv_bfloat16*>(cos), reinterpret_cast<const __nv_bfloat16*>(sin), codes, scales,
             g, M, K, H, H * HD / 64, hpc};
   const int csize = H / hpc;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(qkv_rope_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    cudaFuncSetAttribute(qkv_rope_quant_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    attr = true;
-  }
+  if (int e = set_smem_attr((const void*)qkv_rope_quant_kernel, SMEM_BYTES, true)) return e;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(M / BM), (unsigned)csize, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);

@@ -16,10 +16,16 @@ int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 // Count one kernel launch of this library (read by fp4attn_launch_count()).
 void count_launch();
+// Raise a kernel's dynamic shared memory limit to `bytes` (and allow non-portable
+// cluster sizes when asked) on the current device.  Function attributes belong to
+// each device's context, so this is done once per (kernel, device), under a lock;
+// returns a status.
+int set_smem_attr(const void* fn, int bytes, bool nonportable_cluster = false);
 // Device status words of the translation units with bounded waits.
 unsigned int gemm_status(bool reset);
 unsigned int attn_status(bool reset);
 unsigned int quant_status(bool reset);
 unsigned int decode_status(bool reset);
 unsigned int qkv_status(bool reset);
+unsigned int peak_status(bool reset);
 }  // namespace fp4

@@ -4,9 +4,13 @@ The path partitions with no exchange on the data path:
 
 * attention: a unit is one (batch, kv-head) pair -- the kv-head's K/V and
   the Hq/Hkv query heads of its GQA group.  Units are independent (softmax,
-  the P quantization and PV are per query row; the Q/K/V fake-quant of
-  llama_patch.py:167-196 runs on whole [B*T, H*D] views, so it is done per
-  batch row and every unit of that row reads the same quantized operands);
+  the P quantization and PV are per query row).  The Q/K/V fake-quant of
+  llama_patch.py:167-196 runs on whole [B*T, H*D] views: its per-token global
+  scales span every head of a batch row.  So a rank quantizes every head of
+  the batch rows its units touch (``shard_rows``) and attends only its own
+  KV heads (``fp4_attention_fwd(..., kv_heads=...)``); a row split over two
+  ranks is quantized by both, and every unit reads the operands the
+  unsharded job reads;
 * quantization: rows of the 2-D input.  Row, column and none global-scale
   modes need no exchange for row shards (a column shard would); tensor mode
   needs the tensor's max|x|, which each rank reduces locally and combines
@@ -49,6 +53,19 @@ def attention_shard(B: int, Hq: int, Hkv: int, world: int, rank: int) -> list[At
     units = attention_units(B, Hq, Hkv)
     s, e = balanced_range(len(units), world, rank)
     return units[s:e]
+
+
+def shard_rows(units: list[AttentionUnit]) -> tuple[range, tuple[int, int]]:
+    """The batch rows a shard's units touch and its KV-head range, for a shard that is a
+    (batch rows) x (KV heads) block, as attention_shard gives for 1, 2, 4 or 8 ranks of the
+    long-context prefill job.  Raises ValueError for a shard of another form."""
+    if not units:
+        raise ValueError("empty shard")
+    bs, hs = sorted({u.b for u in units}), sorted({u.hk for u in units})
+    if len(units) != len(bs) * len(hs) or bs != list(range(bs[0], bs[-1] + 1)) or \
+            hs != list(range(hs[0], hs[-1] + 1)):
+        raise ValueError("shard is not a (batch rows) x (KV heads) block")
+    return range(bs[0], bs[-1] + 1), (hs[0], hs[-1] + 1)
 
 
 def unit_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, u: AttentionUnit):

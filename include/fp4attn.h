@@ -178,6 +178,15 @@ int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, con
                             const uint16_t* v_lo, void* out, int B, int Hq, int Hkv, int T, int Tp, int D,
                             int causal, float scaling, int flags, int num_ctas, void* stream);
 
+/* fp4attn_fwd_packed_dual on operands holding Hq / Hkv heads, attending only
+ * KV heads [hkv0, hkv1) and their query groups; out [B, T, (hkv1 - hkv0) *
+ * Hq / Hkv, D].  The kernel step of fp4attn_forward_heads. */
+int fp4attn_fwd_packed_heads(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                             const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
+                             const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g, const uint16_t* v_hi,
+                             const uint16_t* v_lo, void* out, int B, int Hq, int Hkv, int T, int Tp, int D, int hkv0,
+                             int hkv1, int causal, float scaling, int flags, void* stream);
+
 /* Workspace of fp4attn_forward for a shape: writes the byte offsets of its
  * eight pieces -- Q codes, Q scale atoms, Q g, K codes, K scale atoms, K g,
  * V-hat hi plane, V-hat lo plane, each 256-byte aligned, laid out as steps 1
@@ -216,6 +225,18 @@ int fp4attn_forward_ex(const void* q, const void* k, const void* v, int in_dtype
                        int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling, int flags, void* out,
                        void* workspace, int64_t workspace_bytes, void* stream);
 
+/* fp4attn_forward_ex attending only KV heads [hkv0, hkv1) and their query
+ * groups: the shard of one rank when a job is split by (batch, KV head).  The
+ * Q/K/V fake-quant still runs on every head of the B batch rows given (the
+ * reference's per-token global scales span the whole [B*T, H*D] row,
+ * llama_patch.py:167-196), so the packed operands -- and therefore every
+ * attended head's output -- equal the unsharded call's bit for bit.  out is
+ * [B, T, (hkv1 - hkv0) * Hq / Hkv, D]; workspace as fp4attn_forward_ex. */
+int fp4attn_forward_heads(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv, int T,
+                          int D, int64_t q_sB, int64_t q_sH, int64_t q_sT, int64_t k_sB, int64_t k_sH, int64_t k_sT,
+                          int64_t v_sB, int64_t v_sH, int64_t v_sT, int causal, float scaling, int flags, int hkv0,
+                          int hkv1, void* out, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* fp4attn_forward without a caller workspace; allocates no device memory.
  * No counterpart in the reference.  For callers that cannot hand the library
  * device memory: a C/FFI binding without a device allocator of its own, or a
@@ -224,7 +245,10 @@ int fp4attn_forward_ex(const void* q, const void* k, const void* v, int in_dtype
  * fixed library-owned device array of 32 MiB (33554432 bytes); shapes whose
  * fp4attn_workspace_layout size exceeds it are rejected with
  * FP4ATTN_ERR_UNSUPPORTED.  The array's address is looked up on the first
- * call per device, so make that call before any stream capture.  All calls
+ * call per device, so make that call before any stream capture; later calls
+ * look it up again whenever `stream` is not capturing (a device reset
+ * reloads the library's device code, and the array can move), and a call
+ * made during a capture uses the address of the last call outside one.  All calls
  * share the array: calls whose GPU work overlaps race; issue them on one
  * stream or order them with events.  Nothing has to start zeroed. */
 int fp4attn_forward_noalloc(const void* q, const void* k, const void* v, int in_dtype, int B, int Hq, int Hkv, int T,
@@ -271,6 +295,14 @@ int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, const float*
                    const uint8_t* k_scales, const float* k_g, const uint8_t* v_codes, const uint8_t* v_scales,
                    const float* v_g, int B, int Hq, int Hkv, int D, int len, int Tmax, float scaling, float* out,
                    void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Measurement aid, no reference counterpart: one CTA per SM (num_ctas <= 0)
+ * issues `iters` pairs of back-to-back tcgen05.mma.kind::mxf4nvf4 (M=128,
+ * N=128, K=64 each) on fixed pseudo-random NVFP4 operands: the dense NVFP4
+ * tensor throughput the FP4 contractions are measured against.  FLOPs per
+ * launch = ctas * iters * 4194304; time the launch with events on `stream`.
+ * iters <= 2^20. */
+int fp4_mma_peak_run(int iters, int num_ctas, void* stream);
 
 /* Profiling aid: a non-NULL buf makes later fp4attn_fwd_packed calls record
  * an event timeline (SM clock cycles from clock64) of each CTA's first work unit into

@@ -375,7 +375,9 @@ class AttentionWorkload:
     name = "attention"
     metric = "NVFP4 attention forward TFLOP/s per B200, % of dense FP4 tensor peak"
     unit = "TFLOP/s"
-    dtype = "nvfp4 QK^T (tcgen05 mxf4nvf4) + fp16-exact Phat x Vhat (tcgen05 f16), fp32 accumulate"
+    dtype = ("nvfp4 QK^T (tcgen05 mxf4nvf4) + fp16 Phat (exact) x Vhat rounded once to fp16 (tcgen05 f16; exact "
+             "hi+lo Vhat for the first 128 queries), fp32 accumulate")
+    FLAGS = 4 | 8  # FP4ATTN_OUT_BF16 | FP4ATTN_PV_FP16
     B, Hq, Hkv, T, D = 1, 32, 8, 4096, 128
 
     def __init__(self, dev, cpu_only=False, rank=0, world=1):
@@ -417,17 +419,17 @@ class AttentionWorkload:
         _lib.call("fp4attn_forward_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], self.B,
                   self.Hq, self.Hkv, self.T, self.D, q.stride(0), q.stride(1), q.stride(2), k.stride(0),
                   k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), 1, self.D ** -0.5,
-                  self.A.OUT_BF16, self.out[i].data_ptr(), ws.ptr(), ws.nbytes, _lib.stream_of(q))
+                  self.FLAGS, self.out[i].data_ptr(), ws.ptr(), ws.nbytes, _lib.stream_of(q))
 
     def kernel(self, i):
-        """The attention kernel alone on the operands step(i) prepared."""
+        """The contraction kernels alone (row maxima, then attention) on the operands step(i) prepared."""
         from fp4_attn_b200 import _lib
         i %= self.nsets
         ws = self.ws[i]
-        _lib.call("fp4attn_fwd_packed_dual", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), None, None, None,
-                  ws.kc.data_ptr(), ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(),
-                  self.out[i].data_ptr(), self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, 1, self.D ** -0.5,
-                  self.A.OUT_BF16, 0, _lib.stream_of(self.sets[i][0]))
+        _lib.call("fp4attn_fwd_packed_heads", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), None, None,
+                  None, ws.kc.data_ptr(), ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(),
+                  ws.row_max.data_ptr(), self.out[i].data_ptr(), self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D,
+                  0, self.Hkv, 1, self.D ** -0.5, self.FLAGS, _lib.stream_of(self.sets[i][0]))
 
     def e2e_step(self, i):
         """Public API, host buffers: H2D q/k/v, fp4_attention_fwd (bf16 out, the reference's output
@@ -442,7 +444,8 @@ class AttentionWorkload:
                 d.copy_(h, non_blocking=True)
 
         self.pipe.step(i, h2d, lambda: self.A.fp4_attention_fwd(q, k, v, causal=True, workspace=self.ws[i],
-                                                                 out=self.out_bf16[i], out_dtype=torch.bfloat16),
+                                                                 out=self.out_bf16[i], out_dtype=torch.bfloat16,
+                                                                 pv_fp16=True),
                        lambda o: self.out_host.copy_(o, non_blocking=True))
 
     e2e_h2d = property(lambda self: sum(t.numel() * 2 for t in self.host))
@@ -454,7 +457,8 @@ class AttentionWorkload:
     def kernel_roofline(self, kernel_s, peaks, peak_src):
         achieved = self.flops / kernel_s / 1e12
         peak, src = fp4_peak(peaks, peak_src)
-        return {"bound": "tensor", "kernel": "fp4_attn_kernel", "achieved": round(achieved, 1), "peak": round(peak, 1),
+        return {"bound": "tensor", "kernel": "fp4_rowmax_kernel + fp4_attn_kernel", "achieved": round(achieved, 1),
+                "peak": round(peak, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": src,
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4),
                 "algorithmic_flops_per_launch": self.flops,
@@ -953,7 +957,7 @@ class PrefillWorkload(AttentionWorkload):
         _lib.call("fp4attn_forward_heads", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype],
                   self.B, self.Hq, self.Hkv, self.T, self.D, q.stride(0), q.stride(1), q.stride(2), k.stride(0),
                   k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), 1, self.D ** -0.5,
-                  self.A.OUT_BF16, self.h0, self.h1, self.out[i].data_ptr(), ws.ptr(), ws.nbytes,
+                  self.FLAGS, self.h0, self.h1, self.out[i].data_ptr(), ws.ptr(), ws.nbytes,
                   _lib.stream_of(q))
 
     def kernel(self, i):
@@ -963,8 +967,8 @@ class PrefillWorkload(AttentionWorkload):
         ws = self.ws[i]
         _lib.call("fp4attn_fwd_packed_heads", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), None, None,
                   None, ws.kc.data_ptr(), ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(),
-                  self.out[i].data_ptr(), self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D, self.h0, self.h1, 1,
-                  self.D ** -0.5, self.A.OUT_BF16, _lib.stream_of(self.sets[i][0]))
+                  ws.row_max.data_ptr(), self.out[i].data_ptr(), self.B, self.Hq, self.Hkv, self.T, ws.Tp, self.D,
+                  self.h0, self.h1, 1, self.D ** -0.5, self.FLAGS, _lib.stream_of(self.sets[i][0]))
 
     def e2e_step(self, i):
         """Public API, host buffers: H2D q/k/v of the rank's rows, fp4_attention_fwd on its KV heads
@@ -980,7 +984,7 @@ class PrefillWorkload(AttentionWorkload):
 
         self.pipe.step(i, h2d, lambda: self.A.fp4_attention_fwd(q, k, v, causal=True, workspace=self.ws[i],
                                                                  out=self.out_bf16[i], out_dtype=torch.bfloat16,
-                                                                 kv_heads=(self.h0, self.h1)),
+                                                                 kv_heads=(self.h0, self.h1), pv_fp16=True),
                        lambda o: self.out_host.copy_(o, non_blocking=True))
 
     def value(self, seconds_per_step, world):

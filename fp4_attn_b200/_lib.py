@@ -38,8 +38,8 @@ SIGNATURES = {
     "fp4attn_workspace_layout_ex": ([_I, _I, _I, _I, _I, _I, _P], _L),
     "fp4attn_fwd_packed_dual": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                                  _P], _I),
-    "fp4attn_fwd_packed_heads": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I,
-                                  _F, _I, _P], _I),
+    "fp4attn_fwd_packed_heads": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
+                                  _I, _F, _I, _P], _I),
     "fp4attn_decode_workspace_size": ([_I, _I, _I], _L),
     "fp4attn_decode": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _L, _P], _I),
     "fp4attn_forward": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _P, _P, _L,

@@ -20,7 +20,7 @@ import torch
 from . import _lib
 
 HEAD_DIM = 128
-DUAL_Q, DUAL_P, OUT_BF16 = 1, 2, 4  # fp4attn_forward_ex flags
+DUAL_Q, DUAL_P, OUT_BF16, PV_FP16 = 1, 2, 4, 8  # fp4attn_forward_ex flags
 
 
 class AttentionWorkspace:
@@ -28,7 +28,8 @@ class AttentionWorkspace:
 
     One device buffer laid out by fp4attn_workspace_layout, with a tensor
     view per piece: qc/kc codes [B*Tp, H*D/2], qs/ks tcgen05 scale atoms,
-    gq/gk per-token global scales [B*Tp], vhi/vlo V-hat planes [B*Hkv*D, Tp].
+    gq/gk per-token global scales [B*Tp], vhi/vlo V-hat planes [B*Hkv*D, Tp],
+    row_max the row maxima of the scores [B, Hq, Tp] (single-slice Q).
     """
 
     def __init__(self, B, Hq, Hkv, T, D, device, dual_q: bool = False):
@@ -38,7 +39,7 @@ class AttentionWorkspace:
         self.flags = DUAL_Q if dual_q else 0
         self.Tp = (T + 127) // 128 * 128
         Tp = self.Tp
-        offs = (ctypes.c_int64 * 12)()
+        offs = (ctypes.c_int64 * 13)()
         size = _lib.load().fp4attn_workspace_layout_ex(B, Hq, Hkv, T, D, self.flags, offs)
         if size < 0:
             raise ValueError(f"unsupported attention shape B={B} Hq={Hq} Hkv={Hkv} T={T} D={D}")
@@ -68,6 +69,9 @@ class AttentionWorkspace:
             self.qc_lo = view(8, u8, (B * Tp, Hq * D // 2))
             self.qs_lo = view(9, u8, (B * Tp // 128 * Hq * (D // 64) * 512,))
             self.gq_lo = view(10, f32, (B * Tp,))
+            self.row_max = None
+        else:  # row maxima of the scores, written by the row-maximum kernel (piece 12)
+            self.row_max = view(12, f32, (B, Hq, Tp))
 
     def ptr(self) -> int:
         return self.buf.data_ptr() + self.base
@@ -101,7 +105,7 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
                       workspace: AttentionWorkspace | None = None, num_ctas: int = 0,
                       dual_q: bool = False, dual_p: bool = False,
                       out_dtype: torch.dtype = torch.float32,
-                      kv_heads: tuple[int, int] | None = None) -> torch.Tensor:
+                      kv_heads: tuple[int, int] | None = None, pv_fp16: bool = False) -> torch.Tensor:
     """NVFP4 attention forward.  q [B,Hq,T,D], k/v [B,Hkv,T,D] (CUDA) -> [B,T,Hq,D] in out_dtype.
 
     kv_heads=(h0, h1) attends only KV heads h0..h1-1 and their query groups
@@ -113,6 +117,12 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
 
     out_dtype fp32 or bf16 (the reference's output dtype for bf16 inputs,
     llama_patch.py:102-103: the kernel rounds its fp32 result once).
+
+    pv_fp16=True (FP4ATTN_PV_FP16) multiplies P-hat by V-hat rounded once to
+    fp16 for every query past the first 128 of a sequence, half the PV tensor
+    work; the first 128 queries, whose outputs average few keys, keep the exact
+    hi + lo planes.  Measured against the exact V-hat: max-abs 2.7e-3 x RMS(O)
+    on the Llama-3-8B shape, inside the attention tolerance.
 
     One call of the C ABI's fp4attn_forward_ex (quantize Q/K, prepare V-hat,
     attention) with the packed operands in ``workspace``.  dual_q / dual_p
@@ -160,7 +170,8 @@ def fp4_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal:
                   ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(), out.data_ptr(), B, Hq,
                   Hkv, T, ws.Tp, D, 1 if causal else 0, float(scaling), int(num_ctas), _lib.stream_of(q))
         return out
-    flags = (DUAL_Q if dual_q else 0) | (DUAL_P if dual_p else 0) | (OUT_BF16 if out_dtype == torch.bfloat16 else 0)
+    flags = (DUAL_Q if dual_q else 0) | (DUAL_P if dual_p else 0) | \
+        (OUT_BF16 if out_dtype == torch.bfloat16 else 0) | (PV_FP16 if pv_fp16 else 0)
     _lib.call("fp4attn_forward_heads", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.DTYPE_CODE[q.dtype], B, Hq,
               Hkv, T, D, q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0),
               v.stride(1), v.stride(2), 1 if causal else 0, float(scaling), flags, h0, h1, out.data_ptr(), ws.ptr(),

@@ -70,7 +70,9 @@ constexpr int V_STAGE = 4 * V_HALF;  // keys 0-63 hi, lo; keys 64-127 hi, lo
 constexpr int OFF_V = OFF_K + NK * K_STAGE;
 constexpr int OFF_STAT = OFF_V + NV * V_STAGE;  // m[NWG][128], l[NWG][128], residual max[NWG][128]
 constexpr int OFF_RCP = OFF_STAT + 3 * NWG * 128 * 4;
-constexpr int OFF_BAR = OFF_RCP + 128 * 4;
+constexpr int OFF_PTAB = OFF_RCP + 128 * 4;  // per E4M3 scale byte: (1/s, s as an fp16 pair)
+constexpr int OFF_MROW = OFF_PTAB + 128 * 8;  // the unit's 128 row maxima (PRE), loaded with Q
+constexpr int OFF_BAR = OFF_MROW + 128 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 // TMEM columns: S0, S1, O, P (fp16, single-buffered; warpgroup q writes columns
@@ -95,7 +97,14 @@ struct AttnArgs {
   // The packed operands may hold more heads than are attended (a rank of a sharded job
   // quantizes whole batch rows): the attended heads start at head hq0 / hk0 of operands
   // with nkb4q / nkb4k scale atoms per 128-row block (2 per head) and HkvT KV heads.
-  int hq0, hk0, nkb4q, nkb4k, HkvT;
+  int hq0, hk0, nkb4q, nkb4k, HkvT, HqT;
+  // Row maxima of z = (Q K^T) * gk per (batch, query head of the operands, row):
+  // [B][HqT][Tp] fp32, written by fp4_rowmax_kernel and read by the attention kernel
+  // instantiated with PRE (which then has no max pass of its own).
+  float* row_max;
+  // PV uses V-hat's lo plane only for query tiles qt < pv_lo_tiles (the hi plane is
+  // V-hat rounded once to fp16); a large value keeps PV exact everywhere.
+  int pv_lo_tiles;
   int causal;
   float scale_log2;  // scaling * log2(e)
   int units;
@@ -159,14 +168,20 @@ __device__ __forceinline__ int kv_tiles(const Unit& un, const AttnArgs& p) {
 // has no trace code at all.  DQ: dual-slice Q (a second, residual Q slice;
 // both QK products of a key tile go to the two S accumulators and combine per
 // row).  DP: dual-slice P (a residual pass between the max pass and the PV
-// pass finds each row's residual scale; the PV pass writes hi + lo).
-template <bool TRACE, bool DQ, bool DP>
+// pass finds each row's residual scale; the PV pass writes hi + lo).  PRE: the
+// row maxima come from fp4_rowmax_kernel (p.row_max, loaded with Q), so the
+// kernel has no max pass and reads each K tile once (single-slice Q only).
+template <bool TRACE, bool DQ, bool DP, bool PRE>
 __global__ void __launch_bounds__(attn::THREADS, 1)
     fp4_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmQlo,
                     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmVhi,
                     const __grid_constant__ CUtensorMap tmVlo, AttnArgs p) {
   using namespace attn;
-  constexpr int NPASS = DP ? 3 : 2;  // QK passes per unit; the last one feeds PV
+  static_assert(!(PRE && DQ), "precomputed row maxima are for single-slice Q");
+  constexpr int NPASS = (DP ? 3 : 2) - (PRE ? 1 : 0);  // QK passes per unit; the last one feeds PV
+  // With a single pass the PV thread releases each K stage for the softmax warps: it
+  // waits for all of them to finish P (after their last read of the stage's gk) anyway.
+  constexpr bool PV_RELEASES_K = NPASS == 1;
   auto tr = [&](uint32_t uc, int slot, int j) {
     if constexpr (TRACE) trace(p, uc, slot, j);
   };
@@ -176,6 +191,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   float* stat_l = stat_m + NWG * 128;
   float* stat_r = stat_m + 2 * NWG * 128;
   float* rcp = reinterpret_cast<float*>(sm + OFF_RCP);
+  uint2* ptab = reinterpret_cast<uint2*>(sm + OFF_PTAB);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bar + 0;
   uint64_t* q_empty = bar + 1;
@@ -198,10 +214,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    mbar_init(q_empty, 1 + 4 * NWG);  // MMA commit + every softmax warp (they read g and m)
     for (int i = 0; i < NK; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1 + 4 * NWG);  // MMA commit + every softmax warp (they read gk)
+      // MMA commit + every softmax warp (they read gk), or + the PV thread for them
+      mbar_init(&k_empty[i], PV_RELEASES_K ? 2 : 1 + 4 * NWG);
     }
     for (int i = 0; i < NV; ++i) {
       mbar_init(&v_full[i], 1);
@@ -221,6 +238,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     // correctly rounded 1/s for every non-negative E4M3 scale byte (0 -> 0, get_reciprocal)
     const float s = e4m3_to_f32((uint8_t)threadIdx.x);
     rcp[threadIdx.x] = s == 0.0f ? 0.0f : __frcp_rn(s);
+    ptab[threadIdx.x] = make_uint2(__float_as_uint(rcp[threadIdx.x]), e4m3_f16x2((uint32_t)threadIdx.x));
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -245,8 +263,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const int hq = p.hq0 + un.h, hk = p.hk0 + un.h / group;  // heads within the operands
         const int qrow = un.b * p.Tp + un.qt * BM;
         if (uc > 0) mbar_wait(q_empty, (uc - 1) & 1, 0x201);
-        mbar_arrive_expect_tx(q_full, (DQ ? 2 : 1) * (Q_BYTES + 1024 + 512));
+        mbar_arrive_expect_tx(q_full, (DQ ? 2 : 1) * (Q_BYTES + 1024 + 512) + (PRE ? 512 : 0));
         tma_load_2d(sm + OFF_Q, &tmQ, q_full, hq * (HD / 2), qrow);
+        if constexpr (PRE)
+          bulk_load(sm + OFF_MROW, p.row_max + ((int64_t)un.b * p.HqT + hq) * p.Tp + un.qt * BM, 512, q_full);
         bulk_load(sm + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * nkb4q + 2 * hq) * 512, 1024, q_full);
         bulk_load(sm + OFF_GQ, p.gq + qrow, 512, q_full);
         if constexpr (DQ) {
@@ -282,11 +302,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           const int vs = vc % NV;
           if (vc >= NV) mbar_wait(&v_empty[vs], ((vc / NV) - 1) & 1, 0x203);
           uint8_t* v = sm + OFF_V + vs * V_STAGE;
-          mbar_arrive_expect_tx(&v_full[vs], V_STAGE);
+          const bool lo = un.qt < p.pv_lo_tiles;  // the lo plane only where PV reads it
+          mbar_arrive_expect_tx(&v_full[vs], lo ? V_STAGE : V_STAGE / 2);
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             tma_load_2d(v + 2 * half * V_HALF, &tmVhi, &v_full[vs], j * BN + 64 * half, vrow);
-            tma_load_2d(v + (2 * half + 1) * V_HALF, &tmVlo, &v_full[vs], j * BN + 64 * half, vrow);
+            if (lo) tma_load_2d(v + (2 * half + 1) * V_HALF, &tmVlo, &v_full[vs], j * BN + 64 * half, vrow);
           }
         }
       }
@@ -361,12 +382,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
+        const int parts = un.qt < p.pv_lo_tiles ? 2 : 1;  // hi + lo planes, or hi alone
         for (int j = 0; j < n; ++j, ++vc) {
           const int vs = vc % NV;
           mbar_wait(&v_full[vs], (vc / NV) & 1, 0x215);
           tr(uc, TR_PWAIT, j);
           mbar_wait(p_full, pu & 1, 0x214);
           ++pu;
+          if constexpr (PV_RELEASES_K) mbar_arrive(&k_empty[vc % NK]);
           if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
           tc_fence_after();
           tr(uc, TR_PV, j);
@@ -374,8 +397,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {  // keys 16kk .. 16kk+15
             const uint32_t a = tmem + T_P + 8 * kk;  // fp16 P of keys 16kk..16kk+15
-#pragma unroll
-            for (int part = 0; part < 2; ++part) {  // hi, lo planes
+            for (int part = 0; part < parts; ++part) {  // hi, lo planes
               const uint32_t vb = v + ((kk >> 2) * 2 + part) * V_HALF + (kk & 3) * 32;
               mma_f16_ts(tmem + T_O, a, smem_desc(vb, 16, 1024, kSwizzle128B), idv, (j > 0 || kk > 0 || part > 0) ? 1u : 0u);
             }
@@ -456,6 +478,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         ratio = ghi == 0.0f ? 0.0f : __fdiv_rn(glo, ghi);
       }
       const uint64_t ratio2 = pk2(ratio, ratio);
+      float m = -INFINITY;
+      if constexpr (PRE) m = reinterpret_cast<const float*>(sm + OFF_MROW)[r];
+      // g (and m) are in registers: this warp no longer needs the unit's Q buffer
+      __syncwarp();
+      if (wlead) mbar_arrive(q_empty);
       auto load_s = [&](int kb, uint32_t(&a)[32]) {
         tmem_ld32(tmem + lane_base + T_S + 128 * kb + col0, a);
         if constexpr (DQ) {
@@ -479,7 +506,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         }
       };
       // ---- pass 1: row maximum of z = acc * gk over this quarter's keys
-      float m = -INFINITY;
+      if constexpr (!PRE) {
       for (int j = 0; j < n; ++j, ++kc) {
         const int kb = DQ ? 0 : (j & 1), s = kc % NK;
         mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x222);
@@ -506,9 +533,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       named_bar(1 + NWG, NWG * 128);
 #pragma unroll
       for (int w = 0; w < NWG; ++w) m = fmaxf(m, stat_m[w * 128 + r]);
-      // the previous unit's last PV has long finished: write its O now, which
-      // also frees the accumulator for this unit's first PV
-      if (pend) epilogue();
+      }
       const float mu = m == -INFINITY ? 0.0f : m * uscale;
       const uint64_t u2 = pk2(uscale, uscale), nmu2 = pk2(-mu, -mu);
       // ---- dual-slice P: residual pass, row max of |e - hi| over this quarter's keys
@@ -563,10 +588,13 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           if (lim < col0 + 31) chunk_p_dual<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, rg, gr, lsum2, pk);
           else chunk_p_dual<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, rg, gr, lsum2, pk);
         } else {
-          if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
-          else chunk_p<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, lsum2, pk);
+          if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, ptab, r6, lsum2, pk);
+          else chunk_p<false>(a, gk, col0, lim, u2, nmu2, ptab, r6, lsum2, pk);
         }
         if (leader && q == 0) tr(uc, TR_COMP, j);
+        // the previous unit's O is written while its last PV finishes, after this unit's
+        // first P is computed; that also frees the accumulator for this unit's first PV
+        if (j == 0 && pend) epilogue();
         // the previous tile's PV must have read P before quarter q is overwritten
         if (pt > 0) mbar_wait(p_free, (pt - 1) & 1, 0x225);
         ++pt;
@@ -577,7 +605,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         __syncwarp();
         if (wlead) {
           mbar_arrive(p_full);
-          mbar_arrive(&k_empty[s]);
+          if constexpr (!PV_RELEASES_K) mbar_arrive(&k_empty[s]);
         }
         if (leader && q == 0) tr(uc, TR_PDONE, j);
         if (leader && q == 3) tr(uc, TR_PDONE3, j);
@@ -596,6 +624,184 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       pend_off = qpos < p.T ? (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + col0 : -1;
     }
     if (pend) epilogue();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ------------------------------------------------------------ row maxima
+// fp4_rowmax_kernel: the exact row maximum of z = (Q K^T) * gk for every query
+// row of every unit, written to p.row_max; the attention kernel's PRE
+// instantiation reads it instead of running its own max pass.  The scores are
+// the same tcgen05 kind::mxf4nvf4 products of the same operands with the same
+// instruction shape (M=128, N=128, K=64), and z is formed and reduced by the
+// same chunk_max, so the maxima are bit for bit the ones the two-pass kernel
+// finds.  The kernel does nothing else, so three S buffers rotate in TMEM and
+// the QK^T of the next tiles overlaps the reduction of the current one.  As in
+// the attention kernel, a wait that gives up records its site and returns, and
+// every thread carries on through the same barriers, so the kernel ends.
+namespace rmx {
+constexpr int NS = 3;   // S buffers (and K scale-atom slots, one per buffer)
+constexpr int NK = 8;   // K stages: enough copies in flight to cover their latency at this kernel's pace
+constexpr int NWG = 4;  // max warpgroups; warpgroup q owns key columns 32q .. 32q+31
+constexpr int THREADS = 128 + NWG * 128;
+constexpr int Q_STAGE = 10240;  // Q codes 8 KB + scale atoms 1 KB; two stages (the next unit's Q lands early)
+constexpr int OFF_Q = 0, OFF_QSF = 8192;
+constexpr int K_STAGE = 10240;  // codes 8 KB, scale atoms 1 KB, gk 512 B
+constexpr int OFF_K = 2 * Q_STAGE;
+constexpr int OFF_STAT = OFF_K + NK * K_STAGE;     // [2][NWG][128] partial maxima
+constexpr int OFF_BAR = OFF_STAT + 2 * NWG * 128 * 4;
+// 116 KB: more than half of an SM's shared memory, so one CTA per SM (each
+// holds all 512 TMEM columns)
+constexpr int SMEM_BYTES = 116 * 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t T_SFA = NS * 128, T_SFB = T_SFA + 16;  // Q scale atoms per Q stage, K per S buffer
+static_assert(T_SFB + 8 * NS <= TMEM_COLS, "TMEM columns");
+static_assert(OFF_BAR + 256 + 1024 <= SMEM_BYTES, "shared memory map");
+}  // namespace rmx
+
+__global__ void __launch_bounds__(rmx::THREADS, 1)
+    fp4_rowmax_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, AttnArgs p) {
+  using namespace rmx;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* stat = reinterpret_cast<float*>(sm + OFF_STAT);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* q_full = bar + 0;        // [2]
+  uint64_t* q_empty = bar + 2;       // [2]
+  uint64_t* k_full = bar + 4;        // [NK]
+  uint64_t* k_empty = k_full + NK;   // [NK]
+  uint64_t* s_full = k_empty + NK;   // [NS]
+  uint64_t* s_free = s_full + NS;    // [NS]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + NS);
+  static_assert(4 + 2 * NK + 2 * NS + 1 <= 32, "barriers exceed their 256-byte slot");
+  const int warp = threadIdx.x / 32;
+  const int group = p.Hq / p.Hkv;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < NK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1 + 4 * NWG);  // MMA commit + every max warp (they read gk)
+    }
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4 * NWG);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {
+    if (elect_one_lane()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      uint32_t kc = 0, uc = 0;
+      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
+        const Unit un = unit_of(u, p);
+        const int n = kv_tiles(un, p);
+        const int hq = p.hq0 + un.h, hk = p.hk0 + un.h / group;
+        const int qrow = un.b * p.Tp + un.qt * attn::BM;
+        const int qb = uc & 1;
+        uint8_t* qs = sm + OFF_Q + qb * Q_STAGE;
+        if (uc >= 2) mbar_wait(&q_empty[qb], ((uc >> 1) - 1) & 1, 0x501);
+        mbar_arrive_expect_tx(&q_full[qb], attn::Q_BYTES + 1024);
+        tma_load_2d(qs, &tmQ, &q_full[qb], hq * (attn::HD / 2), qrow);
+        bulk_load(qs + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * p.nkb4q + 2 * hq) * 512, 1024, &q_full[qb]);
+        for (int j = 0; j < n; ++j, ++kc) {
+          const int s = kc % NK;
+          if (kc >= NK) mbar_wait(&k_empty[s], ((kc / NK) - 1) & 1, 0x502);
+          uint8_t* ks = sm + OFF_K + s * K_STAGE;
+          const int krow = un.b * p.Tp + j * attn::BN;
+          mbar_arrive_expect_tx(&k_full[s], 8192 + 1024 + 512);
+          tma_load_2d(ks, &tmK, &k_full[s], hk * (attn::HD / 2), krow);
+          bulk_load(ks + 8192, p.ksf + ((int64_t)(krow / 128) * p.nkb4k + 2 * hk) * 512, 1024, &k_full[s]);
+          bulk_load(ks + 9216, p.gk + krow, 512, &k_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one_lane()) {
+      const uint32_t idq = idesc_nvf4(attn::BM, attn::BN);
+      uint32_t kc = 0, uc = 0, tc = 0;
+      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
+        const Unit un = unit_of(u, p);
+        const int n = kv_tiles(un, p);
+        const int qb = uc & 1;
+        uint8_t* qs = sm + OFF_Q + qb * Q_STAGE;
+        const uint32_t sfa = tmem + T_SFA + 8 * qb;
+        mbar_wait(&q_full[qb], (uc >> 1) & 1, 0x503);
+        tc_fence_after();
+        tmem_cp_sf_atom(sfa, smem_desc(smem_u32(qs + OFF_QSF), 16, 128, kSwizzleNone));
+        tmem_cp_sf_atom(sfa + 4, smem_desc(smem_u32(qs + OFF_QSF + 512), 16, 128, kSwizzleNone));
+        for (int j = 0; j < n; ++j, ++kc, ++tc) {
+          const int b = tc % NS, s = kc % NK;
+          if (tc >= NS) mbar_wait(&s_free[b], ((tc / NS) - 1) & 1, 0x504);
+          mbar_wait(&k_full[s], (kc / NK) & 1, 0x505);
+          tc_fence_after();
+          uint8_t* ks = sm + OFF_K + s * K_STAGE;
+          const uint32_t sfb = tmem + T_SFB + 8 * b;
+          tmem_cp_sf_atom(sfb, smem_desc(smem_u32(ks + 8192), 16, 128, kSwizzleNone));
+          tmem_cp_sf_atom(sfb + 4, smem_desc(smem_u32(ks + 8192 + 512), 16, 128, kSwizzleNone));
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint64_t ad = smem_desc(smem_u32(qs) + kk * 32, 16, 512, kSwizzle64B);
+            const uint64_t bd = smem_desc(smem_u32(ks) + kk * 32, 16, 512, kSwizzle64B);
+            mma_nvf4(tmem + 128 * b, ad, bd, idq, sfa + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&k_empty[s]);
+          tc_commit(&s_full[b]);
+        }
+        tc_commit(&q_empty[qb]);
+      }
+    }
+  } else if (warp >= 4) {
+    const int q = (warp - 4) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + (threadIdx.x & 31);
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const bool wlead = (threadIdx.x & 31) == 0;
+    const int col0 = 32 * q;
+    uint32_t kc = 0, uc = 0, tc = 0;
+    for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
+      const Unit un = unit_of(u, p);
+      const int n = kv_tiles(un, p);
+      float m = -INFINITY;
+      for (int j = 0; j < n; ++j, ++kc, ++tc) {
+        const int b = tc % NS, s = kc % NK;
+        mbar_wait(&s_full[b], (tc / NS) & 1, 0x506);
+        tc_fence_after();
+        uint32_t a[32];
+        tmem_ld32(tmem + lane_base + 128 * b + col0, a);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (wlead) mbar_arrive(&s_free[b]);
+        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
+        const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * attn::BN);
+        if (lim < col0 + 31) m = chunk_max<true>(a, gk, col0, lim, m);
+        else m = chunk_max<false>(a, gk, col0, lim, m);
+        __syncwarp();
+        if (wlead) mbar_arrive(&k_empty[s]);
+      }
+      float* st = stat + (uc & 1) * NWG * 128;
+      st[q * 128 + r] = m;
+      named_bar(1, NWG * 128);
+      if (q == 0) {
+#pragma unroll
+        for (int w = 1; w < NWG; ++w) m = fmaxf(m, st[w * 128 + r]);
+        p.row_max[((int64_t)un.b * p.HqT + p.hq0 + un.h) * p.Tp + un.qt * attn::BM + r] = m;
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -930,12 +1136,12 @@ int fp4::launch_attention(const AttnLaunch& L, cudaStream_t st) {
   if (!L.q_codes || !L.q_scales || !L.q_g || !L.k_codes || !L.k_scales || !L.k_g || !L.v_hi || !L.v_lo || !L.out)
     return set_error(FP4ATTN_ERR_ARG, "null pointer");
   const bool dq = L.q_codes_lo != nullptr;
-  if (L.flags & ~(FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16)) return set_error(FP4ATTN_ERR_ARG, "bad flags");
+  if (L.flags & ~(FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16 | FP4ATTN_PV_FP16)) return set_error(FP4ATTN_ERR_ARG, "bad flags");
   const bool dual_p = (L.flags & FP4ATTN_DUAL_P) != 0;
   if (dq && (!L.q_scales_lo || !L.q_g_lo)) return set_error(FP4ATTN_ERR_ARG, "null pointer (residual Q slice)");
   if (((uintptr_t)L.q_codes | (uintptr_t)L.k_codes | (uintptr_t)L.v_hi | (uintptr_t)L.v_lo | (uintptr_t)L.q_scales |
        (uintptr_t)L.k_scales | (uintptr_t)L.q_g | (uintptr_t)L.k_g | (uintptr_t)L.out | (uintptr_t)L.q_codes_lo |
-       (uintptr_t)L.q_scales_lo | (uintptr_t)L.q_g_lo) % 16)
+       (uintptr_t)L.q_scales_lo | (uintptr_t)L.q_g_lo | (uintptr_t)L.row_max) % 16)
     return set_error(FP4ATTN_ERR_ARG, "buffers must be 16-byte aligned");
   const int G = HqT / HkvT;
   CUtensorMap mq, mql, mk, mvh, mvl;
@@ -977,23 +1183,37 @@ int fp4::launch_attention(const AttnLaunch& L, cudaStream_t st) {
   a.nkb4q = 2 * HqT;
   a.nkb4k = 2 * HkvT;
   a.HkvT = HkvT;
+  a.HqT = HqT;
+  a.pv_lo_tiles = (L.flags & FP4ATTN_PV_FP16) ? 1 : 0x7FFFFFFF;
+  // precomputed row maxima: single-slice Q with a scratch for them (the traced kernel keeps its max pass)
+  const bool pre = L.row_max != nullptr && !dq;
+  a.row_max = pre ? L.row_max : nullptr;
   a.causal = L.causal ? 1 : 0;
   a.scale_log2 = L.scaling * 1.4426950408889634f;
   a.units = B * a.Hq * (Tp / 128);
   // the event timeline is recorded by the single-slice kernel only
+  // the event timeline is recorded by the single-slice kernel only
   a.trace = (dq || dual_p) ? nullptr : g_trace;
   using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                         AttnArgs);
-  static const Kern kerns[5] = {fp4_attn_kernel<false, false, false>, fp4_attn_kernel<false, true, false>,
-                                fp4_attn_kernel<false, false, true>, fp4_attn_kernel<false, true, true>,
-                                fp4_attn_kernel<true, false, false>};
-  const Kern kern = a.trace ? kerns[4] : kerns[(dq ? 1 : 0) + (dual_p ? 2 : 0)];
+  static const Kern kerns[8] = {fp4_attn_kernel<false, false, false, false>, fp4_attn_kernel<false, true, false, false>,
+                                fp4_attn_kernel<false, false, true, false>,  fp4_attn_kernel<false, true, true, false>,
+                                fp4_attn_kernel<false, false, false, true>,  fp4_attn_kernel<false, false, true, true>,
+                                fp4_attn_kernel<true, false, false, false>,  fp4_attn_kernel<true, false, false, true>};
+  const Kern kern = a.trace ? kerns[6 + (pre ? 1 : 0)]
+                    : pre   ? kerns[4 + (dual_p ? 1 : 0)]
+                            : kerns[(dq ? 1 : 0) + (dual_p ? 2 : 0)];
   if (int e = set_smem_attr((const void*)kern, SMEM_BYTES)) return e;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int grid = L.num_ctas > 0 ? L.num_ctas : sms;
   if (grid > a.units) grid = a.units;
+  if (pre) {
+    if (int e = set_smem_attr((const void*)fp4_rowmax_kernel, rmx::SMEM_BYTES)) return e;
+    fp4_rowmax_kernel<<<grid, rmx::THREADS, rmx::SMEM_BYTES, st>>>(mq, mk, a);
+    if (int e = check_launch("fp4_rowmax_kernel")) return e;
+  }
   kern<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mql, mk, mvh, mvl, a);
   return check_launch("fp4_attn_kernel");
 }
@@ -1005,22 +1225,22 @@ extern "C" int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_
                                        int Hkv, int T, int Tp, int D, int causal, float scaling, int flags,
                                        int num_ctas, void* stream) {
   clear_error();
-  AttnLaunch L{q_codes, q_scales, q_g,  q_codes_lo, q_scales_lo, q_g_lo, k_codes, k_scales, k_g,     v_hi,
-               v_lo,    out,      B,    Hq,         Hkv,         T,      Tp,      D,        0,       Hkv,
-               causal,  scaling,  flags, num_ctas};
+  AttnLaunch L{q_codes, q_scales, q_g, q_codes_lo, q_scales_lo, q_g_lo, k_codes, k_scales, k_g, v_hi, v_lo,
+               out,     nullptr,  B,   Hq,         Hkv,         T,      Tp,      D,        0,   Hkv,  causal,
+               scaling, flags,    num_ctas};
   return launch_attention(L, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fp4attn_fwd_packed_heads(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
                                         const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
                                         const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
-                                        const uint16_t* v_hi, const uint16_t* v_lo, void* out, int B, int Hq,
-                                        int Hkv, int T, int Tp, int D, int hkv0, int hkv1, int causal, float scaling,
-                                        int flags, void* stream) {
+                                        const uint16_t* v_hi, const uint16_t* v_lo, float* row_max, void* out,
+                                        int B, int Hq, int Hkv, int T, int Tp, int D, int hkv0, int hkv1, int causal,
+                                        float scaling, int flags, void* stream) {
   clear_error();
-  AttnLaunch L{q_codes, q_scales, q_g,  q_codes_lo, q_scales_lo, q_g_lo, k_codes, k_scales, k_g,    v_hi,
-               v_lo,    out,      B,    Hq,         Hkv,         T,      Tp,      D,        hkv0,   hkv1,
-               causal,  scaling,  flags, 0};
+  AttnLaunch L{q_codes, q_scales, q_g, q_codes_lo, q_scales_lo, q_g_lo, k_codes, k_scales, k_g,  v_hi, v_lo,
+               out,     row_max,  B,   Hq,         Hkv,         T,      Tp,      D,        hkv0, hkv1, causal,
+               scaling, flags,    0};
   return launch_attention(L, reinterpret_cast<cudaStream_t>(stream));
 }
 

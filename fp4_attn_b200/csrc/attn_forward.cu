@@ -21,17 +21,18 @@
 namespace {
 
 constexpr int64_t kAlign = 256;
-constexpr int kPieces = 12;
+constexpr int kPieces = 13;
 
 int64_t align_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
-// offsets[0..11]: q codes, q scale atoms, q g, k codes, k scale atoms, k g,
+// offsets[0..12]: q codes, q scale atoms, q g, k codes, k scale atoms, k g,
 // v hi, v lo, then (dual-slice Q only, empty otherwise) the residual Q
 // slice's codes, scale atoms and g, and an fp32 scratch [B*Tp][Hq*D] for
-// Q - hi.  Returns the total size, or -1 for a bad shape.
+// Q - hi, then (single-slice Q only) the row maxima [B][Hq][Tp] fp32 of the
+// row-maximum kernel.  Returns the total size, or -1 for a bad shape.
 int64_t layout(int B, int Hq, int Hkv, int T, int D, int flags, int64_t* offsets) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0 || D <= 0 || D % 64 != 0 || Hq % Hkv != 0) return -1;
-  if (flags & ~(FP4ATTN_DUAL_Q | FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16)) return -1;
+  if (flags & ~(FP4ATTN_DUAL_Q | FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16 | FP4ATTN_PV_FP16)) return -1;
   const int64_t Tp = ((int64_t)T + 127) / 128 * 128;
   const int64_t rows = (int64_t)B * Tp;
   const int64_t dq = (flags & FP4ATTN_DUAL_Q) ? 1 : 0;
@@ -48,6 +49,7 @@ int64_t layout(int B, int Hq, int Hkv, int T, int D, int flags, int64_t* offsets
       dq * rows / 128 * Hq * (D / 64) * 512,
       dq * rows * 4,
       dq * rows * Hq * D * 4,  // Q - hi, fp32
+      (1 - dq) * rows * Hq * 4,  // row maxima [B][Hq][Tp]
   };
   int64_t off = 0;
   for (int i = 0; i < kPieces; ++i) {
@@ -195,6 +197,7 @@ extern "C" int fp4attn_forward_heads(const void* q, const void* k, const void* v
   uint8_t* qs_lo = dq ? ws + off[9] : nullptr;
   float* gq_lo = dq ? reinterpret_cast<float*>(ws + off[10]) : nullptr;
   float* qres = dq ? reinterpret_cast<float*>(ws + off[11]) : nullptr;
+  float* row_max = dq ? nullptr : reinterpret_cast<float*>(ws + off[12]);
   const int64_t qld = (int64_t)Hq * D;
   // The three operand preparations are independent: K and V run on side streams
   // forked from and joined back to the caller's stream (capturable in a CUDA graph),
@@ -245,9 +248,9 @@ extern "C" int fp4attn_forward_heads(const void* q, const void* k, const void* v
     }
   }
   if (int e = joiner.join()) return e;
-  AttnLaunch L{qc,    qs,   gq,   qc_lo, qs_lo, gq_lo, kc,   ks,   gk,     vhi,    vlo,
-               out,   B,    Hq,   Hkv,   T,     Tp,    D,    hkv0, hkv1,   causal, scaling,
-               flags & (FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16), 0};
+  AttnLaunch L{qc,  qs,      gq, qc_lo, qs_lo, gq_lo, kc, ks, gk,   vhi,  vlo,    out,
+               row_max, B, Hq, Hkv,   T,     Tp,    D,  hkv0, hkv1, causal, scaling,
+               flags & (FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16 | FP4ATTN_PV_FP16), 0};
   return launch_attention(L, st);
 }
 

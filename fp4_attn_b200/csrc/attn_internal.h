@@ -24,11 +24,12 @@ struct AttnLaunch {
   const uint16_t* v_hi;
   const uint16_t* v_lo;
   void* out;
+  float* row_max;  // scratch [B][HqT][Tp] fp32 for the row-maximum kernel, or null (max pass in the kernel)
   int B, HqT, HkvT, T, Tp, D;
   int hk0, hk1;
   int causal;
   float scaling;
-  int flags;  // FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16
+  int flags;  // FP4ATTN_DUAL_P | FP4ATTN_OUT_BF16 | FP4ATTN_PV_FP16
   int num_ctas;
 };
 

@@ -120,13 +120,46 @@ __device__ __forceinline__ void block_scale(const float* eb, const float* rcp, f
   s14 = (uint32_t)__half_as_ushort(__float2half_rn(e4m3_to_f32(sb) * 16384.0f)) * 0x10001u;
 }
 
+// The E4M3 scale byte b as an fp16 pair (exact: E4M3 values are fp16 values).
+__device__ __forceinline__ uint32_t e4m3_f16x2(uint32_t b) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(b * 0x101u));
+  return r;
+}
+
+// E2M1 round-to-nearest-even of (x0, x1) (satfinite), times the block scale:
+// the fp16 pair code * s, exact (P's block scales lie in [2^-9, 0.171875] or are 0).
+__device__ __forceinline__ uint32_t quant_pair_cvt(float x0, float x1, uint32_t s2) {
+  uint32_t c;
+  asm("{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(c)
+      : "f"(x0), "f"(x1));
+  return hmul2_u32(c, s2);
+}
+
+// Block scale of 16 values of e from the per-byte table: 1/s as a packed pair
+// (rs2) and s as an fp16 pair (s2), one shared-memory load.
+__device__ __forceinline__ void block_scale_tab(const float* eb, const uint2* tab, float r6, uint64_t& rs2,
+                                                uint32_t& s2) {
+  const float m0 = max3f(eb[0], eb[1], eb[2]), m1 = max3f(eb[3], eb[4], eb[5]);
+  const float m2 = max3f(eb[6], eb[7], eb[8]), m3 = max3f(eb[9], eb[10], eb[11]);
+  const float m4 = max3f(eb[12], eb[13], eb[14]);
+  const float amax = fmaxf(max3f(m0, m1, m2), max3f(m3, m4, eb[15]));
+  const uint2 t = tab[e4m3_satfinite(amax * r6) & 127];
+  const float rs = __uint_as_float(t.x);
+  rs2 = pk2(rs, rs);
+  s2 = t.y;
+}
+
 // Pass 2 on one 32-key chunk: e = exp2(z*u - m*u), running sum, NVFP4
 // fake-quant of e in two blocks of 16 -> 16 words of fp16 pairs.  The exp2 of
 // the second block is interleaved with the quantization of the first, so the
 // MUFU and the conversion pipe work at the same time.
 template <bool MASK>
 __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
-                                        uint64_t nmu2, const float* rcp, float r6, uint64_t (&lsum2)[4],
+                                        uint64_t nmu2, const uint2* tab, float r6, uint64_t (&lsum2)[4],
                                         uint32_t (&pk)[16]) {
   float e[32];
   const float4* g4 = reinterpret_cast<const float4*>(gk);
@@ -137,8 +170,8 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk
     for (int i = 0; i < 16; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
   }
   uint64_t rs2;
-  uint32_t s14;
-  block_scale(e, rcp, r6, rs2, s14);
+  uint32_t s2;
+  block_scale_tab(e, tab, r6, rs2, s2);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     exp4(a + 16 + 4 * q, g4[4 + q], u2, nmu2, e + 16 + 4 * q);
@@ -146,19 +179,19 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk
     for (int i = 4 * q; i < 4 * q + 4; i += 2) {
       float x0, x1;
       upk2(mul2(pk2(e[i], e[i + 1]), rs2), x0, x1);
-      pk[i / 2] = quant_pair_f16(x0, x1, s14);
+      pk[i / 2] = quant_pair_cvt(x0, x1, s2);
     }
   }
   if constexpr (MASK) {
 #pragma unroll
     for (int i = 16; i < 32; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
   }
-  block_scale(e + 16, rcp, r6, rs2, s14);
+  block_scale_tab(e + 16, tab, r6, rs2, s2);
 #pragma unroll
   for (int i = 16; i < 32; i += 2) {
     float x0, x1;
     upk2(mul2(pk2(e[i], e[i + 1]), rs2), x0, x1);
-    pk[i / 2] = quant_pair_f16(x0, x1, s14);
+    pk[i / 2] = quant_pair_cvt(x0, x1, s2);
   }
 #pragma unroll
   for (int i = 0; i < 32; i += 2) lsum2[(i >> 1) & 3] = add2(lsum2[(i >> 1) & 3], pk2(e[i], e[i + 1]));

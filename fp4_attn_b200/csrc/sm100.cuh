@@ -78,21 +78,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait until the phase with `parity` has completed.  Bounded: after kWaitNs
-// (or once another wait in the grid failed) it records `site` and returns
-// false.  The global failure flag and the timer are polled only every 64
-// spins so the common hand-off stays a tight try_wait loop.
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended (it issues nothing) until the phase completes or `ns` pass.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendNs = 20000;  // one suspended try_wait; the failure flag and timer are polled between them
+
+// Wait until the phase with `parity` has completed.  A waiting thread is
+// suspended in try_wait (a spinning one would take issue slots from the
+// warps that share its sub-partition).  Bounded: after kWaitNs (or once
+// another wait in the grid failed) it records `site` and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (dev_failed()) return false;
-      if (globaltimer() - t0 > kWaitNs) {
-        dev_fail(site);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
+    if (dev_failed()) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      dev_fail(site);
+      return false;
     }
   }
 }

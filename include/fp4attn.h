@@ -180,12 +180,16 @@ int fp4attn_fwd_packed_dual(const uint8_t* q_codes, const uint8_t* q_scales, con
 
 /* fp4attn_fwd_packed_dual on operands holding Hq / Hkv heads, attending only
  * KV heads [hkv0, hkv1) and their query groups; out [B, T, (hkv1 - hkv0) *
- * Hq / Hkv, D].  The kernel step of fp4attn_forward_heads. */
+ * Hq / Hkv, D].  The kernel step of fp4attn_forward_heads.  row_max: a
+ * [B][Hq][Tp] fp32 scratch (16-byte aligned) for single-slice Q -- the row
+ * maxima of the scores then come from a separate row-maximum kernel and the
+ * attention kernel reads every K tile once; NULL keeps the kernel's own max
+ * pass.  flags also takes FP4ATTN_PV_FP16. */
 int fp4attn_fwd_packed_heads(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
                              const uint8_t* q_codes_lo, const uint8_t* q_scales_lo, const float* q_g_lo,
                              const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g, const uint16_t* v_hi,
-                             const uint16_t* v_lo, void* out, int B, int Hq, int Hkv, int T, int Tp, int D, int hkv0,
-                             int hkv1, int causal, float scaling, int flags, void* stream);
+                             const uint16_t* v_lo, float* row_max, void* out, int B, int Hq, int Hkv, int T, int Tp,
+                             int D, int hkv0, int hkv1, int causal, float scaling, int flags, void* stream);
 
 /* Workspace of fp4attn_forward for a shape: writes the byte offsets of its
  * eight pieces -- Q codes, Q scale atoms, Q g, K codes, K scale atoms, K g,
@@ -199,10 +203,17 @@ int64_t fp4attn_workspace_layout(int B, int Hq, int Hkv, int T, int D, int64_t* 
 #define FP4ATTN_DUAL_Q 1 /* dual-slice Q (FP4_USE_DUAL_QUANT_Q=true) */
 #define FP4ATTN_DUAL_P 2 /* dual-slice P (FP4_USE_DUAL_QUANT_ATTN=true) */
 #define FP4ATTN_OUT_BF16 4 /* out is bf16 [B,T,Hq,D] (the reference's output dtype), not fp32 */
+/* PV reads V-hat rounded once to fp16 for every query tile but the first 128
+ * queries of each sequence (which keep the exact hi + lo planes): half the
+ * PV tensor work.  Max-abs 2.7e-3 x RMS(O), cosine 0.99999999 against the
+ * exact V-hat on the Llama-3-8B attention shape (1.4e-3 on the long-context
+ * prefill inputs); without it PV is exact. */
+#define FP4ATTN_PV_FP16 8
 
-/* fp4attn_workspace_layout with flags: offsets[0..11], the eight pieces
+/* fp4attn_workspace_layout with flags: offsets[0..12], the eight pieces
  * above, then (FP4ATTN_DUAL_Q only; empty otherwise) the residual Q slice's
- * codes, scale atoms and g, and an fp32 [B*Tp][Hq*D] scratch. */
+ * codes, scale atoms and g, and an fp32 [B*Tp][Hq*D] scratch, then (single-
+ * slice Q only) the row maxima [B][Hq][Tp] fp32 of the row-maximum kernel. */
 int64_t fp4attn_workspace_layout_ex(int B, int Hq, int Hkv, int T, int D, int flags, int64_t* offsets);
 
 /* Steps 1-3 as one call: q [B,Hq,T,D], k and v [B,Hkv,T,D] in in_dtype

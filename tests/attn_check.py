@@ -6,13 +6,18 @@ Tolerance (stated for the attention output O, fp32):
     quantization of P is decided at fp32 precision (rows flagged by
     oracle.torch_port.ambiguous_rows at relative DELTA are excluded from the
     max-abs check and stay in the cosine).
+
+The masked fraction is capped near what the oracle flags on the tests'
+inputs, so a regression that moves many rows cannot hide behind the mask:
+rows of up to a few hundred keys flag at most 1.6 % (cap 5 %), rows of 2048
+keys 4.5-5.5 %, 4096 keys 9.4 % (callers with long rows pass their own cap).
 """
 import torch
 
 DELTA = 1e-5
 
 
-def check(o_gpu, o_ref, flags=None, max_masked_frac=0.25):
+def check(o_gpu, o_ref, flags=None, max_masked_frac=0.05):
     o_gpu, o_ref = o_gpu.double(), o_ref.double()
     rms = o_ref.pow(2).mean().sqrt()
     cos = torch.nn.functional.cosine_similarity(o_gpu.flatten(), o_ref.flatten(), dim=0)

@@ -18,8 +18,9 @@ The reference is imported through a shim that changes no arithmetic:
   silenced.
 
 Outputs (committed): quant_torch.npz (quantizer cases), attention.npz (small
-simulated-FP4 attention cases), and config1.json (hash of the full
-[4096,4096] config-1 output).
+simulated-FP4 attention cases, fp32 simulation), attention_bf16.npz (the same
+attention as the reference ships it for a bf16 model: bf16 quantizer, bf16
+S and P), and config1.json (hash of the full [4096,4096] config-1 output).
 """
 from __future__ import annotations
 
@@ -199,6 +200,56 @@ def make_attention(Quantizer, lp):
     print(f"attention.npz: {len(index)} cases")
 
 
+def make_attention_shipped(Quantizer, lp):
+    """The reference as llama_patch.py wires it for a bf16 model (the configuration it ships with).
+
+    FP4Quantizer(dequant_dtype=bfloat16) as llama_patch.py:126-134 builds it
+    from the q_proj weight dtype; bf16 Q/K/V fake-quantized on their 2-D views
+    (:167-196; single-slice Q, FP4_USE_DUAL_QUANT_Q=false); S as a bf16 matmul
+    times scaling (:71) plus HF's additive bf16 causal mask (finfo(bf16).min
+    above the diagonal); softmax in fp32 rounded to bf16 (:76); P fake-quant in
+    bf16 (single, FP4_USE_DUAL_QUANT_ATTN=false); O = P V as a bf16 matmul
+    (:102).  Outputs bf16 [B, T, Hq, D] (stored as int16 bit patterns).
+    """
+    arrays = {}
+    index = []
+    lp.llama_fp4_attention_forward.quantize_enabled = True
+    os.environ["FP4_USE_DUAL_QUANT_ATTN"] = "false"
+    g = torch.Generator().manual_seed(12)
+    cases = [(1, 2, 1, 256, 128, True), (2, 2, 2, 96, 128, True), (1, 4, 2, 100, 128, True),
+             (1, 8, 2, 384, 128, True), (1, 2, 2, 160, 128, False)]
+    bf = torch.bfloat16
+    for k, (B, Hq, Hkv, T, D, causal) in enumerate(cases):
+        q = torch.randn(B, Hq, T, D, generator=g).bfloat16()
+        kk = torch.randn(B, Hkv, T, D, generator=g).bfloat16()
+        v = torch.randn(B, Hkv, T, D, generator=g).bfloat16()
+        base = f"s{k}"
+        arrays[base + "_q"] = q.view(torch.int16).numpy()
+        arrays[base + "_k"] = kk.view(torch.int16).numpy()
+        arrays[base + "_v"] = v.view(torch.int16).numpy()
+        qz = Quantizer(dequant_dtype=bf)
+        q2 = qz.single_nvfp4_fake_quant(q.permute(0, 2, 1, 3).reshape(B * T, Hq * D))
+        k2 = qz.single_nvfp4_fake_quant(kk.permute(0, 2, 1, 3).reshape(B * T, Hkv * D))
+        v2 = qz.single_nvfp4_fake_quant(v.permute(0, 2, 1, 3).reshape(B * T, Hkv * D).T,
+                                        global_scale_aligned=False).T
+        assert q2.dtype == k2.dtype == v2.dtype == bf
+        Qf = q2.reshape(B, T, Hq, D).permute(0, 2, 1, 3)
+        Kf = k2.reshape(B, T, Hkv, D).permute(0, 2, 1, 3)
+        Vf = v2.reshape(B, T, Hkv, D).permute(0, 2, 1, 3)
+        mask = None
+        if causal:
+            mask = torch.zeros(T, T, dtype=bf).masked_fill(torch.ones(T, T, dtype=torch.bool).triu(1),
+                                                           torch.finfo(bf).min)[None, None].expand(B, 1, T, T)
+        o, _ = lp.eager_attention_forward(_Mod(Hq // Hkv, qz), Qf, Kf, Vf, mask, scaling=D ** -0.5)
+        assert o.dtype == bf
+        arrays[base + "_o"] = o.contiguous().view(torch.int16).numpy()
+        index.append(dict(key=base, B=B, Hq=Hq, Hkv=Hkv, T=T, D=D, causal=causal))
+    os.environ.pop("FP4_USE_DUAL_QUANT_ATTN", None)
+    arrays["index"] = np.frombuffer(json.dumps(index).encode(), dtype=np.uint8)
+    np.savez_compressed(os.path.join(HERE, "attention_bf16.npz"), **arrays)
+    print(f"attention_bf16.npz: {len(index)} cases")
+
+
 def config1_input():
     """Config 1 input: randn [4096,4096] seed 0, 0.1% of entries x50, bf16."""
     g = torch.Generator().manual_seed(0)
@@ -225,7 +276,11 @@ def make_config1(Quantizer):
 
 
 if __name__ == "__main__":
+    # `--only NAME` regenerates one fixture file (quant, attention, attention_bf16, config1)
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
     Quantizer, lp = import_reference()
-    make_quant(Quantizer)
-    make_attention(Quantizer, lp)
-    make_config1(Quantizer)
+    for name, fn in (("quant", lambda: make_quant(Quantizer)), ("attention", lambda: make_attention(Quantizer, lp)),
+                     ("attention_bf16", lambda: make_attention_shipped(Quantizer, lp)),
+                     ("config1", lambda: make_config1(Quantizer))):
+        if only in (None, name):
+            fn()

@@ -95,7 +95,7 @@ def test_attention_llama3_8b_shape_full():
     v = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
     o = _run(q, k, v, True)
     ref, flags = tp.attention_with_margins(q, k, v, True, delta=DELTA)
-    cos, worst = check(o, ref, flags)
+    cos, worst = check(o, ref, flags, max_masked_frac=0.12)  # 9.4 % flagged at 4096 keys
     print(f"config2: cosine {cos:.9f}, max-abs/RMS on decided rows {worst:.3e}, masked {flags.float().mean():.4f}")
 
 
@@ -193,3 +193,67 @@ def test_bf16_output_is_the_fp32_result_rounded():
         o16 = fp4_attention_fwd(q, k, v, causal=True, dual_q=dual, dual_p=dual, out_dtype=torch.bfloat16)
         assert device_status() == 0
         assert o16.dtype == torch.bfloat16 and torch.equal(o16, o32.bfloat16())
+
+
+# ---------------------------------------------------------------- row-maximum kernel, fp16 V-hat PV
+def _packed_heads(ws, out, B, Hq, Hkv, T, D, row_max, flags, causal=True):
+    from fp4_attn_b200 import _lib
+    _lib.call("fp4attn_fwd_packed_heads", ws.qc.data_ptr(), ws.qs.data_ptr(), ws.gq.data_ptr(), None, None, None,
+              ws.kc.data_ptr(), ws.ks.data_ptr(), ws.gk.data_ptr(), ws.vhi.data_ptr(), ws.vlo.data_ptr(),
+              _lib.ptr(row_max), out.data_ptr(), B, Hq, Hkv, T, ws.Tp, D, 0, Hkv, 1 if causal else 0, D ** -0.5,
+              flags, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,causal", [(1, 8, 2, 1000, True), (2, 4, 1, 384, False), (1, 32, 8, 4096, True)])
+def test_row_max_kernel_equals_two_pass(B, Hq, Hkv, T, causal):
+    """The row-maximum kernel + the attention kernel without its max pass give, bit for bit, the output of
+    the two-pass kernel (same MMAs, same z, same maxima), for single and dual-slice P."""
+    from fp4_attn_b200.attention import DUAL_P, AttentionWorkspace, fp4_attention_fwd
+    from fp4_attn_b200.gemm import device_status
+    g = torch.Generator().manual_seed(T + 5 * Hq)
+    dev = torch.device("cuda", 0)
+    q = torch.randn(B, Hq, T, 128, generator=g).bfloat16().to(dev)
+    k = torch.randn(B, Hkv, T, 128, generator=g).bfloat16().to(dev)
+    v = torch.randn(B, Hkv, T, 128, generator=g).bfloat16().to(dev)
+    ws = AttentionWorkspace(B, Hq, Hkv, T, 128, dev)
+    fp4_attention_fwd(q, k, v, causal=causal, workspace=ws)  # prepares the packed operands
+    for flags in (0, DUAL_P):
+        a = torch.full((B, T, Hq, 128), float("nan"), device=dev)
+        b = torch.full((B, T, Hq, 128), float("nan"), device=dev)
+        _packed_heads(ws, a, B, Hq, Hkv, T, 128, None, flags, causal)
+        _packed_heads(ws, b, B, Hq, Hkv, T, 128, ws.row_max, flags, causal)
+        torch.cuda.synchronize()
+        assert device_status() == 0
+        assert torch.equal(a, b), f"flags {flags}"
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,causal", [(1, 8, 2, 1000, True), (2, 4, 1, 384, False), (1, 2, 1, 100, True)])
+def test_pv_fp16_small(B, Hq, Hkv, T, causal):
+    """FP4ATTN_PV_FP16 (V-hat rounded once to fp16 past the first 128 queries) within the tolerance."""
+    from fp4_attn_b200.attention import fp4_attention_fwd
+    from fp4_attn_b200.gemm import device_status
+    g = torch.Generator().manual_seed(B * 31 + T)
+    q = torch.randn(B, Hq, T, 128, generator=g).bfloat16()
+    k = torch.randn(B, Hkv, T, 128, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, T, 128, generator=g).bfloat16()
+    dev = torch.device("cuda", 0)
+    o = fp4_attention_fwd(q.to(dev), k.to(dev), v.to(dev), causal=causal, pv_fp16=True).cpu()
+    assert device_status() == 0
+    ref, flags = tp.attention_with_margins(q, k, v, causal, delta=DELTA)
+    check(o, ref, flags)
+
+
+def test_pv_fp16_llama3_8b_shape_full():
+    """Config 2 at full size with FP4ATTN_PV_FP16; bf16 output, as the bench runs it."""
+    from fp4_attn_b200.attention import fp4_attention_fwd
+    from fp4_attn_b200.gemm import device_status
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, 32, 4096, 128, generator=g).bfloat16()
+    k = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
+    v = torch.randn(1, 8, 4096, 128, generator=g).bfloat16()
+    dev = torch.device("cuda", 0)
+    o = fp4_attention_fwd(q.to(dev), k.to(dev), v.to(dev), causal=True, pv_fp16=True).cpu()
+    assert device_status() == 0
+    ref, flags = tp.attention_with_margins(q, k, v, True, delta=DELTA)
+    cos, worst = check(o, ref, flags, max_masked_frac=0.12)
+    print(f"config2 pv_fp16: cosine {cos:.9f}, max-abs/RMS on decided rows {worst:.3e}")

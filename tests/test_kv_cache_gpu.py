@@ -73,4 +73,4 @@ def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0):
             for h in range(Hq):
                 S = (Qf[b, h].double() @ Kf[b, h // G].double().T) * D ** -0.5
                 flags[b, :, h] = tp.ambiguous_rows(S, DELTA)
-        check(o, ref, flags, max_masked_frac=0.5)
+        check(o, ref, flags, max_masked_frac=0.08)  # the oracle flags 0-4.4 % of these decode rows

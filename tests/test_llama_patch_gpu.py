@@ -90,4 +90,4 @@ def test_llama2_7b_attention_shape():
             S = (qs[0, 0].double() @ ks[0, 0].double().T) * D ** -0.5
             S = S + torch.triu(torch.full((T, T), float("-inf"), dtype=torch.float64), 1)
             flags = tp.ambiguous_rows(S, DELTA)[None, :, None]
-            check(o[b:b + 1, :, h:h + 1], ref, flags)
+            check(o[b:b + 1, :, h:h + 1], ref, flags, max_masked_frac=0.08)  # 4.5-5.5 % flagged at 2048 keys

@@ -182,17 +182,29 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   // With a single pass the PV thread releases each K stage for the softmax warps: it
   // waits for all of them to finish P (after their last read of the stage's gk) anyway.
   constexpr bool PV_RELEASES_K = NPASS == 1;
+  // SPLIT (the precomputed-maximum kernel): one S buffer and two P buffers, so the softmax
+  // stores P(j+1) while PV(j) still runs; S is read at the start of a tile, so QK(j+1) lands
+  // while the softmax still works on tile j.  Otherwise two S buffers (the max pass has
+  // little work to hide QK's latency behind) and one P buffer.  TMEM: S [0,128), O
+  // [128,256), P0, P1 [256,384), scale atoms from 384 (SPLIT).
+  constexpr bool SPLIT = PRE;
+  constexpr uint32_t tO = SPLIT ? 128 : T_O, tP = SPLIT ? 256 : T_P;
+  constexpr uint32_t tSFA = SPLIT ? 384 : T_SFA, tSFB = SPLIT ? 392 : T_SFB;
+  static_assert(!SPLIT || tSFB + 8 * NK <= TMEM_COLS, "TMEM columns of the split layout");
+  constexpr int oK = OFF_K, oV = OFF_V, oSTAT = OFF_STAT, oRCP = OFF_RCP, oPTAB = OFF_PTAB, oMROW = OFF_MROW;
+  constexpr int oBAR = OFF_BAR;
+  constexpr int nV = NV;
   auto tr = [&](uint32_t uc, int slot, int j) {
     if constexpr (TRACE) trace(p, uc, slot, j);
   };
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* stat_m = reinterpret_cast<float*>(sm + OFF_STAT);
+  float* stat_m = reinterpret_cast<float*>(sm + oSTAT);
   float* stat_l = stat_m + NWG * 128;
   float* stat_r = stat_m + 2 * NWG * 128;
-  float* rcp = reinterpret_cast<float*>(sm + OFF_RCP);
-  uint2* ptab = reinterpret_cast<uint2*>(sm + OFF_PTAB);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  float* rcp = reinterpret_cast<float*>(sm + oRCP);
+  uint2* ptab = reinterpret_cast<uint2*>(sm + oPTAB);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + oBAR);
   uint64_t* q_full = bar + 0;
   uint64_t* q_empty = bar + 1;
   uint64_t* k_full = bar + 2;          // [NK]
@@ -201,12 +213,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint64_t* v_empty = v_full + NV;     // [NV]
   uint64_t* s_full = v_empty + NV;     // [2] S buffer written (MMA commit)
   uint64_t* s_free = s_full + 2;       // [2] S buffer read by every softmax warp
-  uint64_t* p_full = s_free + 2;       // P written by every softmax warp
-  uint64_t* p_free = p_full + 1;       // PV has read P (PV thread's commit)
-  uint64_t* o_full = p_free + 1;
+  uint64_t* p_full = s_free + 2;       // [2] P written by every softmax warp
+  uint64_t* p_free = p_full + 2;       // [2] PV has read P (PV thread's commit)
+  uint64_t* o_full = p_free + 2;
   uint64_t* o_free = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 1);
-  static_assert(2 + 2 * NK + 2 * NV + 8 + 1 <= 64, "barriers exceed their 512-byte slot");
+  static_assert(2 + 2 * NK + 2 * NV + 10 + 1 <= 64, "barriers exceed their 512-byte slot");
 
   const int warp = threadIdx.x / 32;
   const int nkb4q = p.nkb4q, nkb4k = p.nkb4k;
@@ -220,7 +232,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       // MMA commit + every softmax warp (they read gk), or + the PV thread for them
       mbar_init(&k_empty[i], PV_RELEASES_K ? 2 : 1 + 4 * NWG);
     }
-    for (int i = 0; i < NV; ++i) {
+    for (int i = 0; i < nV; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
@@ -228,8 +240,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4 * NWG);  // every softmax warp has loaded its rows
     }
-    mbar_init(p_full, 4 * NWG);  // every softmax warp has stored its P
-    mbar_init(p_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 4 * NWG);  // every softmax warp has stored its P
+      mbar_init(&p_free[i], 1);
+    }
     mbar_init(o_full, 1);
     mbar_init(o_free, 1);
     fence_barrier_init();
@@ -266,7 +280,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         mbar_arrive_expect_tx(q_full, (DQ ? 2 : 1) * (Q_BYTES + 1024 + 512) + (PRE ? 512 : 0));
         tma_load_2d(sm + OFF_Q, &tmQ, q_full, hq * (HD / 2), qrow);
         if constexpr (PRE)
-          bulk_load(sm + OFF_MROW, p.row_max + ((int64_t)un.b * p.HqT + hq) * p.Tp + un.qt * BM, 512, q_full);
+          bulk_load(sm + oMROW, p.row_max + ((int64_t)un.b * p.HqT + hq) * p.Tp + un.qt * BM, 512, q_full);
         bulk_load(sm + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * nkb4q + 2 * hq) * 512, 1024, q_full);
         bulk_load(sm + OFF_GQ, p.gq + qrow, 512, q_full);
         if constexpr (DQ) {
@@ -278,7 +292,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           for (int j = 0; j < n; ++j, ++kc) {
             const int s = kc % NK;
             if (kc >= NK) mbar_wait(&k_empty[s], ((kc / NK) - 1) & 1, 0x202);
-            uint8_t* ks = sm + OFF_K + s * K_STAGE;
+            uint8_t* ks = sm + oK + s * K_STAGE;
             const int krow = un.b * p.Tp + j * BN;
             mbar_arrive_expect_tx(&k_full[s], 8192 + 1024 + 512);
             tma_load_2d(ks, &tmK, &k_full[s], hk * (HD / 2), krow);
@@ -298,17 +312,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         const int vrow = (un.b * p.HkvT + p.hk0 + un.h / group) * HD;
-        for (int j = 0; j < n; ++j, ++vc) {
-          const int vs = vc % NV;
-          if (vc >= NV) mbar_wait(&v_empty[vs], ((vc / NV) - 1) & 1, 0x203);
-          uint8_t* v = sm + OFF_V + vs * V_STAGE;
+        for (int j = 0; j < n; ++j) {
           const bool lo = un.qt < p.pv_lo_tiles;  // the lo plane only where PV reads it
+          const int vs = vc % nV;
+          if (vc >= nV) mbar_wait(&v_empty[vs], ((vc / nV) - 1) & 1, 0x203);
+          uint8_t* v = sm + oV + vs * V_STAGE;
           mbar_arrive_expect_tx(&v_full[vs], lo ? V_STAGE : V_STAGE / 2);
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             tma_load_2d(v + 2 * half * V_HALF, &tmVhi, &v_full[vs], j * BN + 64 * half, vrow);
             if (lo) tma_load_2d(v + (2 * half + 1) * V_HALF, &tmVlo, &v_full[vs], j * BN + 64 * half, vrow);
           }
+          ++vc;
         }
       }
     }
@@ -328,8 +343,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         mbar_wait(&k_full[s], (kc / NK) & 1, 0x212);
         tc_fence_after();
         if (pass < 2) tr(uc, TR_QK + 32 * pass, j);
-        uint8_t* ks = sm + OFF_K + s * K_STAGE;
-        const uint32_t sfb = tmem + T_SFB + 8 * s;
+        uint8_t* ks = sm + oK + s * K_STAGE;
+        const uint32_t sfb = tmem + tSFB + 8 * s;
         tmem_cp_sf_atom(sfb, smem_desc(smem_u32(ks + 8192), 16, 128, kSwizzleNone));
         tmem_cp_sf_atom(sfb + 4, smem_desc(smem_u32(ks + 8192 + 512), 16, 128, kSwizzleNone));
         const uint32_t d = tmem + T_S + 128 * kb;
@@ -337,7 +352,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         for (int kk = 0; kk < 2; ++kk) {
           const uint64_t ad = smem_desc(smem_u32(sm + OFF_Q) + kk * 32, 16, 512, kSwizzle64B);
           const uint64_t bd = smem_desc(smem_u32(ks) + kk * 32, 16, 512, kSwizzle64B);
-          mma_nvf4(d, ad, bd, idq, tmem + T_SFA + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
+          mma_nvf4(d, ad, bd, idq, tmem + tSFA + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
         }
         if constexpr (DQ) {  // residual slice into the second accumulator
 #pragma unroll
@@ -359,14 +374,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         mbar_wait(q_full, uc & 1, 0x213);
         tr(uc, TR_UNIT, 0);
         tc_fence_after();
-        tmem_cp_sf_atom(tmem + T_SFA, smem_desc(smem_u32(sm + OFF_QSF), 16, 128, kSwizzleNone));
-        tmem_cp_sf_atom(tmem + T_SFA + 4, smem_desc(smem_u32(sm + OFF_QSF + 512), 16, 128, kSwizzleNone));
+        tmem_cp_sf_atom(tmem + tSFA, smem_desc(smem_u32(sm + OFF_QSF), 16, 128, kSwizzleNone));
+        tmem_cp_sf_atom(tmem + tSFA + 4, smem_desc(smem_u32(sm + OFF_QSF + 512), 16, 128, kSwizzleNone));
         if constexpr (DQ) {
           tmem_cp_sf_atom(tmem + T_SFA_LO, smem_desc(smem_u32(sm + OFF_QLOSF), 16, 128, kSwizzleNone));
           tmem_cp_sf_atom(tmem + T_SFA_LO + 4, smem_desc(smem_u32(sm + OFF_QLOSF + 512), 16, 128, kSwizzleNone));
         }
         for (int pass = 0; pass < NPASS; ++pass)
-          for (int j = 0; j < n; ++j) issue_qk(j, DQ ? 0 : (j & 1), pass);
+          for (int j = 0; j < n; ++j) issue_qk(j, (DQ || SPLIT) ? 0 : (j & 1), pass);
         tc_commit(q_empty);
         tr(uc, TR_UEND, 0);
       }
@@ -378,32 +393,37 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     // tile has landed; its commit frees the P buffer for the next tile.
     if (elect_one_lane()) {
       const uint32_t idv = idesc_f16(BM, HD);
-      uint32_t vc = 0, uc = 0, pu = 0;
+      uint32_t vc = 0, uc = 0, pu = 0, tcnt = 0;
       for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
         const Unit un = unit_of(u, p);
         const int n = kv_tiles(un, p);
         const int parts = un.qt < p.pv_lo_tiles ? 2 : 1;  // hi + lo planes, or hi alone
-        for (int j = 0; j < n; ++j, ++vc) {
-          const int vs = vc % NV;
-          mbar_wait(&v_full[vs], (vc / NV) & 1, 0x215);
+        for (int j = 0; j < n; ++j, ++tcnt) {
+          const int pb = SPLIT ? (int)(pu & 1) : 0;
+          mbar_wait(&v_full[vc % nV], (vc / nV) & 1, 0x215);  // the tile's (hi) stage
           tr(uc, TR_PWAIT, j);
-          mbar_wait(p_full, pu & 1, 0x214);
+          mbar_wait(&p_full[pb], (SPLIT ? (pu >> 1) : pu) & 1, 0x214);
           ++pu;
-          if constexpr (PV_RELEASES_K) mbar_arrive(&k_empty[vc % NK]);
+          if constexpr (PV_RELEASES_K) mbar_arrive(&k_empty[tcnt % NK]);
           if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x216);
           tc_fence_after();
           tr(uc, TR_PV, j);
-          const uint32_t v = smem_u32(sm + OFF_V + vs * V_STAGE);
+          {
+            const int vs = vc % nV;
+            const uint32_t v = smem_u32(sm + oV + vs * V_STAGE);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {  // keys 16kk .. 16kk+15
-            const uint32_t a = tmem + T_P + 8 * kk;  // fp16 P of keys 16kk..16kk+15
-            for (int part = 0; part < parts; ++part) {  // hi, lo planes
-              const uint32_t vb = v + ((kk >> 2) * 2 + part) * V_HALF + (kk & 3) * 32;
-              mma_f16_ts(tmem + T_O, a, smem_desc(vb, 16, 1024, kSwizzle128B), idv, (j > 0 || kk > 0 || part > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BN / 16; ++kk) {  // keys 16kk .. 16kk+15
+              const uint32_t a = tmem + tP + 64 * pb + 8 * kk;  // fp16 P of keys 16kk..16kk+15
+              for (int part = 0; part < parts; ++part) {  // hi, lo planes
+                const uint32_t vb = v + ((kk >> 2) * 2 + part) * V_HALF + (kk & 3) * 32;
+                mma_f16_ts(tmem + tO, a, smem_desc(vb, 16, 1024, kSwizzle128B), idv,
+                           (j > 0 || kk > 0 || part > 0) ? 1u : 0u);
+              }
             }
+            tc_commit(&v_empty[vs]);
+            ++vc;
           }
-          tc_commit(&v_empty[vs]);
-          tc_commit(p_free);
+          tc_commit(&p_free[pb]);
         }
         tc_commit(o_full);
       }
@@ -432,7 +452,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       if (threadIdx.x == 128) tr(pend_uc, TR_OFULL, 0);
       tc_fence_after();
       uint32_t a[32];
-      tmem_ld32(tmem + lane_base + T_O + col0, a);
+      tmem_ld32(tmem + lane_base + tO + col0, a);
       tmem_ld_wait();
       if (pend_off >= 0) {
         if (p.out_bf16) {  // rounded to bf16 as the reference's bf16 matmul output is
@@ -479,7 +499,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       }
       const uint64_t ratio2 = pk2(ratio, ratio);
       float m = -INFINITY;
-      if constexpr (PRE) m = reinterpret_cast<const float*>(sm + OFF_MROW)[r];
+      if constexpr (PRE) m = reinterpret_cast<const float*>(sm + oMROW)[r];
       // g (and m) are in registers: this warp no longer needs the unit's Q buffer
       __syncwarp();
       if (wlead) mbar_arrive(q_empty);
@@ -508,7 +528,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       // ---- pass 1: row maximum of z = acc * gk over this quarter's keys
       if constexpr (!PRE) {
       for (int j = 0; j < n; ++j, ++kc) {
-        const int kb = DQ ? 0 : (j & 1), s = kc % NK;
+        const int kb = (DQ || SPLIT) ? 0 : (j & 1), s = kc % NK;
         mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x222);
         if (kb) ++sfu1;
         else ++sfu0;
@@ -520,7 +540,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (wlead) mbar_arrive(&s_free[kb]);
-        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
+        const float* gk = reinterpret_cast<const float*>(sm + oK + s * K_STAGE + 9216) + col0;
         // keys with column > lim are masked (causal diagonal tile, or keys past T)
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         if (lim < col0 + 31) m = chunk_max<true>(a, gk, col0, lim, m);
@@ -541,7 +561,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       if constexpr (DP) {
         float rm = 0.0f;
         for (int j = 0; j < n; ++j, ++kc) {
-          const int kb = DQ ? 0 : (j & 1), s = kc % NK;
+          const int kb = (DQ || SPLIT) ? 0 : (j & 1), s = kc % NK;
           mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x226);
           if (kb) ++sfu1;
           else ++sfu0;
@@ -551,7 +571,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           tc_fence_before();
           __syncwarp();
           if (wlead) mbar_arrive(&s_free[kb]);
-          const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
+          const float* gk = reinterpret_cast<const float*>(sm + oK + s * K_STAGE + 9216) + col0;
           const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
           if (lim < col0 + 31) rm = chunk_rmax<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, rm);
           else rm = chunk_rmax<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, rm);
@@ -568,7 +588,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       // ---- pass 2: e = exp2(z*u - m*u), sum, NVFP4 fake-quant of e -> P quarter q
       uint64_t lsum2[4] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
       for (int j = 0; j < n; ++j, ++kc) {
-        const int kb = DQ ? 0 : (j & 1), s = kc % NK;
+        const int kb = (DQ || SPLIT) ? 0 : (j & 1), s = kc % NK;
         mbar_wait(&s_full[kb], (kb ? sfu1 : sfu0) & 1, 0x223);
         if (kb) ++sfu1;
         else ++sfu0;
@@ -581,7 +601,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         __syncwarp();
         if (wlead) mbar_arrive(&s_free[kb]);
         if (leader && q == 0) tr(uc, TR_LDDONE, j);
-        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
+        const float* gk = reinterpret_cast<const float*>(sm + oK + s * K_STAGE + 9216) + col0;
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         uint32_t pk[16];
         if constexpr (DP) {
@@ -596,15 +616,20 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         // first P is computed; that also frees the accumulator for this unit's first PV
         if (j == 0 && pend) epilogue();
         // the previous tile's PV must have read P before quarter q is overwritten
-        if (pt > 0) mbar_wait(p_free, (pt - 1) & 1, 0x225);
-        ++pt;
+        const int pb = SPLIT ? (int)(pt & 1) : 0;
+        if constexpr (SPLIT) {
+          if (pt >= 2) mbar_wait(&p_free[pb], ((pt >> 1) - 1) & 1, 0x225);
+        } else {
+          if (pt > 0) mbar_wait(&p_free[0], (pt - 1) & 1, 0x225);
+        }
         tc_fence_after();
-        tmem_st16(tmem + lane_base + T_P + 16 * q, pk);
+        tmem_st16(tmem + lane_base + tP + 64 * pb + 16 * q, pk);
         tmem_st_wait();
         tc_fence_before();
+        ++pt;
         __syncwarp();
         if (wlead) {
-          mbar_arrive(p_full);
+          mbar_arrive(&p_full[pb]);
           if constexpr (!PV_RELEASES_K) mbar_arrive(&k_empty[s]);
         }
         if (leader && q == 0) tr(uc, TR_PDONE, j);

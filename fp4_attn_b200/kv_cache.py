@@ -47,6 +47,24 @@ class NVFP4KVCache:
         self.v_g = torch.zeros(B, Tmax, dtype=torch.float32, device=device)
         self.len = 0
 
+    def grow(self, capacity: int) -> None:
+        """Reallocate for at least `capacity` tokens, keeping the cached ones (the HF cache grows the same way)."""
+        if capacity <= self.capacity:
+            return
+        Tmax = (capacity + 255) // 256 * 256
+        L = self.len
+        for name in ("k_codes", "k_scales", "v_codes", "v_scales"):  # [B, Hkv, Tmax, x]
+            old = getattr(self, name)
+            new = torch.zeros(self.B, self.Hkv, Tmax, old.shape[-1], dtype=old.dtype, device=old.device)
+            new[:, :, :L] = old[:, :, :L]
+            setattr(self, name, new)
+        for name in ("k_g", "v_g"):  # [B, Tmax]
+            old = getattr(self, name)
+            new = torch.zeros(self.B, Tmax, dtype=old.dtype, device=old.device)
+            new[:, :L] = old[:, :L]
+            setattr(self, name, new)
+        self.capacity, self.Tmax = capacity, Tmax
+
     def append(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """Quantize q new tokens k, v [B, Hkv, q, D] (post-RoPE K) as one call of the reference does, and store them."""
         _lib.require_cuda(k, v)

@@ -11,7 +11,12 @@ kernels:
   never materialised, so the weights slot is None.
 * ``llama_fp4_attention_forward`` is a drop-in LlamaAttention.forward
   (transformers 5.x signature): projections, RoPE, the KV-cache update,
-  ``fp4_eager_attention``, o_proj.
+  ``fp4_eager_attention``, o_proj.  With a cache it also keeps, per layer,
+  an NVFP4 copy of the cached K/V (``kv_cache.NVFP4KVCache``, attached to the
+  HF cache object), built at the first one-token call from the prefill's
+  tokens; every call's tokens are quantized as that call of the reference
+  quantizes them (llama_patch.py:167-196, 212-215), and one-token calls
+  (generation) attend over it with ``decode_attention``.
 * ``install()`` / ``uninstall()`` swap it in and out like eval.py does.
 * Single- or dual-slice Q and P follow FP4_USE_DUAL_QUANT_Q and
   FP4_USE_DUAL_QUANT_ATTN as the reference reads them (llama_patch.py:84,183:
@@ -25,8 +30,9 @@ Semantics that differ from the reference, by design:
   operands, so the native path quantizes the rotated Q and K.
 * The quantizer arithmetic is fp32 (the FP4Quantizer default) whatever the
   model dtype; the reference uses the weight dtype (llama_patch.py:126-134).
-* Prefill only: query and key lengths must match (a non-empty KV cache,
-  i.e. decode, raises).  The attention mask must be causal without padding.
+* Calls are a prefill (query and key lengths equal) or one new token over
+  the cache; several new tokens over a non-empty cache (chunked prefill)
+  raise.  The attention mask must be causal without padding.
 """
 from __future__ import annotations
 
@@ -65,7 +71,8 @@ def _check_mask(mask: torch.Tensor | None, T: int, S: int) -> None:
         allowed = m
     else:
         allowed = m > torch.finfo(m.dtype).min / 2
-    causal = torch.ones(T, S, dtype=torch.bool, device=m.device).tril()
+    # the T queries are the last T of the S positions: query i sees keys 0 .. i + S - T
+    causal = torch.ones(T, S, dtype=torch.bool, device=m.device).tril(S - T)
     if not bool((allowed == causal).all()):
         raise NotImplementedError("the FP4 attention kernel supports a plain causal mask (no padding)")
     _CHECKED = (weakref.ref(mask), mask._version, T, S)
@@ -97,6 +104,34 @@ def fp4_eager_attention(module, query, key, value, attention_mask, scaling, drop
 attention_interface = fp4_eager_attention
 
 
+def fp4_decode_attention(module, query, cache, attention_mask, scaling):
+    """One new token per sequence over the layer's NVFP4 cache (llama_patch.py:212-215 then :57-105):
+    query [B, Hq, 1, D] post-RoPE -> [B, 1, Hq, D] in query's dtype."""
+    from .kv_cache import decode_attention
+    _check_mask(attention_mask, 1, cache.len)
+    return decode_attention(query, cache, scaling=float(scaling)).to(query.dtype)
+
+
+# the decode call used by llama_fp4_attention_forward (tests may wrap it)
+decode_interface = fp4_decode_attention
+
+
+def nvfp4_cache(past_key_values, layer_idx: int, k: torch.Tensor):
+    """The layer's NVFP4 K/V cache kept beside an HF cache object (created empty on first use).
+    k: the new tokens' keys [B, Hkv, T, D] (shape and device)."""
+    from .kv_cache import NVFP4KVCache
+    caches = getattr(past_key_values, "_fp4_attn_nvfp4", None)
+    if caches is None:
+        caches = {}
+        past_key_values._fp4_attn_nvfp4 = caches
+    c = caches.get(layer_idx)
+    if c is None:
+        B, Hkv, T, D = k.shape
+        c = NVFP4KVCache(B, Hkv, max(T, 1) + 256, D, k.device)
+        caches[layer_idx] = c
+    return c
+
+
 def llama_fp4_attention_forward(self, hidden_states, position_embeddings=None, attention_mask=None,
                                 past_key_values=None, **kwargs):
     """LlamaAttention.forward with FP4 attention (llama_patch.py:108-250, post-RoPE quantization)."""
@@ -111,11 +146,29 @@ def llama_fp4_attention_forward(self, hidden_states, position_embeddings=None, a
     v = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
     cos, sin = position_embeddings
     q, k = apply_rotary_pos_emb(q, k, cos, sin)
-    if past_key_values is not None:
-        k, v = past_key_values.update(k, v, self.layer_idx)
     # llama_patch.py:228-232 (one host read for the three tensors)
     if bool(torch.isnan(q).any() | torch.isnan(k).any() | torch.isnan(v).any()):
         raise FloatingPointError("NaN in the attention inputs")
+    T = q.shape[2]
+    if past_key_values is not None:
+        past = past_key_values.get_seq_length(self.layer_idx)
+        if past and T != 1:
+            raise NotImplementedError(f"{T} new tokens over a cache of {past}: chunked prefill is not implemented")
+        k_all, v_all = past_key_values.update(k, v, self.layer_idx)  # HF's own bookkeeping (lengths, positions)
+        if past:
+            cache = nvfp4_cache(past_key_values, self.layer_idx, k)
+            if cache.len == 0:  # the first decode step: the prefill call's tokens, quantized as that one call
+                cache.grow(past + 256)
+                cache.append(k_all[:, :, :past], v_all[:, :, :past])
+            if cache.len != past:
+                raise RuntimeError(f"NVFP4 cache holds {cache.len} tokens, the HF cache {past}")
+            if cache.len + 1 > cache.capacity:
+                cache.grow(2 * cache.capacity)
+            cache.append(k, v)  # this call's own token
+            out = decode_interface(self, q, cache, attention_mask, self.scaling)
+            out = out.reshape(*input_shape, -1).contiguous()
+            return self.o_proj(out), None
+        k, v = k_all, v_all
     out, weights = attention_interface(self, q, k, v, attention_mask, scaling=self.scaling,
                                        dropout=0.0 if not self.training else self.attention_dropout)
     out = out.reshape(*input_shape, -1).contiguous()

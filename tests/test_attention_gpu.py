@@ -206,8 +206,11 @@ def _packed_heads(ws, out, B, Hq, Hkv, T, D, row_max, flags, causal=True):
 
 @pytest.mark.parametrize("B,Hq,Hkv,T,causal", [(1, 8, 2, 1000, True), (2, 4, 1, 384, False), (1, 32, 8, 4096, True)])
 def test_row_max_kernel_equals_two_pass(B, Hq, Hkv, T, causal):
-    """The row-maximum kernel + the attention kernel without its max pass give, bit for bit, the output of
-    the two-pass kernel (same MMAs, same z, same maxima), for single and dual-slice P."""
+    """The row-maximum kernel + the attention kernel without its max pass give the output of the two-pass
+    kernel: the same MMAs, the same z and the same maxima, hence the same P-hat.  The two kernels read P-hat
+    for PV from different places (shared memory, TMEM), which may sum the fp32 products of O in another
+    order, so O is compared to 1e-5 x RMS rather than bit for bit; one flipped P decision would move a row
+    by ~1e-3 x RMS or more."""
     from fp4_attn_b200.attention import DUAL_P, AttentionWorkspace, fp4_attention_fwd
     from fp4_attn_b200.gemm import device_status
     g = torch.Generator().manual_seed(T + 5 * Hq)
@@ -224,7 +227,9 @@ def test_row_max_kernel_equals_two_pass(B, Hq, Hkv, T, causal):
         _packed_heads(ws, b, B, Hq, Hkv, T, 128, ws.row_max, flags, causal)
         torch.cuda.synchronize()
         assert device_status() == 0
-        assert torch.equal(a, b), f"flags {flags}"
+        rms = a.double().pow(2).mean().sqrt()
+        worst = float((a.double() - b.double()).abs().max() / rms)
+        assert worst <= 1e-5, f"flags {flags}: max-abs / RMS {worst}"
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,T,causal", [(1, 8, 2, 1000, True), (2, 4, 1, 384, False), (1, 2, 1, 100, True)])

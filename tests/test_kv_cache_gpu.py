@@ -59,6 +59,7 @@ def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0):
         return q, Qf
 
     call(T0)
+    masked = []
     for _ in range(steps):
         q, Qf = call(1)
         o = decode_attention(q.to(dev), cache).cpu()
@@ -73,4 +74,7 @@ def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0):
             for h in range(Hq):
                 S = (Qf[b, h].double() @ Kf[b, h // G].double().T) * D ** -0.5
                 flags[b, :, h] = tp.ambiguous_rows(S, DELTA)
-        check(o, ref, flags, max_masked_frac=0.08)  # the oracle flags 0-4.4 % of these decode rows
+        # a step has only B * Hq rows: cap it at a quarter, and the whole run near the measured 0-4.4 %
+        check(o, ref, flags, max_masked_frac=0.25)
+        masked.append(flags.float().mean())
+    assert float(torch.stack(masked).mean()) <= 0.08

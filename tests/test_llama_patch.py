@@ -124,3 +124,28 @@ def test_kv_cache_host_checks():
         c.append(k, k)
     with pytest.raises(RuntimeError, match="CUDA"):
         kv_cache.decode_attention(torch.randn(1, 4, 1, 128), c)
+
+
+def test_mask_check_for_new_tokens_over_a_cache():
+    """T new queries over S keys: query i sees keys 0 .. i + S - T (a one-token decode sees all)."""
+    S = 8
+    lp._check_mask(torch.zeros(1, 1, 1, S), 1, S)
+    m = torch.full((2, S), torch.finfo(torch.float32).min).triu(S - 2 + 1)[None, None]
+    lp._check_mask(m, 2, S)
+    bad = torch.zeros(1, 1, 1, S)
+    bad[..., 3] = torch.finfo(torch.float32).min
+    with pytest.raises(NotImplementedError):
+        lp._check_mask(bad, 1, S)
+
+
+def test_kv_cache_grow_keeps_tokens():
+    from fp4_attn_b200 import kv_cache
+    c = kv_cache.NVFP4KVCache(2, 2, 10, 128, "cpu")
+    c.k_codes[:, :, :5] = 7
+    c.v_scales[:, :, :5] = 3
+    c.k_g[:, :5] = 1.5
+    c.len = 5
+    c.grow(300)
+    assert c.capacity == 300 and c.Tmax == 512 and c.k_codes.shape[2] == 512
+    assert (c.k_codes[:, :, :5] == 7).all() and (c.k_codes[:, :, 5:] == 0).all()
+    assert (c.v_scales[:, :, :5] == 3).all() and (c.k_g[:, :5] == 1.5).all() and (c.k_g[:, 5:] == 0).all()

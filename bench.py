@@ -463,7 +463,8 @@ class AttentionWorkload:
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4),
                 "algorithmic_flops_per_launch": self.flops,
                 "traffic": profile_traffic("fp4_attn_kernel_llama3-8b_T4096"),
-                "traffic_source": "profiles/fp4_attn_kernel_llama3-8b_T4096.md: ncu dram__bytes_read+write per launch"}
+                "traffic_source": "profiles/fp4_attn_kernel_llama3-8b_T4096.md: ncu dram__bytes_read+write per "
+                                  "launch of both kernels"}
 
     def cpu_sample(self, reps=None):
         """The reference's CPU path (torch ops) on one KV-head group (4 of 32 query heads)."""
@@ -992,7 +993,8 @@ class PrefillWorkload(AttentionWorkload):
 
     def kernel_roofline(self, kernel_s, peaks, peak_src):
         r = super().kernel_roofline(kernel_s, peaks, peak_src)
-        r["traffic"], r["traffic_source"] = None, "not captured at this shape"
+        r["traffic"], r["traffic_source"] = None, ("not captured at this shape (launch list only: "
+                                                   "profiles/attention_prefill_B4_Hq64_T32768_launches.md)")
         return r
 
     def cpu_sample(self, reps=None):

@@ -250,6 +250,58 @@ def make_attention_shipped(Quantizer, lp):
     print(f"attention_bf16.npz: {len(index)} cases")
 
 
+def tiny_llama(torch_mod=torch):
+    """The 2-layer random Llama of the logits fixture (4 query / 2 KV heads, head_dim 128), bf16 weights N(0, 0.02)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=128, vocab_size=256, max_position_embeddings=512,
+                      rope_theta=10000.0, attn_implementation="eager")
+    torch.manual_seed(3)
+    model = LlamaForCausalLM(cfg)
+    for p in model.parameters():
+        torch.nn.init.normal_(p, 0.0, 0.02)
+    ids = torch.randint(0, 256, (2, 128), generator=torch.Generator().manual_seed(4))
+    return model.to(torch.bfloat16).eval(), ids
+
+
+def make_llama_logits(Quantizer, lp):
+    """Logits of the reference's patched Llama (llama_patch.py:108-250 installed as eval.py:176-179 does,
+    quantization on, single-slice Q and P) on the tiny bf16 model, and of the stock model, for the
+    post-RoPE drop-in's logit-level comparison.
+
+    Shim (no arithmetic change): llama_patch.py:129-141 builds FP4Quantizer with keyword arguments
+    the shipped fp4_quant_utils.py does not take (global_sf, use_search) and moves a global_sf tensor;
+    the stand-in accepts them and holds that tensor.
+    """
+    from transformers.models.llama import modeling_llama
+
+    class PatchQuantizer(Quantizer):
+        def __init__(self, *a, global_sf=0.5, use_search=False, **kw):
+            super().__init__(*a, **kw)
+            self.global_sf = torch.tensor(global_sf)
+
+    model, ids = tiny_llama()
+    with torch.no_grad():
+        stock = model(ids, use_cache=False).logits.float()
+    os.environ["FP4_USE_DUAL_QUANT_Q"] = "false"
+    os.environ["FP4_USE_DUAL_QUANT_ATTN"] = "false"
+    lp.FP4Quantizer = PatchQuantizer
+    lp.llama_fp4_attention_forward.quantize_enabled = True
+    orig = modeling_llama.LlamaAttention.forward
+    modeling_llama.LlamaAttention.forward = lp.llama_fp4_attention_forward
+    try:
+        with torch.no_grad():
+            fp4 = model(ids, use_cache=False).logits.float()
+    finally:
+        modeling_llama.LlamaAttention.forward = orig
+        os.environ.pop("FP4_USE_DUAL_QUANT_Q", None)
+        os.environ.pop("FP4_USE_DUAL_QUANT_ATTN", None)
+    np.savez_compressed(os.path.join(HERE, "llama_logits.npz"), ref_fp4=fp4.numpy(), stock=stock.numpy(),
+                        ids=ids.numpy())
+    cos = torch.nn.functional.cosine_similarity(fp4.flatten(), stock.flatten(), dim=0)
+    print(f"llama_logits.npz: reference FP4 vs stock logits cosine {float(cos):.6f}")
+
+
 def config1_input():
     """Config 1 input: randn [4096,4096] seed 0, 0.1% of entries x50, bf16."""
     g = torch.Generator().manual_seed(0)
@@ -281,6 +333,7 @@ if __name__ == "__main__":
     Quantizer, lp = import_reference()
     for name, fn in (("quant", lambda: make_quant(Quantizer)), ("attention", lambda: make_attention(Quantizer, lp)),
                      ("attention_bf16", lambda: make_attention_shipped(Quantizer, lp)),
+                     ("llama_logits", lambda: make_llama_logits(Quantizer, lp)),
                      ("config1", lambda: make_config1(Quantizer))):
         if only in (None, name):
             fn()

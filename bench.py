@@ -1217,7 +1217,7 @@ class GemmWorkload:
     def kernel_roofline(self, kernel_s, peaks, peak_src):
         achieved = self.flops / kernel_s / 1e12
         peak, src = fp4_peak(peaks, peak_src)
-        return {"bound": "tensor", "kernel": "gemm_nvf4_kernel", "achieved": round(achieved, 1), "peak": round(peak, 1),
+        return {"bound": "tensor", "kernel": "gemm_nvf4_persistent", "achieved": round(achieved, 1), "peak": round(peak, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": src,
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4), "algorithmic_flops_per_launch": self.flops,
                 "traffic": profile_traffic("gemm_nvf4_kernel_8192x28672x8192"),

@@ -18,7 +18,8 @@ def _decoded(x_np, mode):
     return q, (g.astype(np.float64) if g is not None else None)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 128, 256), (300, 200, 512), (1024, 512, 4096), (64, 1000, 256)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 256), (300, 200, 512), (1024, 512, 4096), (64, 1000, 256),
+                                   (256, 384, 512), (512, 256, 1024), (4096, 2560, 512)])
 def test_gemm_matches_decoded_products(M, N, K):
     from fp4_attn_b200 import quant
     from fp4_attn_b200.gemm import device_status, gemm_nvf4

@@ -709,12 +709,15 @@ class DecodeWorkload:
     use_graph = True
 
     def __init__(self, dev, cpu_only=False, rank=0, world=1):
-        self.cache_bytes = self.B * self.Hkv * self.T * (64 + 8 + 64 + 128) + 2 * self.B * self.T * 4
+        # per (token, KV head): K codes 64 B + K scales 8 B + V codes 64 B + V scales 8 B (one per
+        # 16-token group: the appends are whole groups); per token: g_k, g_v
+        self.cache_bytes = self.B * self.Hkv * self.T * (64 + 8 + 64 + 8) + 2 * self.B * self.T * 4
         self.config = {"workload": "NVFP4 KV-cache decode: B=8, Hq=32, Hkv=8, D=128, 32768 cached tokens "
-                                   "(appended in calls of 4096), one new query token per sequence",
+                                   "(appended in calls of 4096, so V scales are read per 16-token group), "
+                                   "one new query token per sequence",
                        "cache_bytes": self.cache_bytes, "global_batch": world * self.B,
                        "shard": "batch rows 8r..8r+7 on rank r (own cache, seed 2 + r)",
-                       "l2": "cache 556 MB > L2"}
+                       "l2": "cache bytes read 304 MB > L2"}
         if cpu_only:
             return
         from fp4_attn_b200 import _lib

@@ -42,6 +42,8 @@ SIGNATURES = {
                                   _I, _F, _I, _P], _I),
     "fp4attn_decode_workspace_size": ([_I, _I, _I], _L),
     "fp4attn_decode": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _L, _P], _I),
+    "fp4attn_decode_ex": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _L, _P],
+                          _I),
     "fp4attn_forward": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _P, _P, _L,
                          _P], _I),
     "fp4attn_forward_ex": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _I, _F, _I, _P, _P,

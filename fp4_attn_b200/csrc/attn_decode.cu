@@ -9,7 +9,12 @@
 //      per-token global scale g_k [B][Tmax] (row mode on the [B*q, Hkv*D] view);
 //   V: codes [B][Hkv][Tmax][D/2], one E4M3 scale byte per element
 //      [B][Hkv][Tmax][D] (V's blocks of 16 run along the tokens of the call that
-//      appended them, so a token's scale is per channel), per-token g_v [B][Tmax].
+//      appended them, so a token's scale is per channel), per-token g_v [B][Tmax];
+//      optionally the same scales once per 16-token group [B][Hkv][Tmax/16][D]
+//      for a prefix of len16 tokens whose groups each came from one block (a
+//      call that started on a group boundary with whole blocks per sequence).
+//      Chunks of 256 keys inside that prefix read the 2 KB of group scales
+//      instead of 32 KB of per-element scales.
 // Tmax is a multiple of 256, so every chunk of 256 keys is whole in memory.
 // The query comes in the same packed form (row mode on its [B, Hq*D] view):
 // codes [B][Hq*D/2], E4M3 scales [B][Hq*D/16], g_q [B].
@@ -56,7 +61,7 @@ constexpr uint32_t SC_STAGE = SC_KC + SC_KS + SC_KG;
 constexpr int SC_STAGES = 3;
 // pv stage: V codes | V scales | g_v | S of the G heads
 constexpr uint32_t PV_VC = DK_KEYS * DK_D / 2;
-constexpr uint32_t PV_VS = DK_KEYS * DK_D;
+constexpr uint32_t PV_VS16 = DK_KEYS / 16 * DK_D;  // V scales of a chunk, one row per 16-token group
 constexpr uint32_t PV_VG = DK_KEYS * 4;
 constexpr uint32_t PV_S1 = DK_KEYS * 4;  // S of one head
 // MG bounds the query heads per KV head (NT = MG/8 rounded up MMA n-tiles of
@@ -74,8 +79,9 @@ struct PvCfg {
   static constexpr int KSTEPS = KPW / 16;
   static constexpr int LG = 32 / KPW;  // lane groups sharing a key in phase e
   static constexpr int THREADS = (NW + 1) * 32;
-  static constexpr int STAGES = MG <= 8 ? 3 : 2;
-  static constexpr uint32_t STAGE = PV_VC + PV_VS + PV_VG + MG * PV_S1;
+  // 4 heads per KV head: three stages fit two CTAs on an SM
+  static constexpr int STAGES = MG == 8 ? 4 : 3;
+  static constexpr uint32_t STAGE = PV_VC + PV_VS16 + PV_VG + MG * PV_S1;
   static constexpr uint32_t RING = STAGES * STAGE;
   static constexpr uint32_t PH = 2 * MG * PV_PH_LD * 2;
   static constexpr uint32_t PART = NW * MG * PV_PART_LD * 4;
@@ -94,7 +100,8 @@ struct DecodeArgs {
   const uint8_t* v_codes;
   const uint8_t* v_scales;
   const float* v_g;
-  int B, Hq, Hkv, len, Tmax, nsplit;
+  const uint8_t* v_scales16;  // [B][Hkv][Tmax/16][D], read for chunks split < nsplit16
+  int B, Hq, Hkv, len, Tmax, nsplit, nsplit16;
   float scaling;
   float* S;            // [B*Hq][nsplit*DK_KEYS]
   float* opart;        // [B*Hq][nsplit][D]
@@ -343,12 +350,13 @@ __global__ void __launch_bounds__((NW + 1) * 32) decode_pv_kernel(DecodeArgs p) 
         const int bk = item / p.nsplit, split = item % p.nsplit, b = bk / p.Hkv, hk = bk % p.Hkv;
         const int64_t row = (int64_t)bk * p.Tmax + (int64_t)split * DK_KEYS;
         const int ks = p.nsplit * DK_KEYS;
-        mbar_arrive_expect_tx(bar, PV_VC + PV_VS + PV_VG + (uint32_t)G * PV_S1);
+        const bool compact = split < p.nsplit16;
+        mbar_arrive_expect_tx(bar, PV_VC + (compact ? PV_VS16 : 0u) + PV_VG + (uint32_t)G * PV_S1);
         bulk_load(st, p.v_codes + row * (DK_D / 2), PV_VC, bar);
-        bulk_load(st + PV_VC, p.v_scales + row * DK_D, PV_VS, bar);
-        bulk_load(st + PV_VC + PV_VS, p.v_g + (int64_t)b * p.Tmax + (int64_t)split * DK_KEYS, PV_VG, bar);
+        if (compact) bulk_load(st + PV_VC, p.v_scales16 + row / 16 * DK_D, PV_VS16, bar);
+        bulk_load(st + PV_VC + PV_VS16, p.v_g + (int64_t)b * p.Tmax + (int64_t)split * DK_KEYS, PV_VG, bar);
         for (int g = 0; g < G; ++g)
-          bulk_load(st + PV_VC + PV_VS + PV_VG + g * PV_S1,
+          bulk_load(st + PV_VC + PV_VS16 + PV_VG + g * PV_S1,
                     p.S + ((int64_t)b * p.Hq + hk * G + g) * ks + (int64_t)split * DK_KEYS, PV_S1, bar);
       });
     return;
@@ -379,20 +387,17 @@ __global__ void __launch_bounds__((NW + 1) * 32) decode_pv_kernel(DecodeArgs p) 
     uint8_t* st = ring + (size_t)s * C::STAGE;
     const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
     const bool live = key < nlive;
-    if (!live) {
-      // the key is past len: whatever the cache holds there becomes V = 0 (P-hat is 0 there too)
-      if (lg == 0) {
-        uint4* vc = reinterpret_cast<uint4*>(st + key * (DK_D / 2));
+    // chunks inside the group-scale prefix hold every key live
+    const bool compact = split < p.nsplit16;
+    const int64_t vrow = (int64_t)bk * p.Tmax + (int64_t)split * DK_KEYS;  // first cache row of the chunk
+    if (!live && lg == 0) {
+      // the key is past len: whatever the cache holds there becomes V = 0 (its scales read as 0
+      // below; P-hat is 0 there too)
+      uint4* vc = reinterpret_cast<uint4*>(st + key * (DK_D / 2));
 #pragma unroll
-        for (int i = 0; i < DK_D / 2 / 16; ++i) vc[i] = make_uint4(0u, 0u, 0u, 0u);
-      }
-      if (lg == LG - 1) {
-        uint4* vs = reinterpret_cast<uint4*>(st + PV_VC + key * DK_D);
-#pragma unroll
-        for (int i = 0; i < DK_D / 16; ++i) vs[i] = make_uint4(0u, 0u, 0u, 0u);
-      }
+      for (int i = 0; i < DK_D / 2 / 16; ++i) vc[i] = make_uint4(0u, 0u, 0u, 0u);
     }
-    const float gv = live ? reinterpret_cast<const float*>(st + PV_VC + PV_VS)[key] : 0.0f;
+    const float gv = live ? reinterpret_cast<const float*>(st + PV_VC + PV_VS16)[key] : 0.0f;
     float gmax = gv;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
@@ -401,7 +406,7 @@ __global__ void __launch_bounds__((NW + 1) * 32) decode_pv_kernel(DecodeArgs p) 
     if (gmax > 0.0f) E = max(-100, min(100, 13 - (((__float_as_int(gmax) >> 23) & 0xFF) - 127)));
     const float up = __int_as_float((E + 127) << 23), down = __int_as_float((127 - E) << 23);
     {
-      const float* Ss = reinterpret_cast<const float*>(st + PV_VC + PV_VS + PV_VG);
+      const float* Ss = reinterpret_cast<const float*>(st + PV_VC + PV_VS16 + PV_VG);
 #pragma unroll
       for (int gi = 0; gi < (MG + LG - 1) / LG; ++gi) {
         const int g = lg + gi * LG;
@@ -449,7 +454,20 @@ __global__ void __launch_bounds__((NW + 1) * 32) decode_pv_kernel(DecodeArgs p) 
       for (int i = 0; i < 4; ++i) {
         const int kk = kb + t4 + 4 * i;
         cw[i] = *reinterpret_cast<const uint2*>(st + kk * (DK_D / 2) + 8 * g8);
-        sw[i] = *reinterpret_cast<const uint4*>(st + PV_VC + kk * DK_D + 16 * g8);
+      }
+      if (compact) {
+        // the four keys of this lane lie in one 16-token group: one row of group scales
+        const uint4 s16 = *reinterpret_cast<const uint4*>(st + PV_VC + (kb >> 4) * DK_D + 16 * g8);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sw[i] = s16;
+      } else {
+        // per-element scales straight from the cache (L2): only the chunks past the prefix
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int kk = kb + t4 + 4 * i;
+          sw[i] = kk < nlive ? __ldg(reinterpret_cast<const uint4*>(p.v_scales + (vrow + kk) * DK_D + 16 * g8))
+                             : make_uint4(0u, 0u, 0u, 0u);
+        }
       }
       uint32_t bhi[NT][2], blo[NT][2];
 #pragma unroll
@@ -613,12 +631,15 @@ extern "C" int64_t fp4attn_decode_workspace_size(int B, int Hq, int len) {
   return (bh * nsplit * DK_KEYS + bh * nsplit * (DK_D + 1) + bh) * (int64_t)sizeof(float);
 }
 
-extern "C" int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
-                              const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
-                              const uint8_t* v_codes, const uint8_t* v_scales, const float* v_g, int B, int Hq,
-                              int Hkv, int D, int len, int Tmax, float scaling, float* out, void* workspace,
-                              int64_t workspace_bytes, void* stream) {
+extern "C" int fp4attn_decode_ex(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                                 const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                                 const uint8_t* v_codes, const uint8_t* v_scales, const float* v_g,
+                                 const uint8_t* v_scales16, int len16, int B, int Hq, int Hkv, int D, int len,
+                                 int Tmax, float scaling, float* out, void* workspace, int64_t workspace_bytes,
+                                 void* stream) {
   clear_error();
+  if (len16 < 0 || len16 > len || len16 % 16 || (len16 > 0 && !v_scales16) || (uintptr_t)v_scales16 % 16)
+    return set_error(FP4ATTN_ERR_ARG, "group-scale prefix: len16 a multiple of 16 in [0, len], 16-byte aligned");
   if (!q_codes || !q_scales || !q_g || !k_codes || !k_scales || !k_g || !v_codes || !v_scales || !v_g || !out ||
       !workspace)
     return set_error(FP4ATTN_ERR_ARG, "null pointer");
@@ -639,8 +660,9 @@ extern "C" int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, c
   float* opart = S + bh * nsplit * DK_KEYS;
   float* lpart = opart + bh * nsplit * DK_D;
   unsigned int* mrow = reinterpret_cast<unsigned int*>(lpart + bh * nsplit);
-  DecodeArgs a{q_codes, q_scales, q_g, k_codes, k_scales, k_g,   v_codes, v_scales, v_g,  B,  Hq,
-               Hkv,     len,      Tmax, nsplit, scaling,  S,     opart,   lpart,    mrow, out};
+  DecodeArgs a{q_codes, q_scales, q_g,    k_codes, k_scales, k_g,  v_codes, v_scales,
+               v_g,     v_scales16, B,   Hq,      Hkv,      len,  Tmax,    nsplit,
+               len16 / DK_KEYS, scaling, S, opart, lpart, mrow, out};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(mrow, 0xFF, bh * sizeof(unsigned int), st) != cudaSuccess)
     return set_error(FP4ATTN_ERR_CUDA, "memset: %s", cudaGetErrorString(cudaGetLastError()));
@@ -658,4 +680,13 @@ extern "C" int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, c
   if (e) return e;
   decode_combine_kernel<<<(unsigned)bh, CB_GROUPS * 32, 0, st>>>(a);
   return check_launch("decode_combine_kernel");
+}
+
+extern "C" int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
+                              const uint8_t* k_codes, const uint8_t* k_scales, const float* k_g,
+                              const uint8_t* v_codes, const uint8_t* v_scales, const float* v_g, int B, int Hq,
+                              int Hkv, int D, int len, int Tmax, float scaling, float* out, void* workspace,
+                              int64_t workspace_bytes, void* stream) {
+  return fp4attn_decode_ex(q_codes, q_scales, q_g, k_codes, k_scales, k_g, v_codes, v_scales, v_g, nullptr, 0, B, Hq,
+                           Hkv, D, len, Tmax, scaling, out, workspace, workspace_bytes, stream);
 }

@@ -20,6 +20,15 @@ decode kernels stream whole chunks of 256 keys):
                                        16 runs along the tokens of the call
                                        that appended it
   v_g      fp32  [B, Tmax]             per-token global scale (column max / 1536)
+  v_scales16 uint8 [B, Hkv, Tmax/16, D] the same V scales once per 16-token group,
+                                       valid for the first len16 tokens
+
+A call's V blocks coincide with whole 16-token groups of the cache when the
+call starts on a group boundary and each sequence's tokens fill whole blocks
+(q a multiple of 16, or B == 1, where the blocks simply run along the call's
+tokens).  While every call so far did, the cache keeps len16 = the tokens
+covered by such groups, and the decode kernels read those groups' scales
+(1/16 of the per-element bytes).  Every scale is also stored per element.
 """
 from __future__ import annotations
 
@@ -45,7 +54,9 @@ class NVFP4KVCache:
         self.v_codes = torch.zeros(B, Hkv, Tmax, D // 2, dtype=u8, device=device)
         self.v_scales = torch.zeros(B, Hkv, Tmax, D, dtype=u8, device=device)
         self.v_g = torch.zeros(B, Tmax, dtype=torch.float32, device=device)
+        self.v_scales16 = torch.zeros(B, Hkv, Tmax // 16, D, dtype=u8, device=device)
         self.len = 0
+        self.len16 = 0
 
     def grow(self, capacity: int) -> None:
         """Reallocate for at least `capacity` tokens, keeping the cached ones (the HF cache grows the same way)."""
@@ -58,6 +69,10 @@ class NVFP4KVCache:
             new = torch.zeros(self.B, self.Hkv, Tmax, old.shape[-1], dtype=old.dtype, device=old.device)
             new[:, :, :L] = old[:, :, :L]
             setattr(self, name, new)
+        old = self.v_scales16  # [B, Hkv, Tmax/16, D]
+        new = torch.zeros(self.B, self.Hkv, Tmax // 16, self.D, dtype=old.dtype, device=old.device)
+        new[:, :, :(L + 15) // 16] = old[:, :, :(L + 15) // 16]
+        self.v_scales16 = new
         for name in ("k_g", "v_g"):  # [B, Tmax]
             old = getattr(self, name)
             new = torch.zeros(self.B, Tmax, dtype=old.dtype, device=old.device)
@@ -94,6 +109,13 @@ class NVFP4KVCache:
         self.v_codes[:, :, t0:t1] = packed
         self.v_scales[:, :, t0:t1] = sc
         self.v_g[:, t0:t1] = pv.g[:n].view(B, q)
+        if self.len16 == t0 and t0 % 16 == 0 and (q % 16 == 0 or B == 1):
+            # the call's blocks are the cache's groups t0/16 ... (the last one partial when q % 16 != 0,
+            # its scale padded like the reference's block; the next call then starts mid-group)
+            ng = (q + 15) // 16
+            s16 = pv.scales[:, :B * ng].view(H, D, B, ng).permute(2, 0, 3, 1)  # [B, H, groups, D]
+            self.v_scales16[:, :, t0 // 16:t0 // 16 + ng] = s16
+            self.len16 = t0 + (q // 16) * 16 if q % 16 else t1
         self.len = t1
 
 
@@ -119,8 +141,9 @@ def decode_attention(q: torch.Tensor, cache: NVFP4KVCache, scaling: float | None
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
     out = torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
-    _lib.call("fp4attn_decode", pq.codes.data_ptr(), pq.scales.data_ptr(), pq.g.data_ptr(), cache.k_codes.data_ptr(), cache.k_scales.data_ptr(),
-              cache.k_g.data_ptr(), cache.v_codes.data_ptr(), cache.v_scales.data_ptr(), cache.v_g.data_ptr(),
+    _lib.call("fp4attn_decode_ex", pq.codes.data_ptr(), pq.scales.data_ptr(), pq.g.data_ptr(),
+              cache.k_codes.data_ptr(), cache.k_scales.data_ptr(), cache.k_g.data_ptr(), cache.v_codes.data_ptr(),
+              cache.v_scales.data_ptr(), cache.v_g.data_ptr(), cache.v_scales16.data_ptr(), cache.len16,
               B, Hq, cache.Hkv, D, cache.len, cache.Tmax, float(scaling), out.data_ptr(), workspace.data_ptr(),
               workspace.numel() * workspace.element_size(), _lib.stream_of(q))
     return out.view(B, 1, Hq, D)

@@ -306,6 +306,17 @@ int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, const float*
                    const uint8_t* k_scales, const float* k_g, const uint8_t* v_codes, const uint8_t* v_scales,
                    const float* v_g, int B, int Hq, int Hkv, int D, int len, int Tmax, float scaling, float* out,
                    void* workspace, int64_t workspace_bytes, void* stream);
+/* fp4attn_decode with V's scales also stored once per 16-token group for a
+ * prefix of the cache: v_scales16 E4M3 [B][Hkv][Tmax/16][D], valid for the
+ * first len16 tokens (a multiple of 16, <= len; 0 and NULL = none), whose
+ * groups each came from one quantization block (a call that started on a group
+ * boundary with whole blocks per sequence).  Chunks of 256 keys inside the
+ * prefix read these instead of v_scales (2 KB instead of 32 KB per chunk and
+ * KV head); the result is identical. */
+int fp4attn_decode_ex(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g, const uint8_t* k_codes,
+                      const uint8_t* k_scales, const float* k_g, const uint8_t* v_codes, const uint8_t* v_scales,
+                      const float* v_g, const uint8_t* v_scales16, int len16, int B, int Hq, int Hkv, int D, int len,
+                      int Tmax, float scaling, float* out, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Measurement aid, no reference counterpart: one CTA per SM (num_ctas <= 0)
  * issues `iters` pairs of back-to-back tcgen05.mma.kind::mxf4nvf4 (M=128,

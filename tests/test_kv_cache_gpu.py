@@ -37,15 +37,29 @@ def _dequant_cache(c):
     return k, v
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,T0", [(2, 8, 2, 300), (3, 4, 4, 300), (1, 16, 2, 520), (2, 16, 1, 700)])
-def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0):
-    """Query heads per KV head 4, 1, 8 and 16; one to three splits of 256 keys."""
+def _check_group_scales(c, expect_len16):
+    """The per-group V scales of the prefix repeat the per-element ones."""
+    L16 = c.len16
+    assert L16 == expect_len16
+    if L16:
+        rep = c.v_scales16[:, :, :L16 // 16].repeat_interleave(16, dim=2)
+        assert torch.equal(rep.cpu(), c.v_scales[:, :, :L16].cpu())
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T0,len16", [(2, 8, 2, 300, 0), (3, 4, 4, 300, 0), (1, 16, 2, 520, 512),
+                                               (2, 16, 1, 700, 0), (2, 8, 2, 512, 512), (4, 32, 8, 1024, 1024),
+                                               (2, 8, 2, (256, 256), 512), (2, 8, 2, (256, 200), 256)])
+def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0, len16):
+    """Query heads per KV head 4, 1, 8 and 16; one to four splits of 256 keys; prefills whose V
+    blocks are whole 16-token groups (one call, or chunks of 256) put len16 tokens of the cache
+    on the group-scale path, and decode steps then extend the per-element tail."""
     from fp4_attn_b200.gemm import device_status
     from fp4_attn_b200.kv_cache import NVFP4KVCache, decode_attention
     D, steps = 128, 5
     dev = torch.device("cuda", 0)
-    g = torch.Generator().manual_seed(17 + B + Hq + T0)
-    cache = NVFP4KVCache(B, Hkv, T0 + steps, D, dev)
+    pre = T0 if isinstance(T0, tuple) else (T0,)
+    g = torch.Generator().manual_seed(17 + B + Hq + sum(pre))
+    cache = NVFP4KVCache(B, Hkv, sum(pre) + steps, D, dev)
     ks, vs = [], []
 
     def call(q_len):
@@ -58,7 +72,9 @@ def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0):
         vs.append(Vf)
         return q, Qf
 
-    call(T0)
+    for n in pre:
+        call(n)
+    _check_group_scales(cache, len16)
     masked = []
     for _ in range(steps):
         q, Qf = call(1)
@@ -67,6 +83,7 @@ def test_decode_over_nvfp4_cache(B, Hq, Hkv, T0):
         Kf, Vf = torch.cat(ks, dim=2), torch.cat(vs, dim=2)
         kd, vd = _dequant_cache(cache)
         assert torch.equal(kd, Kf) and torch.equal(vd, Vf)  # the cache holds the reference's values
+        _check_group_scales(cache, len16)
         ref = tp.eager_attention(Qf, Kf, Vf, False, D ** -0.5)  # [B, 1, Hq, D]
         G = Hq // Hkv
         flags = torch.zeros(B, 1, Hq, dtype=torch.bool)

@@ -278,8 +278,10 @@ int fp4attn_forward_noalloc(const void* q, const void* k, const void* v, int in_
  * Writes codes [M][H*64], E4M3 scales in tcgen05 atoms (H*2 groups per
  * 128-row block, the layout fp4attn_fwd_packed reads) and g [M].  T % 128 ==
  * 0, M % T == 0, K % 32 == 0, H = 1, 2 or a multiple of 4 up to 64; 16-byte
- * aligned buffers.  One launch, thread-block clusters of H/4 CTAs (one CTA
- * for H <= 4). */
+ * aligned buffers.  Two memsets (g, and 8 code bytes per 128-token block
+ * that serve as the block's hand-off words until the kernel writes them) and
+ * one cooperative launch of at most one CTA per SM; needs a device with
+ * cooperative launch. */
 int fp4qkv_rope_quant(const void* x, const void* w, const void* cos, const void* sin, int M, int K, int H, int T,
                       uint8_t* codes, uint8_t* scales, float* g, void* stream);
 

@@ -44,11 +44,14 @@ def _atoms_to_linear(sc, M, nblk):
     return sc[off]
 
 
-@pytest.mark.parametrize("H", [32, 8, 4, 2, 1])
-def test_rope_quant_projection_bit_exact(H):
+@pytest.mark.parametrize("H,B,T,K", [(32, 2, 256, 1024), (8, 2, 256, 1024), (4, 2, 256, 1024), (2, 2, 256, 1024),
+                                     (1, 2, 256, 1024), (32, 1, 4096, 256), (8, 4, 4096, 256)])
+def test_rope_quant_projection_bit_exact(H, B, T, K):
+    """The last two shapes have more tiles (token block x 4-head group) than SMs, so CTAs take
+    several tiles and some token blocks' tiles run in different rounds of the persistent grid."""
     from fp4_attn_b200.gemm import device_status
     from fp4_attn_b200.qkv import rope_quant_projection
-    B, T, K, D = 2, 256, 1024, 128
+    D = 128
     g = torch.Generator().manual_seed(7 + H)
     x = (torch.randint(-4, 5, (B * T, K), generator=g).float() / 8).bfloat16()
     w = (torch.randint(-4, 5, (H * D, K), generator=g).float() / 64).bfloat16()

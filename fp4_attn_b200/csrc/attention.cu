@@ -35,6 +35,8 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <stdlib.h>
+
 #include <type_traits>
 
 #include "common.cuh"
@@ -540,7 +542,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (wlead) mbar_arrive(&s_free[kb]);
-        const float* gk = reinterpret_cast<const float*>(sm + oK + s * K_STAGE + 9216) + col0;
+        const uint32_t gk = smem_u32(sm + oK + s * K_STAGE + 9216) + 4 * col0;
         // keys with column > lim are masked (causal diagonal tile, or keys past T)
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         if (lim < col0 + 31) m = chunk_max<true>(a, gk, col0, lim, m);
@@ -571,10 +573,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           tc_fence_before();
           __syncwarp();
           if (wlead) mbar_arrive(&s_free[kb]);
-          const float* gk = reinterpret_cast<const float*>(sm + oK + s * K_STAGE + 9216) + col0;
+          const uint32_t gk = smem_u32(sm + oK + s * K_STAGE + 9216) + 4 * col0;
           const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
-          if (lim < col0 + 31) rm = chunk_rmax<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, rm);
-          else rm = chunk_rmax<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, rm);
+          if (lim < col0 + 31) rm = chunk_rmax<true>(a, gk, col0, lim, u2, nmu2, smem_u32(rcp), r6, rm);
+          else rm = chunk_rmax<false>(a, gk, col0, lim, u2, nmu2, smem_u32(rcp), r6, rm);
           __syncwarp();
           if (wlead) mbar_arrive(&k_empty[s]);
         }
@@ -601,15 +603,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         __syncwarp();
         if (wlead) mbar_arrive(&s_free[kb]);
         if (leader && q == 0) tr(uc, TR_LDDONE, j);
-        const float* gk = reinterpret_cast<const float*>(sm + oK + s * K_STAGE + 9216) + col0;
+        const uint32_t gk = smem_u32(sm + oK + s * K_STAGE + 9216) + 4 * col0;
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * BN);
         uint32_t pk[16];
         if constexpr (DP) {
-          if (lim < col0 + 31) chunk_p_dual<true>(a, gk, col0, lim, u2, nmu2, rcp, r6, rg, gr, lsum2, pk);
-          else chunk_p_dual<false>(a, gk, col0, lim, u2, nmu2, rcp, r6, rg, gr, lsum2, pk);
+          if (lim < col0 + 31) chunk_p_dual<true>(a, gk, col0, lim, u2, nmu2, smem_u32(rcp), r6, rg, gr, lsum2, pk);
+          else chunk_p_dual<false>(a, gk, col0, lim, u2, nmu2, smem_u32(rcp), r6, rg, gr, lsum2, pk);
         } else {
-          if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, ptab, r6, lsum2, pk);
-          else chunk_p<false>(a, gk, col0, lim, u2, nmu2, ptab, r6, lsum2, pk);
+          if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, smem_u32(ptab), r6, lsum2, pk);
+          else chunk_p<false>(a, gk, col0, lim, u2, nmu2, smem_u32(ptab), r6, lsum2, pk);
         }
         if (leader && q == 0) tr(uc, TR_COMP, j);
         // the previous unit's O is written while its last PV finishes, after this unit's
@@ -811,7 +813,7 @@ __global__ void __launch_bounds__(rmx::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (wlead) mbar_arrive(&s_free[b]);
-        const float* gk = reinterpret_cast<const float*>(sm + OFF_K + s * K_STAGE + 9216) + col0;
+        const uint32_t gk = smem_u32(sm + OFF_K + s * K_STAGE + 9216) + 4 * col0;
         const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * attn::BN);
         if (lim < col0 + 31) m = chunk_max<true>(a, gk, col0, lim, m);
         else m = chunk_max<false>(a, gk, col0, lim, m);
@@ -832,6 +834,9 @@ __global__ void __launch_bounds__(rmx::THREADS, 1)
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
+
+#include "attn_pingpong.cuh"
+#include "attn_rowmax.cuh"
 
 // ------------------------------------------------------------ V preparation
 // Vhat = single_nvfp4(v2d.T, global_scale_aligned=False) in fp32 arithmetic
@@ -1151,6 +1156,19 @@ extern "C" int fp4attn_prepare_v(const void* v, int in_dtype, int B, int Hkv, in
   return launch_vprep(a, st);
 }
 
+// Kernel-variant switches, read from the environment once per process: unset or
+// anything but "0" means on.
+static bool env_on(const char* name) {
+  const char* e = getenv(name);
+  return !(e && e[0] == '0');
+}
+// The single-slice attention (precomputed maxima, single-slice P) runs on the two-group
+// kernel unless FP4ATTN_PINGPONG=0 selects the one-group kernel.
+static bool pingpong_enabled() {
+  static const bool on = env_on("FP4ATTN_PINGPONG");
+  return on;
+}
+
 int fp4::launch_attention(const AttnLaunch& L, cudaStream_t st) {
   using namespace attn;
   const int B = L.B, HqT = L.HqT, HkvT = L.HkvT, T = L.T, Tp = L.Tp;
@@ -1235,9 +1253,21 @@ int fp4::launch_attention(const AttnLaunch& L, cudaStream_t st) {
   int grid = L.num_ctas > 0 ? L.num_ctas : sms;
   if (grid > a.units) grid = a.units;
   if (pre) {
-    if (int e = set_smem_attr((const void*)fp4_rowmax_kernel, rmx::SMEM_BYTES)) return e;
-    fp4_rowmax_kernel<<<grid, rmx::THREADS, rmx::SMEM_BYTES, st>>>(mq, mk, a);
-    if (int e = check_launch("fp4_rowmax_kernel")) return e;
+    static const bool groups = env_on("FP4ATTN_ROWMAX_GROUPS");
+    if (groups) {
+      if (int e = set_smem_attr((const void*)fp4_rowmax_groups_kernel, rmg::SMEM_BYTES)) return e;
+      fp4_rowmax_groups_kernel<<<grid, rmg::THREADS, rmg::SMEM_BYTES, st>>>(mq, mk, a);
+      if (int e = check_launch("fp4_rowmax_groups_kernel")) return e;
+    } else {
+      if (int e = set_smem_attr((const void*)fp4_rowmax_kernel, rmx::SMEM_BYTES)) return e;
+      fp4_rowmax_kernel<<<grid, rmx::THREADS, rmx::SMEM_BYTES, st>>>(mq, mk, a);
+      if (int e = check_launch("fp4_rowmax_kernel")) return e;
+    }
+    if (!dual_p && !a.trace && pingpong_enabled()) {
+      if (int e = set_smem_attr((const void*)fp4_attn_pingpong_kernel, pp::SMEM_BYTES)) return e;
+      fp4_attn_pingpong_kernel<<<grid, pp::THREADS, pp::SMEM_BYTES, st>>>(mq, mk, mvh, mvl, a);
+      return check_launch("fp4_attn_pingpong_kernel");
+    }
   }
   kern<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mql, mk, mvh, mvl, a);
   return check_launch("fp4_attn_kernel");

@@ -8,6 +8,27 @@
 
 namespace fp4 {
 
+// Shared-memory loads at 32-bit shared-window addresses.  The kernels re-align
+// their dynamic shared memory base through an integer, after which the
+// compiler cannot prove a pointer is shared and would issue generic loads
+// (longer latency); volatile keeps them after the mbarrier waits that order
+// them behind the asynchronous copies that filled the buffers.
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds_u2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_f(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -69,17 +90,18 @@ __device__ __forceinline__ uint32_t quant_pair_f16(float x0, float x1, uint32_t 
 }
 
 // Pass 1 on one 32-key chunk: running max of z = acc * gk (keys with
-// column > lim masked when MASK).
+// column > lim masked when MASK); gk is the shared address of the chunk's 32
+// key scales.  The products round like the packed ones of chunk_p.
 template <bool MASK>
-__device__ __forceinline__ float chunk_max(const uint32_t (&a)[32], const float* gk, int col0, int lim, float m) {
+__device__ __forceinline__ float chunk_max(const uint32_t (&a)[32], uint32_t gk, int col0, int lim, float m) {
   float z[32];
-  const float4* g4 = reinterpret_cast<const float4*>(gk);
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
-    const float4 g = g4[q];
-    upk2(mul2(pk2(__uint_as_float(a[4 * q]), __uint_as_float(a[4 * q + 1])), pk2(g.x, g.y)), z[4 * q], z[4 * q + 1]);
-    upk2(mul2(pk2(__uint_as_float(a[4 * q + 2]), __uint_as_float(a[4 * q + 3])), pk2(g.z, g.w)), z[4 * q + 2],
-         z[4 * q + 3]);
+    const float4 g = lds_f4(gk + 16 * q);
+    z[4 * q] = __fmul_rn(__uint_as_float(a[4 * q]), g.x);
+    z[4 * q + 1] = __fmul_rn(__uint_as_float(a[4 * q + 1]), g.y);
+    z[4 * q + 2] = __fmul_rn(__uint_as_float(a[4 * q + 2]), g.z);
+    z[4 * q + 3] = __fmul_rn(__uint_as_float(a[4 * q + 3]), g.w);
   }
   if constexpr (MASK) {
 #pragma unroll
@@ -108,14 +130,14 @@ __device__ __forceinline__ void exp4(const uint32_t* a, float4 g, uint64_t u2, u
 
 // Block scale of 16 values of e: the E4M3 scale byte's reciprocal (rs) and
 // the scale * 2^14 as two fp16 halves (s14).
-__device__ __forceinline__ void block_scale(const float* eb, const float* rcp, float r6, uint64_t& rs2,
+__device__ __forceinline__ void block_scale(const float* eb, uint32_t rcp, float r6, uint64_t& rs2,
                                             uint32_t& s14) {
   const float m0 = max3f(eb[0], eb[1], eb[2]), m1 = max3f(eb[3], eb[4], eb[5]);
   const float m2 = max3f(eb[6], eb[7], eb[8]), m3 = max3f(eb[9], eb[10], eb[11]);
   const float m4 = max3f(eb[12], eb[13], eb[14]);
   const float amax = fmaxf(max3f(m0, m1, m2), max3f(m3, m4, eb[15]));
   const uint8_t sb = e4m3_satfinite(amax * r6);
-  const float rs = rcp[sb & 127];
+  const float rs = lds_f(rcp + 4 * (sb & 127));
   rs2 = pk2(rs, rs);
   s14 = (uint32_t)__half_as_ushort(__float2half_rn(e4m3_to_f32(sb) * 16384.0f)) * 0x10001u;
 }
@@ -141,13 +163,13 @@ __device__ __forceinline__ uint32_t quant_pair_cvt(float x0, float x1, uint32_t 
 
 // Block scale of 16 values of e from the per-byte table: 1/s as a packed pair
 // (rs2) and s as an fp16 pair (s2), one shared-memory load.
-__device__ __forceinline__ void block_scale_tab(const float* eb, const uint2* tab, float r6, uint64_t& rs2,
+__device__ __forceinline__ void block_scale_tab(const float* eb, uint32_t tab, float r6, uint64_t& rs2,
                                                 uint32_t& s2) {
   const float m0 = max3f(eb[0], eb[1], eb[2]), m1 = max3f(eb[3], eb[4], eb[5]);
   const float m2 = max3f(eb[6], eb[7], eb[8]), m3 = max3f(eb[9], eb[10], eb[11]);
   const float m4 = max3f(eb[12], eb[13], eb[14]);
   const float amax = fmaxf(max3f(m0, m1, m2), max3f(m3, m4, eb[15]));
-  const uint2 t = tab[e4m3_satfinite(amax * r6) & 127];
+  const uint2 t = lds_u2(tab + 8 * (e4m3_satfinite(amax * r6) & 127));
   const float rs = __uint_as_float(t.x);
   rs2 = pk2(rs, rs);
   s2 = t.y;
@@ -158,13 +180,12 @@ __device__ __forceinline__ void block_scale_tab(const float* eb, const uint2* ta
 // the second block is interleaved with the quantization of the first, so the
 // MUFU and the conversion pipe work at the same time.
 template <bool MASK>
-__device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
-                                        uint64_t nmu2, const uint2* tab, float r6, uint64_t (&lsum2)[4],
+__device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], uint32_t gk, int col0, int lim, uint64_t u2,
+                                        uint64_t nmu2, uint32_t tab, float r6, uint64_t (&lsum2)[4],
                                         uint32_t (&pk)[16]) {
   float e[32];
-  const float4* g4 = reinterpret_cast<const float4*>(gk);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) exp4(a + 4 * q, g4[q], u2, nmu2, e + 4 * q);
+  for (int q = 0; q < 4; ++q) exp4(a + 4 * q, lds_f4(gk + 16 * q), u2, nmu2, e + 4 * q);
   if constexpr (MASK) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
@@ -174,7 +195,7 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk
   block_scale_tab(e, tab, r6, rs2, s2);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    exp4(a + 16 + 4 * q, g4[4 + q], u2, nmu2, e + 16 + 4 * q);
+    exp4(a + 16 + 4 * q, lds_f4(gk + 64 + 16 * q), u2, nmu2, e + 16 + 4 * q);
 #pragma unroll
     for (int i = 4 * q; i < 4 * q + 4; i += 2) {
       float x0, x1;
@@ -208,11 +229,10 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], const float* gk
 
 // e = exp2(z*u - m*u) of one 32-key chunk (keys with column > lim zeroed when MASK).
 template <bool MASK>
-__device__ __forceinline__ void chunk_e(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
+__device__ __forceinline__ void chunk_e(const uint32_t (&a)[32], uint32_t gk, int col0, int lim, uint64_t u2,
                                         uint64_t nmu2, float (&e)[32]) {
-  const float4* g4 = reinterpret_cast<const float4*>(gk);
 #pragma unroll
-  for (int q = 0; q < 8; ++q) exp4(a + 4 * q, g4[q], u2, nmu2, e + 4 * q);
+  for (int q = 0; q < 8; ++q) exp4(a + 4 * q, lds_f4(gk + 16 * q), u2, nmu2, e + 4 * q);
   if constexpr (MASK) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
@@ -220,7 +240,7 @@ __device__ __forceinline__ void chunk_e(const uint32_t (&a)[32], const float* gk
 }
 
 // hi slice of 16 values: fp16 pairs code * scale (exact), as chunk_p forms them.
-__device__ __forceinline__ void slice_hi(const float* eb, const float* rcp, float r6, uint32_t (&hp)[8]) {
+__device__ __forceinline__ void slice_hi(const float* eb, uint32_t rcp, float r6, uint32_t (&hp)[8]) {
   uint64_t rs2;
   uint32_t s14;
   block_scale(eb, rcp, r6, rs2, s14);
@@ -238,8 +258,8 @@ __device__ __forceinline__ float2 f16x2_to_f32(uint32_t h) {
 
 // Residual pass on one 32-key chunk: running max of |e - hi|.
 template <bool MASK>
-__device__ __forceinline__ float chunk_rmax(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
-                                            uint64_t nmu2, const float* rcp, float r6, float rm) {
+__device__ __forceinline__ float chunk_rmax(const uint32_t (&a)[32], uint32_t gk, int col0, int lim, uint64_t u2,
+                                            uint64_t nmu2, uint32_t rcp, float r6, float rm) {
   float e[32];
   chunk_e<MASK>(a, gk, col0, lim, u2, nmu2, e);
 #pragma unroll
@@ -258,8 +278,8 @@ __device__ __forceinline__ float chunk_rmax(const uint32_t (&a)[32], const float
 // Final pass of dual-slice P on one 32-key chunk: running sum of e, then
 // P-hat = hi + lo per key, rounded to fp16 pairs (pk).  rg = recip(gr).
 template <bool MASK>
-__device__ __forceinline__ void chunk_p_dual(const uint32_t (&a)[32], const float* gk, int col0, int lim, uint64_t u2,
-                                             uint64_t nmu2, const float* rcp, float r6, float rg, float gr,
+__device__ __forceinline__ void chunk_p_dual(const uint32_t (&a)[32], uint32_t gk, int col0, int lim, uint64_t u2,
+                                             uint64_t nmu2, uint32_t rcp, float r6, float rg, float gr,
                                              uint64_t (&lsum2)[4], uint32_t (&pk)[16]) {
   float e[32];
   chunk_e<MASK>(a, gk, col0, lim, u2, nmu2, e);
@@ -280,7 +300,7 @@ __device__ __forceinline__ void chunk_p_dual(const uint32_t (&a)[32], const floa
       am = max3f(am, fabsf(xr[2 * i]), fabsf(xr[2 * i + 1]));
     }
     const uint32_t sb = e4m3_satfinite(am * r6);
-    const float rs = rcp[sb & 127];
+    const float rs = lds_f(rcp + 4 * (sb & 127));
     const uint64_t rs2 = pk2(rs, rs);
     uint32_t s2;
     asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(s2) : "r"(sb * 0x101u));

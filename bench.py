@@ -457,14 +457,15 @@ class AttentionWorkload:
     def kernel_roofline(self, kernel_s, peaks, peak_src):
         achieved = self.flops / kernel_s / 1e12
         peak, src = fp4_peak(peaks, peak_src)
-        return {"bound": "tensor", "kernel": "fp4_rowmax_kernel + fp4_attn_kernel", "achieved": round(achieved, 1),
+        return {"bound": "tensor", "kernel": "fp4_rowmax_t_kernel + fp4_attn_pingpong_kernel",
+                "achieved": round(achieved, 1),
                 "peak": round(peak, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": src,
                 "frac_of_nominal_fp4": round(achieved / 9000.0, 4),
                 "algorithmic_flops_per_launch": self.flops,
-                "traffic": profile_traffic("fp4_attn_kernel_llama3-8b_T4096"),
-                "traffic_source": "profiles/fp4_attn_kernel_llama3-8b_T4096.md: ncu dram__bytes_read+write per "
-                                  "launch of both kernels"}
+                "traffic": profile_traffic("fp4_attn_pingpong_kernel_llama3-8b_T4096"),
+                "traffic_source": "profiles/fp4_attn_pingpong_kernel_llama3-8b_T4096.md: ncu dram__bytes_read+write "
+                                  "per launch of both kernels"}
 
     def cpu_sample(self, reps=None):
         """The reference's CPU path (torch ops) on one KV-head group (4 of 32 query heads)."""

@@ -72,8 +72,7 @@ constexpr int V_STAGE = 4 * V_HALF;  // keys 0-63 hi, lo; keys 64-127 hi, lo
 constexpr int OFF_V = OFF_K + NK * K_STAGE;
 constexpr int OFF_STAT = OFF_V + NV * V_STAGE;  // m[NWG][128], l[NWG][128], residual max[NWG][128]
 constexpr int OFF_RCP = OFF_STAT + 3 * NWG * 128 * 4;
-constexpr int OFF_PTAB = OFF_RCP + 128 * 4;  // per E4M3 scale byte: (1/s, s as an fp16 pair)
-constexpr int OFF_MROW = OFF_PTAB + 128 * 8;  // the unit's 128 row maxima (PRE), loaded with Q
+constexpr int OFF_MROW = OFF_RCP + 128 * 4;  // the unit's 128 row maxima (PRE), loaded with Q
 constexpr int OFF_BAR = OFF_MROW + 128 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
@@ -101,7 +100,7 @@ struct AttnArgs {
   // with nkb4q / nkb4k scale atoms per 128-row block (2 per head) and HkvT KV heads.
   int hq0, hk0, nkb4q, nkb4k, HkvT, HqT;
   // Row maxima of z = (Q K^T) * gk per (batch, query head of the operands, row):
-  // [B][HqT][Tp] fp32, written by fp4_rowmax_kernel and read by the attention kernel
+  // [B][HqT][Tp] fp32, written by fp4_rowmax_t_kernel and read by the attention kernels
   // instantiated with PRE (which then has no max pass of its own).
   float* row_max;
   // PV uses V-hat's lo plane only for query tiles qt < pv_lo_tiles (the hi plane is
@@ -171,7 +170,7 @@ __device__ __forceinline__ int kv_tiles(const Unit& un, const AttnArgs& p) {
 // both QK products of a key tile go to the two S accumulators and combine per
 // row).  DP: dual-slice P (a residual pass between the max pass and the PV
 // pass finds each row's residual scale; the PV pass writes hi + lo).  PRE: the
-// row maxima come from fp4_rowmax_kernel (p.row_max, loaded with Q), so the
+// row maxima come from fp4_rowmax_t_kernel (p.row_max, loaded with Q), so the
 // kernel has no max pass and reads each K tile once (single-slice Q only).
 template <bool TRACE, bool DQ, bool DP, bool PRE>
 __global__ void __launch_bounds__(attn::THREADS, 1)
@@ -193,7 +192,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   constexpr uint32_t tO = SPLIT ? 128 : T_O, tP = SPLIT ? 256 : T_P;
   constexpr uint32_t tSFA = SPLIT ? 384 : T_SFA, tSFB = SPLIT ? 392 : T_SFB;
   static_assert(!SPLIT || tSFB + 8 * NK <= TMEM_COLS, "TMEM columns of the split layout");
-  constexpr int oK = OFF_K, oV = OFF_V, oSTAT = OFF_STAT, oRCP = OFF_RCP, oPTAB = OFF_PTAB, oMROW = OFF_MROW;
+  constexpr int oK = OFF_K, oV = OFF_V, oSTAT = OFF_STAT, oRCP = OFF_RCP, oMROW = OFF_MROW;
   constexpr int oBAR = OFF_BAR;
   constexpr int nV = NV;
   auto tr = [&](uint32_t uc, int slot, int j) {
@@ -205,7 +204,6 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   float* stat_l = stat_m + NWG * 128;
   float* stat_r = stat_m + 2 * NWG * 128;
   float* rcp = reinterpret_cast<float*>(sm + oRCP);
-  uint2* ptab = reinterpret_cast<uint2*>(sm + oPTAB);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + oBAR);
   uint64_t* q_full = bar + 0;
   uint64_t* q_empty = bar + 1;
@@ -254,7 +252,6 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     // correctly rounded 1/s for every non-negative E4M3 scale byte (0 -> 0, get_reciprocal)
     const float s = e4m3_to_f32((uint8_t)threadIdx.x);
     rcp[threadIdx.x] = s == 0.0f ? 0.0f : __frcp_rn(s);
-    ptab[threadIdx.x] = make_uint2(__float_as_uint(rcp[threadIdx.x]), e4m3_f16x2((uint32_t)threadIdx.x));
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -610,8 +607,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           if (lim < col0 + 31) chunk_p_dual<true>(a, gk, col0, lim, u2, nmu2, smem_u32(rcp), r6, rg, gr, lsum2, pk);
           else chunk_p_dual<false>(a, gk, col0, lim, u2, nmu2, smem_u32(rcp), r6, rg, gr, lsum2, pk);
         } else {
-          if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, smem_u32(ptab), r6, lsum2, pk);
-          else chunk_p<false>(a, gk, col0, lim, u2, nmu2, smem_u32(ptab), r6, lsum2, pk);
+          if (lim < col0 + 31) chunk_p<true>(a, gk, col0, lim, u2, nmu2, r6, lsum2, pk);
+          else chunk_p<false>(a, gk, col0, lim, u2, nmu2, r6, lsum2, pk);
         }
         if (leader && q == 0) tr(uc, TR_COMP, j);
         // the previous unit's O is written while its last PV finishes, after this unit's
@@ -651,184 +648,6 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       pend_off = qpos < p.T ? (((int64_t)un.b * p.T + qpos) * p.Hq + un.h) * HD + col0 : -1;
     }
     if (pend) epilogue();
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
-}
-
-// ------------------------------------------------------------ row maxima
-// fp4_rowmax_kernel: the exact row maximum of z = (Q K^T) * gk for every query
-// row of every unit, written to p.row_max; the attention kernel's PRE
-// instantiation reads it instead of running its own max pass.  The scores are
-// the same tcgen05 kind::mxf4nvf4 products of the same operands with the same
-// instruction shape (M=128, N=128, K=64), and z is formed and reduced by the
-// same chunk_max, so the maxima are bit for bit the ones the two-pass kernel
-// finds.  The kernel does nothing else, so three S buffers rotate in TMEM and
-// the QK^T of the next tiles overlaps the reduction of the current one.  As in
-// the attention kernel, a wait that gives up records its site and returns, and
-// every thread carries on through the same barriers, so the kernel ends.
-namespace rmx {
-constexpr int NS = 3;   // S buffers (and K scale-atom slots, one per buffer)
-constexpr int NK = 8;   // K stages: enough copies in flight to cover their latency at this kernel's pace
-constexpr int NWG = 4;  // max warpgroups; warpgroup q owns key columns 32q .. 32q+31
-constexpr int THREADS = 128 + NWG * 128;
-constexpr int Q_STAGE = 10240;  // Q codes 8 KB + scale atoms 1 KB; two stages (the next unit's Q lands early)
-constexpr int OFF_Q = 0, OFF_QSF = 8192;
-constexpr int K_STAGE = 10240;  // codes 8 KB, scale atoms 1 KB, gk 512 B
-constexpr int OFF_K = 2 * Q_STAGE;
-constexpr int OFF_STAT = OFF_K + NK * K_STAGE;     // [2][NWG][128] partial maxima
-constexpr int OFF_BAR = OFF_STAT + 2 * NWG * 128 * 4;
-// 116 KB: more than half of an SM's shared memory, so one CTA per SM (each
-// holds all 512 TMEM columns)
-constexpr int SMEM_BYTES = 116 * 1024;
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t T_SFA = NS * 128, T_SFB = T_SFA + 16;  // Q scale atoms per Q stage, K per S buffer
-static_assert(T_SFB + 8 * NS <= TMEM_COLS, "TMEM columns");
-static_assert(OFF_BAR + 256 + 1024 <= SMEM_BYTES, "shared memory map");
-}  // namespace rmx
-
-__global__ void __launch_bounds__(rmx::THREADS, 1)
-    fp4_rowmax_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, AttnArgs p) {
-  using namespace rmx;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* stat = reinterpret_cast<float*>(sm + OFF_STAT);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* q_full = bar + 0;        // [2]
-  uint64_t* q_empty = bar + 2;       // [2]
-  uint64_t* k_full = bar + 4;        // [NK]
-  uint64_t* k_empty = k_full + NK;   // [NK]
-  uint64_t* s_full = k_empty + NK;   // [NS]
-  uint64_t* s_free = s_full + NS;    // [NS]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + NS);
-  static_assert(4 + 2 * NK + 2 * NS + 1 <= 32, "barriers exceed their 256-byte slot");
-  const int warp = threadIdx.x / 32;
-  const int group = p.Hq / p.Hkv;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-    }
-    for (int i = 0; i < NK; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1 + 4 * NWG);  // MMA commit + every max warp (they read gk)
-    }
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4 * NWG);
-    }
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  if (warp == 0) {
-    if (elect_one_lane()) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      uint32_t kc = 0, uc = 0;
-      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
-        const Unit un = unit_of(u, p);
-        const int n = kv_tiles(un, p);
-        const int hq = p.hq0 + un.h, hk = p.hk0 + un.h / group;
-        const int qrow = un.b * p.Tp + un.qt * attn::BM;
-        const int qb = uc & 1;
-        uint8_t* qs = sm + OFF_Q + qb * Q_STAGE;
-        if (uc >= 2) mbar_wait(&q_empty[qb], ((uc >> 1) - 1) & 1, 0x501);
-        mbar_arrive_expect_tx(&q_full[qb], attn::Q_BYTES + 1024);
-        tma_load_2d(qs, &tmQ, &q_full[qb], hq * (attn::HD / 2), qrow);
-        bulk_load(qs + OFF_QSF, p.qsf + ((int64_t)(qrow / 128) * p.nkb4q + 2 * hq) * 512, 1024, &q_full[qb]);
-        for (int j = 0; j < n; ++j, ++kc) {
-          const int s = kc % NK;
-          if (kc >= NK) mbar_wait(&k_empty[s], ((kc / NK) - 1) & 1, 0x502);
-          uint8_t* ks = sm + OFF_K + s * K_STAGE;
-          const int krow = un.b * p.Tp + j * attn::BN;
-          mbar_arrive_expect_tx(&k_full[s], 8192 + 1024 + 512);
-          tma_load_2d(ks, &tmK, &k_full[s], hk * (attn::HD / 2), krow);
-          bulk_load(ks + 8192, p.ksf + ((int64_t)(krow / 128) * p.nkb4k + 2 * hk) * 512, 1024, &k_full[s]);
-          bulk_load(ks + 9216, p.gk + krow, 512, &k_full[s]);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (elect_one_lane()) {
-      const uint32_t idq = idesc_nvf4(attn::BM, attn::BN);
-      uint32_t kc = 0, uc = 0, tc = 0;
-      for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
-        const Unit un = unit_of(u, p);
-        const int n = kv_tiles(un, p);
-        const int qb = uc & 1;
-        uint8_t* qs = sm + OFF_Q + qb * Q_STAGE;
-        const uint32_t sfa = tmem + T_SFA + 8 * qb;
-        mbar_wait(&q_full[qb], (uc >> 1) & 1, 0x503);
-        tc_fence_after();
-        tmem_cp_sf_atom(sfa, smem_desc(smem_u32(qs + OFF_QSF), 16, 128, kSwizzleNone));
-        tmem_cp_sf_atom(sfa + 4, smem_desc(smem_u32(qs + OFF_QSF + 512), 16, 128, kSwizzleNone));
-        for (int j = 0; j < n; ++j, ++kc, ++tc) {
-          const int b = tc % NS, s = kc % NK;
-          if (tc >= NS) mbar_wait(&s_free[b], ((tc / NS) - 1) & 1, 0x504);
-          mbar_wait(&k_full[s], (kc / NK) & 1, 0x505);
-          tc_fence_after();
-          uint8_t* ks = sm + OFF_K + s * K_STAGE;
-          const uint32_t sfb = tmem + T_SFB + 8 * b;
-          tmem_cp_sf_atom(sfb, smem_desc(smem_u32(ks + 8192), 16, 128, kSwizzleNone));
-          tmem_cp_sf_atom(sfb + 4, smem_desc(smem_u32(ks + 8192 + 512), 16, 128, kSwizzleNone));
-#pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            const uint64_t ad = smem_desc(smem_u32(qs) + kk * 32, 16, 512, kSwizzle64B);
-            const uint64_t bd = smem_desc(smem_u32(ks) + kk * 32, 16, 512, kSwizzle64B);
-            mma_nvf4(tmem + 128 * b, ad, bd, idq, sfa + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
-          }
-          tc_commit(&k_empty[s]);
-          tc_commit(&s_full[b]);
-        }
-        tc_commit(&q_empty[qb]);
-      }
-    }
-  } else if (warp >= 4) {
-    const int q = (warp - 4) >> 2;
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + (threadIdx.x & 31);
-    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const bool wlead = (threadIdx.x & 31) == 0;
-    const int col0 = 32 * q;
-    uint32_t kc = 0, uc = 0, tc = 0;
-    for (int i = 0, u = cta_unit(0, p.units); u >= 0; u = cta_unit(++i, p.units), ++uc) {
-      const Unit un = unit_of(u, p);
-      const int n = kv_tiles(un, p);
-      float m = -INFINITY;
-      for (int j = 0; j < n; ++j, ++kc, ++tc) {
-        const int b = tc % NS, s = kc % NK;
-        mbar_wait(&s_full[b], (tc / NS) & 1, 0x506);
-        tc_fence_after();
-        uint32_t a[32];
-        tmem_ld32(tmem + lane_base + 128 * b + col0, a);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (wlead) mbar_arrive(&s_free[b]);
-        const uint32_t gk = smem_u32(sm + OFF_K + s * K_STAGE + 9216) + 4 * col0;
-        const int lim = (p.causal && j == un.qt) ? r : (p.T - 1 - j * attn::BN);
-        if (lim < col0 + 31) m = chunk_max<true>(a, gk, col0, lim, m);
-        else m = chunk_max<false>(a, gk, col0, lim, m);
-        __syncwarp();
-        if (wlead) mbar_arrive(&k_empty[s]);
-      }
-      float* st = stat + (uc & 1) * NWG * 128;
-      st[q * 128 + r] = m;
-      named_bar(1, NWG * 128);
-      if (q == 0) {
-#pragma unroll
-        for (int w = 1; w < NWG; ++w) m = fmaxf(m, st[w * 128 + r]);
-        p.row_max[((int64_t)un.b * p.HqT + p.hq0 + un.h) * p.Tp + un.qt * attn::BM + r] = m;
-      }
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1234,8 +1053,7 @@ int fp4::launch_attention(const AttnLaunch& L, cudaStream_t st) {
   a.causal = L.causal ? 1 : 0;
   a.scale_log2 = L.scaling * 1.4426950408889634f;
   a.units = B * a.Hq * (Tp / 128);
-  // the event timeline is recorded by the single-slice kernel only
-  // the event timeline is recorded by the single-slice kernel only
+  // the event timeline is recorded by the one-group single-slice kernel only
   a.trace = (dq || dual_p) ? nullptr : g_trace;
   using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                         AttnArgs);
@@ -1253,16 +1071,18 @@ int fp4::launch_attention(const AttnLaunch& L, cudaStream_t st) {
   int grid = L.num_ctas > 0 ? L.num_ctas : sms;
   if (grid > a.units) grid = a.units;
   if (pre) {
-    static const bool groups = env_on("FP4ATTN_ROWMAX_GROUPS");
-    if (groups) {
-      if (int e = set_smem_attr((const void*)fp4_rowmax_groups_kernel, rmg::SMEM_BYTES)) return e;
-      fp4_rowmax_groups_kernel<<<grid, rmg::THREADS, rmg::SMEM_BYTES, st>>>(mq, mk, a);
-      if (int e = check_launch("fp4_rowmax_groups_kernel")) return e;
-    } else {
-      if (int e = set_smem_attr((const void*)fp4_rowmax_kernel, rmx::SMEM_BYTES)) return e;
-      fp4_rowmax_kernel<<<grid, rmx::THREADS, rmx::SMEM_BYTES, st>>>(mq, mk, a);
-      if (int e = check_launch("fp4_rowmax_kernel")) return e;
-    }
+    // K codes two key tiles per box, and a 32-bit view of the K scale atoms ([B*Tp/128] row blocks of
+    // HkvT * 1024 bytes) boxed two row blocks at a time
+    CUtensorMap mk2, mksf;
+    if (int e = encode_tiled_2d(&mk2, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.k_codes, (uint64_t)HkvT * (HD / 2),
+                                (uint64_t)B * Tp, (uint64_t)HkvT * (HD / 2), HD / 2, 256, CU_TENSOR_MAP_SWIZZLE_64B))
+      return e;
+    if (int e = encode_tiled_2d(&mksf, CU_TENSOR_MAP_DATA_TYPE_UINT32, L.k_scales, (uint64_t)HkvT * 256,
+                                (uint64_t)B * Tp / 128, (uint64_t)HkvT * 1024, 256, 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return e;
+    if (int e = set_smem_attr((const void*)fp4_rowmax_t_kernel, rmt::SMEM_BYTES)) return e;
+    fp4_rowmax_t_kernel<<<grid, rmt::THREADS, rmt::SMEM_BYTES, st>>>(mq, mk2, mksf, a);
+    if (int e = check_launch("fp4_rowmax_t_kernel")) return e;
     if (!dual_p && !a.trace && pingpong_enabled()) {
       if (int e = set_smem_attr((const void*)fp4_attn_pingpong_kernel, pp::SMEM_BYTES)) return e;
       fp4_attn_pingpong_kernel<<<grid, pp::THREADS, pp::SMEM_BYTES, st>>>(mq, mk, mvh, mvl, a);

@@ -4,7 +4,7 @@
 //
 // Same computation as fp4_attn_kernel with precomputed row maxima
 // (llama_patch.py:57-105 on the NVFP4 operands of llama_patch.py:167-196):
-// e = exp2(z*u - m*u) with the exact row maximum m from fp4_rowmax_kernel, the
+// e = exp2(z*u - m*u) with the exact row maximum m from fp4_rowmax_t_kernel, the
 // row sum l = sum e, P-hat = NVFP4 fake-quant of e per 16 keys (E4M3 block
 // scale, E2M1 round-to-nearest-even), O = (P-hat V-hat) / l.  The chunk
 // arithmetic is chunk_p, so a key tile's P-hat is bit for bit the one
@@ -18,7 +18,14 @@
 // its own S buffer in TMEM, so one group computes while the other loads its
 // scores or stores its P-hat, and the tensor pipe sees QK and PV of both.
 // P-hat has one TMEM buffer: a group stores tile t's P-hat once PV(t-1) has
-// read the previous one, so PV runs strictly in tile order.
+// read the previous one, so PV runs strictly in tile order.  (Handing P-hat
+// over in two halves of 64 keys, so that the next tile's first half is stored
+// while PV still runs on the second, measured slower: the extra wait costs the
+// PV thread more than the overlap gains.)  The tensor pipe is what bounds the kernel
+// (8 kind::f16 MMAs of ~100 cycles per tile for PV, 2 mxf4nvf4 MMAs and 2
+// scale-atom copies for QK), so each tile carries only the commits it needs:
+// the PV thread releases the K stage (the group is done with its gk when it
+// hands over P-hat), and P-hat's release also frees the V-hat stage.
 //
 // TMEM: S0 [0,128), S1 [128,256), O [256,384), P-hat [384,448) (fp16; keys
 // 32c .. 32c+31 at columns 16c .. 16c+15), Q scale atoms per Q stage from
@@ -50,8 +57,7 @@ constexpr int V_HALF = HD * 64 * 2;  // 128 channels x 64 keys x fp16 (one TMA b
 constexpr int V_STAGE = 4 * V_HALF;  // keys 0-63 hi, lo; keys 64-127 hi, lo
 constexpr int OFF_V = OFF_K + NK * K_STAGE;
 constexpr int OFF_L = OFF_V + NV * V_STAGE;         // [NL][4 partials][128 rows] fp32
-constexpr int OFF_PTAB = OFF_L + NL * 4 * 128 * 4;  // per E4M3 scale byte: (1/s, s as an fp16 pair)
-constexpr int OFF_BAR = OFF_PTAB + 128 * 8;
+constexpr int OFF_BAR = OFF_L + NL * 4 * 128 * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t T_S = 0, T_O = 256, T_P = 384, T_SFA = 448, T_SFB = T_SFA + 8 * NQ;
@@ -68,24 +74,23 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* lpart = reinterpret_cast<float*>(sm + OFF_L);
-  uint2* ptab = reinterpret_cast<uint2*>(sm + OFF_PTAB);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bar;              // [NQ]
   uint64_t* q_empty = q_full + NQ;     // [NQ] MMA commit + every softmax warp (they read g and m)
   uint64_t* k_full = q_empty + NQ;     // [NK]
-  uint64_t* k_empty = k_full + NK;     // [NK] MMA commit + the PV thread for the softmax warps
+  uint64_t* k_empty = k_full + NK;     // [NK] the PV thread, for the softmax warps (their last gk read)
   uint64_t* v_full = k_empty + NK;     // [NV]
-  uint64_t* v_empty = v_full + NV;     // [NV]
-  uint64_t* s_full = v_empty + NV;     // [2] per group: its S buffer written
+  uint64_t* s_full = v_full + NV;      // [2] per group: its S buffer written
   uint64_t* s_free = s_full + 2;       // [2] per group: every warp of the group has loaded it
   uint64_t* p_full = s_free + 2;       // [2] per tile parity: the group stored its P-hat
-  uint64_t* p_free = p_full + 2;       // [2] per tile parity: PV has read that P-hat
+  uint64_t* p_free = p_full + 2;       // [2] per tile parity: PV has read that P-hat (and its V-hat stage)
   uint64_t* o_full = p_free + 2;       // a unit's last PV finished
   uint64_t* o_free = o_full + 1;       // every softmax warp has read O
   uint64_t* l_full = o_free + 1;       // [NL] every softmax warp wrote its row-sum partial
   uint64_t* l_free = l_full + NL;      // [NL] every softmax warp read the slot
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(l_free + NL);
-  static_assert(4 * NQ / 2 + 2 * NK + 2 * NV + 10 + 2 * NL + 1 <= 64, "barriers exceed their 512-byte slot");
+  static_assert(2 * NQ + 2 * NK + NV + 10 + 2 * NL + 1 <= 64, "barriers exceed their 512-byte slot");
+  static_assert(NV == 2, "a V-hat stage is released with the P-hat of the same tile parity");
 
   const int warp = threadIdx.x / 32;
   const int group = p.Hq / p.Hkv;  // query heads per KV head
@@ -96,15 +101,14 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
     }
     for (int i = 0; i < NK; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 2);
+      mbar_init(&k_empty[i], 1);
     }
-    for (int i = 0; i < NV; ++i) {
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-    }
+    for (int i = 0; i < NV; ++i) mbar_init(&v_full[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], GW);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], GW);
       mbar_init(&p_free[i], 1);
     }
@@ -115,11 +119,6 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
       mbar_init(&l_free[i], 2 * GW);
     }
     fence_barrier_init();
-  }
-  if (threadIdx.x < 128) {
-    // correctly rounded 1/s for every non-negative E4M3 scale byte (0 -> 0, get_reciprocal), and s as fp16 pair
-    const float s = e4m3_to_f32((uint8_t)threadIdx.x);
-    ptab[threadIdx.x] = make_uint2(__float_as_uint(s == 0.0f ? 0.0f : __frcp_rn(s)), e4m3_f16x2((uint32_t)threadIdx.x));
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -174,7 +173,7 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
         const bool lo = un.qt < p.pv_lo_tiles;  // the lo plane only where PV reads it
         for (int j = 0; j < n; ++j, ++vc) {
           const int vs = vc % NV;
-          if (vc >= NV) mbar_wait(&v_empty[vs], ((vc / NV) - 1) & 1, 0x603);
+          if (vc >= NV) mbar_wait(&p_free[vs], ((vc / NV) - 1) & 1, 0x603);
           uint8_t* v = sm + OFF_V + vs * V_STAGE;
           mbar_arrive_expect_tx(&v_full[vs], lo ? V_STAGE : V_STAGE / 2);
 #pragma unroll
@@ -216,7 +215,6 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
             const uint64_t bd = smem_desc(smem_u32(ks) + kk * 32, 16, 512, kSwizzle64B);
             mma_nvf4(tmem + T_S + 128 * g, ad, bd, idq, sfa + 4 * kk, sfb + 4 * kk, kk > 0 ? 1u : 0u);
           }
-          tc_commit(&k_empty[s]);
           tc_commit(&s_full[g]);
         }
         tc_commit(&q_empty[qs]);
@@ -237,7 +235,7 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
           const int par = t & 1, vs = t % NV;
           mbar_wait(&v_full[vs], (t / NV) & 1, 0x621);
           mbar_wait(&p_full[par], (t >> 1) & 1, 0x622);
-          mbar_arrive(&k_empty[t % NK]);  // the group is done with the stage's gk
+          mbar_arrive(&k_empty[t % NK]);  // P-hat stored: the group is done with the stage's gk
           if (j == 0 && uc > 0) mbar_wait(o_free, (uc - 1) & 1, 0x623);
           tc_fence_after();
           const uint32_t v = smem_u32(sm + OFF_V + vs * V_STAGE);
@@ -250,7 +248,6 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
                          (j > 0 || kk > 0 || part > 0) ? 1u : 0u);
             }
           }
-          tc_commit(&v_empty[vs]);
           tc_commit(&p_free[par]);
         }
         tc_commit(o_full);
@@ -268,7 +265,6 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
     const float r6 = __frcp_rn(6.0f);
     const int c0 = 64 * half;  // first of this warp's two 32-key chunks
     const uint32_t s_cols = tmem + lane_base + T_S + 128 * grp;
-    const uint32_t ptab_s = smem_u32(ptab);
     const int part_idx = grp * 2 + half;  // this warp's row-sum partial
     uint32_t pend_lo = 0, pend_hi = 0;    // units [pend_lo, pend_hi) whose O this warp still writes
 
@@ -343,16 +339,16 @@ __global__ void __launch_bounds__(pp::THREADS, 1)
         uint32_t a[32], pk0[16], pk1[16];
         tmem_ld32(s_cols + c0, a);
         tmem_ld_wait();
-        if (lim < c0 + 31) chunk_p<true>(a, gk, c0, lim, u2, nmu2, ptab_s, r6, lsum2, pk0);
-        else chunk_p<false>(a, gk, c0, lim, u2, nmu2, ptab_s, r6, lsum2, pk0);
+        if (lim < c0 + 31) chunk_p<true>(a, gk, c0, lim, u2, nmu2, r6, lsum2, pk0);
+        else chunk_p<false>(a, gk, c0, lim, u2, nmu2, r6, lsum2, pk0);
         tmem_ld32(s_cols + c0 + 32, a);
         tmem_ld_wait();
         // both chunks are in registers: the group's S buffer may take S(tt + 2)
         tc_fence_before();
         __syncwarp();
         if (wlead) mbar_arrive(&s_free[grp]);
-        if (lim < c0 + 63) chunk_p<true>(a, gk + 128, c0 + 32, lim, u2, nmu2, ptab_s, r6, lsum2, pk1);
-        else chunk_p<false>(a, gk + 128, c0 + 32, lim, u2, nmu2, ptab_s, r6, lsum2, pk1);
+        if (lim < c0 + 63) chunk_p<true>(a, gk + 128, c0 + 32, lim, u2, nmu2, r6, lsum2, pk1);
+        else chunk_p<false>(a, gk + 128, c0 + 32, lim, u2, nmu2, r6, lsum2, pk1);
         // outputs of finished units first (their last PV precedes PV(tt - 1))
         while (pend_lo < pend_hi) epilogue(pend_lo++);
         // the P-hat buffer is free once PV(tt - 1) has read it

@@ -142,13 +142,6 @@ __device__ __forceinline__ void block_scale(const float* eb, uint32_t rcp, float
   s14 = (uint32_t)__half_as_ushort(__float2half_rn(e4m3_to_f32(sb) * 16384.0f)) * 0x10001u;
 }
 
-// The E4M3 scale byte b as an fp16 pair (exact: E4M3 values are fp16 values).
-__device__ __forceinline__ uint32_t e4m3_f16x2(uint32_t b) {
-  uint32_t r;
-  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(b * 0x101u));
-  return r;
-}
-
 // E2M1 round-to-nearest-even of (x0, x1) (satfinite), times the block scale:
 // the fp16 pair code * s, exact (P's block scales lie in [2^-9, 0.171875] or are 0).
 __device__ __forceinline__ uint32_t quant_pair_cvt(float x0, float x1, uint32_t s2) {
@@ -161,18 +154,30 @@ __device__ __forceinline__ uint32_t quant_pair_cvt(float x0, float x1, uint32_t 
   return hmul2_u32(c, s2);
 }
 
-// Block scale of 16 values of e from the per-byte table: 1/s as a packed pair
-// (rs2) and s as an fp16 pair (s2), one shared-memory load.
-__device__ __forceinline__ void block_scale_tab(const float* eb, uint32_t tab, float r6, uint64_t& rs2,
-                                                uint32_t& s2) {
+// The E4M3 scale byte b as an fp16 pair (exact: E4M3 values are fp16 values).
+__device__ __forceinline__ uint32_t e4m3_f16x2(uint32_t b) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(b * 0x101u));
+  return r;
+}
+
+// Block scale of 16 values of e without a table lookup (shared-memory loads
+// wait behind the tensor core's operand reads while MMAs run): the scale as an
+// fp16 pair (s2, exact) and 1/s by the hardware reciprocal (rs2; 0 for a zero
+// block, as get_reciprocal gives).  1/s is within an ulp or two of the
+// correctly rounded reciprocal the reference multiplies by, which moves only
+// E2M1 decisions lying within ~1e-7 of a rounding boundary.
+__device__ __forceinline__ void block_scale_rcp(const float* eb, float r6, uint64_t& rs2, uint32_t& s2) {
   const float m0 = max3f(eb[0], eb[1], eb[2]), m1 = max3f(eb[3], eb[4], eb[5]);
   const float m2 = max3f(eb[6], eb[7], eb[8]), m3 = max3f(eb[9], eb[10], eb[11]);
   const float m4 = max3f(eb[12], eb[13], eb[14]);
   const float amax = fmaxf(max3f(m0, m1, m2), max3f(m3, m4, eb[15]));
-  const uint2 t = lds_u2(tab + 8 * (e4m3_satfinite(amax * r6) & 127));
-  const float rs = __uint_as_float(t.x);
+  s2 = e4m3_f16x2(e4m3_satfinite(amax * r6) & 127);
+  const float sv = __half2float(__ushort_as_half((unsigned short)(s2 & 0xFFFFu)));
+  float rs;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rs) : "f"(sv));
+  rs = sv == 0.0f ? 0.0f : rs;
   rs2 = pk2(rs, rs);
-  s2 = t.y;
 }
 
 // Pass 2 on one 32-key chunk: e = exp2(z*u - m*u), running sum, NVFP4
@@ -181,8 +186,7 @@ __device__ __forceinline__ void block_scale_tab(const float* eb, uint32_t tab, f
 // MUFU and the conversion pipe work at the same time.
 template <bool MASK>
 __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], uint32_t gk, int col0, int lim, uint64_t u2,
-                                        uint64_t nmu2, uint32_t tab, float r6, uint64_t (&lsum2)[4],
-                                        uint32_t (&pk)[16]) {
+                                        uint64_t nmu2, float r6, uint64_t (&lsum2)[4], uint32_t (&pk)[16]) {
   float e[32];
 #pragma unroll
   for (int q = 0; q < 4; ++q) exp4(a + 4 * q, lds_f4(gk + 16 * q), u2, nmu2, e + 4 * q);
@@ -192,7 +196,7 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], uint32_t gk, in
   }
   uint64_t rs2;
   uint32_t s2;
-  block_scale_tab(e, tab, r6, rs2, s2);
+  block_scale_rcp(e, r6, rs2, s2);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     exp4(a + 16 + 4 * q, lds_f4(gk + 64 + 16 * q), u2, nmu2, e + 16 + 4 * q);
@@ -207,7 +211,7 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&a)[32], uint32_t gk, in
 #pragma unroll
     for (int i = 16; i < 32; ++i) e[i] = (col0 + i > lim) ? 0.0f : e[i];
   }
-  block_scale_tab(e + 16, tab, r6, rs2, s2);
+  block_scale_rcp(e + 16, r6, rs2, s2);
 #pragma unroll
   for (int i = 16; i < 32; i += 2) {
     float x0, x1;

@@ -206,14 +206,18 @@ __global__ void __launch_bounds__(gemm::THREADS, 2)
 
 // Persistent 128x256 tiles: one CTA per SM walks the tiles t = blockIdx.x, + gridDim.x, ... (M
 // tile fastest, so consecutive tiles share the B block and the CTAs in flight share all of A in L2).
-// Warp 0 runs the TMA ring ahead across tile boundaries, warp 1 issues the MMAs, and eight
-// epilogue warps (two per TMEM lane quarter, one per 128-column half) move the accumulator into
-// registers, hand it back to the MMA warp at once (acc_empty) and scale and store while the next
-// tile's main loop runs.
+// Warp 0 runs the TMA ring ahead across tile boundaries, warp 2 copies each stage's twelve scale
+// atoms into TMEM, warp 1 issues the MMAs, and eight epilogue warps (two per TMEM lane quarter,
+// one per 128-column half) move the accumulator into registers, hand it back to the MMA warp at
+// once (acc_empty) and scale and store while the next tile's main loop runs.  The atom copies
+// have their own warp because the tensor pipe takes them in issue order from one thread (~50
+// cycles each, twelve per stage against four ~134-cycle MMAs) but overlaps them with another
+// thread's MMAs (measured: 64 copies from a second warp leave a stream of 64 MMAs unslowed); the
+// copier commits sf_full[s] once a stage's atoms are in TMEM, which the MMA warp waits for.
 namespace gemmp {
 constexpr int NB = 2, BN = 256, STAGES = 4;
-constexpr int THREADS = 64 + 256;
-constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 96 + 256;
+constexpr int EPI_WARPS = 8;  // warps 3..10
 constexpr int A_BYTES = gemm::BM * gemm::BK / 2, B_BYTES = BN * gemm::BK / 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + (1 + NB) * gemm::SF_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
@@ -234,7 +238,9 @@ __global__ void __launch_bounds__(gemmp::THREADS, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drained = acc_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+  uint64_t* sf_full = drained + 1;        // [STAGES] the stage's scale atoms are in TMEM (copier's commit)
+  uint64_t* cp_drained = sf_full + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cp_drained + 1);
   // set when a wait gave up; every role then stops at its next tile boundary
   volatile uint32_t* failed = tmem_slot + 1;
 
@@ -252,6 +258,8 @@ __global__ void __launch_bounds__(gemmp::THREADS, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, EPI_WARPS);
     mbar_init(drained, 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&sf_full[s], 1);
+    mbar_init(cp_drained, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -301,21 +309,14 @@ __global__ void __launch_bounds__(gemmp::THREADS, 1)
       tc_fence_after();
       for (int k = 0; k < ksteps; ++k, ++it) {
         const int s = it % STAGES;
-        if (!mbar_wait(&full[s], (it / STAGES) & 1, 0x113)) {
+        // the copier waited for the stage's TMA before its atom copies: their commit covers both
+        if (!mbar_wait(&sf_full[s], (it / STAGES) & 1, 0x113)) {
           ok = false;
           break;
         }
         tc_fence_after();
         uint8_t* st = smem + s * STAGE_BYTES;
         const uint32_t sfa_t = tmem + BN + s * SF_COLS, sfb_t = sfa_t + 16;
-#pragma unroll
-        for (int a = 0; a < 4; ++a) {
-          tmem_cp_sf_atom(sfa_t + 4 * a, smem_desc(smem_u32(st + A_BYTES + B_BYTES + a * 512), 16, 128, kSwizzleNone));
-          tmem_cp_sf_atom(sfb_t + 8 * a,
-                          smem_desc(smem_u32(st + A_BYTES + B_BYTES + SF_BYTES + a * 512), 16, 128, kSwizzleNone));
-          tmem_cp_sf_atom(sfb_t + 8 * a + 4,
-                          smem_desc(smem_u32(st + A_BYTES + B_BYTES + 2 * SF_BYTES + a * 512), 16, 128, kSwizzleNone));
-        }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint64_t ad = smem_desc(smem_u32(st) + kk * 32, 16, 1024, kSwizzle128B);
@@ -335,9 +336,41 @@ __global__ void __launch_bounds__(gemmp::THREADS, 1)
     // no MMA of this CTA is in flight when TMEM is released, on every path
     tc_commit(drained);
     mbar_wait(drained, 0, 0x115);
-  } else if (warp >= 2) {
+  } else if (warp == 2) {
+    // ------------------------------------------------- scale atoms: shared memory -> TMEM
+    if (elect_one_lane()) {
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles && !*failed; t += gridDim.x) {
+        for (int k = 0; k < ksteps; ++k, ++it) {
+          const int s = it % STAGES;
+          // the TMA for this use of the stage is issued only after the MMAs of its previous use
+          // (empty[s]), so the stage's TMEM atom slot is free once the stage is full
+          if (!mbar_wait(&full[s], (it / STAGES) & 1, 0x116)) {
+            *failed = 1u;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = smem + s * STAGE_BYTES;
+          const uint32_t sfa_t = tmem + BN + s * SF_COLS, sfb_t = sfa_t + 16;
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            tmem_cp_sf_atom(sfa_t + 4 * a, smem_desc(smem_u32(st + A_BYTES + B_BYTES + a * 512), 16, 128, kSwizzleNone));
+            tmem_cp_sf_atom(sfb_t + 8 * a,
+                            smem_desc(smem_u32(st + A_BYTES + B_BYTES + SF_BYTES + a * 512), 16, 128, kSwizzleNone));
+            tmem_cp_sf_atom(sfb_t + 8 * a + 4,
+                            smem_desc(smem_u32(st + A_BYTES + B_BYTES + 2 * SF_BYTES + a * 512), 16, 128,
+                                      kSwizzleNone));
+          }
+          tc_commit(&sf_full[s]);
+        }
+      }
+      // no copy of this CTA is in flight when TMEM is released
+      tc_commit(cp_drained);
+      mbar_wait(cp_drained, 0, 0x117);
+    }
+  } else if (warp >= 3) {
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - 3) >> 2;
     const int row = quarter * 32 + (threadIdx.x & 31);
     const bool vec_out = p.ldc % 4 == 0 && (uintptr_t)p.c % 16 == 0 && (uintptr_t)p.gb % 16 == 0;
     int nt = 0;

@@ -7,14 +7,15 @@
 // key.  Here the cache holds the packed NVFP4 data of those same values:
 //   K: codes [B][Hkv][Tmax][D/2], E4M3 scales per 16 dims [B][Hkv][Tmax][D/16],
 //      per-token global scale g_k [B][Tmax] (row mode on the [B*q, Hkv*D] view);
-//   V: codes [B][Hkv][Tmax][D/2], one E4M3 scale byte per element
-//      [B][Hkv][Tmax][D] (V's blocks of 16 run along the tokens of the call that
-//      appended them, so a token's scale is per channel), per-token g_v [B][Tmax];
-//      optionally the same scales once per 16-token group [B][Hkv][Tmax/16][D]
-//      for a prefix of len16 tokens whose groups each came from one block (a
-//      call that started on a group boundary with whole blocks per sequence).
-//      Chunks of 256 keys inside that prefix read the 2 KB of group scales
-//      instead of 32 KB of per-element scales.
+//   V, dim-major: codes [B][Hkv][D][Tmax/2] (byte j of a channel holds
+//      tokens 2j and 2j+1, the first in the low nibble), one E4M3 scale byte
+//      per element [B][Hkv][D][Tmax] (V's blocks of 16 run along the tokens of
+//      the call that appended them, so a token's scale is per channel),
+//      per-token g_v [B][Tmax]; optionally the same scales once per 16-token
+//      group [B][Hkv][D][Tmax/16] for a prefix of len16 tokens whose groups
+//      each came from one block (a call that started on a group boundary with
+//      whole blocks per sequence).  Chunks of 256 keys inside that prefix read
+//      the 2 KB of group scales instead of 32 KB of per-element scales.
 // Tmax is a multiple of 256, so every chunk of 256 keys is whole in memory.
 // The query comes in the same packed form (row mode on its [B, Hq*D] view):
 // codes [B][Hq*D/2], E4M3 scales [B][Hq*D/16], g_q [B].
@@ -26,11 +27,12 @@
 //    mma.sync m16n8k16 (fp16 products exact, fp32 accumulate; the query heads
 //    of the KV head are the MMA rows, 8 keys its columns), write S and fold
 //    each row's maximum into an order-free atomic maximum;
-//  * pv: the same ring over V and S; the exact row max, e = exp2((S - m)
-//    log2 e), the NVFP4 fake-quant of e per 16 keys (as the prefill kernel
-//    does), then O-partial^T = (code*scale)_v^T (P-hat * g_v)^T on mma.sync
-//    m16n8k16 (V-hat exact in fp16; P-hat * g_v as fp16 hi + lo, since V's
-//    per-token g_v is not exact in fp16), fp32 accumulate;
+//  * pv: a ring of V (a TMA tile of 128 channels x 256 keys), S and g_v;
+//    the exact row max, e = exp2((S - m) log2 e), the NVFP4 fake-quant of e
+//    per 16 keys (as the prefill kernel does), then O-partial^T =
+//    (code*scale)_v^T (P-hat * g_v)^T on tcgen05 kind::f16 with V-hat in
+//    TMEM (exact in fp16) and P-hat * g_v as fp16 hi + lo rows in shared
+//    memory (V's per-token g_v is not exact in fp16), fp32 accumulate in TMEM;
 //  * combine: O = sum O-partial / sum l over the chunks, in a fixed order.
 #include <stdint.h>
 
@@ -40,6 +42,7 @@
 #include "fp4attn.h"
 #include "sm100.cuh"
 #include "status.h"
+#include "tmap.h"
 
 namespace fp4 {
 
@@ -59,37 +62,6 @@ constexpr uint32_t SC_KS = DK_KEYS * DK_D / 16;
 constexpr uint32_t SC_KG = DK_KEYS * 4;
 constexpr uint32_t SC_STAGE = SC_KC + SC_KS + SC_KG;
 constexpr int SC_STAGES = 3;
-// pv stage: V codes | V scales | g_v | S of the G heads
-constexpr uint32_t PV_VC = DK_KEYS * DK_D / 2;
-constexpr uint32_t PV_VS16 = DK_KEYS / 16 * DK_D;  // V scales of a chunk, one row per 16-token group
-constexpr uint32_t PV_VG = DK_KEYS * 4;
-constexpr uint32_t PV_S1 = DK_KEYS * 4;  // S of one head
-// MG bounds the query heads per KV head (NT = MG/8 rounded up MMA n-tiles of
-// 8 heads).  Dynamic shared memory: the ring, then P-hat * g_v * 2^E as fp16
-// hi and lo rows [2*MG][PV_PH_LD] (keys in MMA k order), then each warp's
-// partial O [DK_WARPS][MG][PV_PART_LD] (dim 16g + c at position c*8 + g).
-constexpr int PV_PART_LD = 132;  // 4 mod 16 floats: the fragment stores hit 32 distinct banks
-constexpr int PV_PH_LD = DK_KEYS + 8;  // fp16 P-hat row: 132 words, so the 8 heads of a B load hit 32 banks
-// NW consumer warps: warp w owns KPW = 256 / NW keys of an item (KSTEPS MMA
-// k-steps of 16); with 16 warps the two half-warps split the heads in phase e.
-template <int MG, int NW>
-struct PvCfg {
-  static constexpr int NT = (MG + 7) / 8;
-  static constexpr int KPW = DK_KEYS / NW;
-  static constexpr int KSTEPS = KPW / 16;
-  static constexpr int LG = 32 / KPW;  // lane groups sharing a key in phase e
-  static constexpr int THREADS = (NW + 1) * 32;
-  // 4 heads per KV head: three stages fit two CTAs on an SM
-  static constexpr int STAGES = MG == 8 ? 4 : 3;
-  static constexpr uint32_t STAGE = PV_VC + PV_VS16 + PV_VG + MG * PV_S1;
-  static constexpr uint32_t RING = STAGES * STAGE;
-  static constexpr uint32_t PH = 2 * MG * PV_PH_LD * 2;
-  static constexpr uint32_t PART = NW * MG * PV_PART_LD * 4;
-  static constexpr uint32_t SMEM = RING + PH + PART;
-  static_assert(KPW == 16 || KPW == 32, "a warp covers one or two 16-key steps");
-  static_assert(SMEM + 2048 <= 232448, "shared memory");
-};
-
 struct DecodeArgs {
   const uint8_t* q_codes;   // [B][Hq*D/2]
   const uint8_t* q_scales;  // [B][Hq*D/16]
@@ -293,264 +265,349 @@ __global__ void __launch_bounds__(DK_THREADS) decode_scores_kernel(DecodeArgs p)
 }
 
 // -------------------------------------------------------------------- pv
-// Phase e: thread t handles key t of the item (e, the per-16-key NVFP4
-// fake-quant of e, P-hat * g_v), as the prefill kernel quantizes P.
-//
-// PV on mma.sync m16n8k16 (fp16 operands, fp32 accumulate), transposed:
-// O^T[dim][head] += V-hat^T[dim][key] * (P-hat g_v)^T[key][head].  Warp w owns
-// keys 32w..32w+31 of the item -- the keys its own phase-e threads produced,
-// so no CTA barrier sits between the phases -- as two k-steps of 16 keys.
-//  * A = V-hat = code * scale, exact in fp16 (E2M1 x E4M3 has at most five
-//    significant bits and lies in [2^-10, 2688]).  M index: m-tile mt, row g
-//    (g = lane/4) is dim 16g + 2mt, row g+8 dim 16g + 2mt + 1, so a lane's
-//    dims are one 8-byte run of codes and one 16-byte run of scales per key.
-//  * K index within a k-step: k = 8h + 2t + j (t = lane%4) is key 8h + 4j + t,
-//    so lane t's keys are t, t+4, t+8, t+12 and each load instruction reads
-//    four consecutive key rows (no bank conflicts).  The code nibbles of keys
-//    t and t+4 are merged into (key t, key t+4) bytes, which convert to the
-//    A register pairs directly.
-//  * B = P-hat * g_v as fp16 hi + lo (22 significant bits; g_v varies along
-//    the keys, so it cannot be factored out), scaled by a per-warp power of
-//    two 2^E that keeps the largest value below 2^15 (P-hat <= 1.03125 and
-//    g_v < 2^(e+1)); the partial O is scaled back by 2^-E, exactly.
-//  * N index: head 8nt + g (heads >= G are zero).
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
-}
+// O-partial^T[channel][head] = V-hat^T[channel][key] (P-hat g_v)^T[key][head]
+// on tcgen05 (kind::f16, A from TMEM, fp32 accumulate in TMEM), one 256-key
+// item at a time:
+//  * V is dim-major in the cache, so an item's codes are one 128 x 128-byte
+//    tile (a row per channel, TMA with the 128-byte swizzle) and TMEM lane d
+//    (channel d) takes its own run of tokens: code byte j converts to the
+//    fp16 pair (token 2j, token 2j+1) of A column j, times the pair's E4M3
+//    scales (one group scale per 16 tokens inside the group prefix, per
+//    element past it).  V-hat = code * scale is exact in fp16 (at most five
+//    significant bits in [2^-10, 2688]).  Eight converter warps: TMEM lane
+//    quarter = warp % 4, half of the item's tokens = the warpgroup.
+//  * B = P-hat * g_v * 2^E as fp16 hi (rows [0, MG)) + lo (rows [MG, 2 MG)),
+//    K-major with the 128-byte swizzle: g_v varies along the keys, so it
+//    cannot be factored out, and hi + lo keep 22 significant bits; 2^E, one
+//    power of two per item, puts the largest value just below 2^15 and is
+//    taken back out of the partial exactly.  Eight P warps: a thread takes a
+//    key pair and every other query head; e = exp2((S - m) log2 e) and the
+//    NVFP4 fake-quant of e per 16 keys (block maximum over eight lanes), as
+//    the prefill kernel quantizes P.
+//  * one thread issues an item's 16 MMAs (M = 128 channels, N = 2 MG rounded
+//    up to 16, K = 16 keys) into one of two accumulators; the first four P
+//    warps write an item's partial, (hi + lo) 2^-E, while the next item's
+//    MMAs run.
+namespace dpv {
+constexpr int NS = 4;               // ring stages
+constexpr int CW0 = 2, NCW = 8;     // converter warps 2 .. 9
+constexpr int PW0 = 10, NPW = 8;    // P warps 10 .. 17 (10 .. 13 also write the partials)
+constexpr int THREADS = (PW0 + NPW) * 32;
+constexpr uint32_t VC = DK_KEYS * DK_D / 2;       // codes [128 channels][128 B]
+constexpr uint32_t VS16 = DK_D * (DK_KEYS / 16);  // group scales [128 channels][16]
+constexpr uint32_t VG = DK_KEYS * 4;
+constexpr uint32_t S1 = DK_KEYS * 4;              // S of one head
+constexpr uint32_t T_A = 0, T_ACC = 256;          // TMEM: A buffers 0 / 128, accumulators 256 / 288
+template <int MG>
+struct Cfg {
+  static constexpr int NP = 2 * MG < 16 ? 16 : 2 * MG;  // B rows (MMA N)
+  static constexpr uint32_t STAGE = VC + VS16 + VG + MG * S1;
+  static constexpr uint32_t KBLK = NP * 128;  // B rows of one 64-key block
+  static constexpr uint32_t PB = 4 * KBLK;    // B of one item
+  static constexpr uint32_t OFF_PB = NS * STAGE;
+  static constexpr uint32_t SMEM = OFF_PB + 2 * PB + 1024;  // + alignment slack
+  static_assert(STAGE % 1024 == 0, "every stage keeps the 1024-byte alignment of the swizzled tile");
+  static_assert(NP <= 32, "two accumulators of NP columns at T_ACC");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+}  // namespace dpv
 
-template <int MG, int NW>
-__global__ void __launch_bounds__((NW + 1) * 32) decode_pv_kernel(DecodeArgs p) {
-  using C = PvCfg<MG, NW>;
-  constexpr int NT = C::NT, KPW = C::KPW, LG = C::LG;
-  extern __shared__ __align__(128) uint8_t ring[];
-  __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES];
-  __shared__ float lred[NW][MG];
+template <int MG>
+__global__ void __launch_bounds__(dpv::THREADS, 1)
+    decode_pv_kernel(const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmVs,
+                     DecodeArgs p) {
+  using namespace dpv;
+  using C = Cfg<MG>;
+  constexpr int NH = MG / 2;  // query heads per P thread: hs, hs + 2, ...
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[NS], empty[NS], a_full[2], a_free[2], b_full[2], b_free[2], acc_full[2],
+      acc_free[2], drained;
+  __shared__ uint32_t tslot;
+  __shared__ float lred[2][NPW][NH];
+  __shared__ float gmx[2][NPW];
   __shared__ float rcp_tab[128];  // correctly rounded 1/s of every non-negative E4M3 scale byte (0 -> 0)
-  __half(*ph)[PV_PH_LD] = reinterpret_cast<__half(*)[PV_PH_LD]>(ring + C::RING);  // hi rows [0,MG), lo rows [MG,2MG)
-  float(*part)[MG][PV_PART_LD] = reinterpret_cast<float(*)[MG][PV_PART_LD]>(ring + C::RING + C::PH);
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, t = threadIdx.x;
-  const int g8 = lane >> 2, t4 = lane & 3;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int G = p.Hq / p.Hkv;
   int i0, i1;
   item_range(p.nsplit * p.B * p.Hkv, i0, i1);
+  const int n_items = i1 - i0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], NW);
+    for (int s = 0; s < NS; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], NCW + NPW);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], NCW), mbar_init(&a_free[i], 1);
+      mbar_init(&b_full[i], NPW), mbar_init(&b_free[i], 1);
+      mbar_init(&acc_full[i], 1), mbar_init(&acc_free[i], 4);
+    }
+    mbar_init(&drained, 1);
     fence_barrier_init();
   }
   if (threadIdx.x < 128) {
     const float sv = e4m3_to_f32((uint8_t)threadIdx.x);
     rcp_tab[threadIdx.x] = sv == 0.0f ? 0.0f : __frcp_rn(sv);
   }
-  __syncthreads();
-  if (warp == NW) {
-    if (lane == 0)
-      produce<C::STAGES>(full, empty, ring, C::STAGE, i0, i1, 0x411, [&](int item, uint8_t* st, uint64_t* bar) {
-        const int bk = item / p.nsplit, split = item % p.nsplit, b = bk / p.Hkv, hk = bk % p.Hkv;
-        const int64_t row = (int64_t)bk * p.Tmax + (int64_t)split * DK_KEYS;
-        const int ks = p.nsplit * DK_KEYS;
-        const bool compact = split < p.nsplit16;
-        mbar_arrive_expect_tx(bar, PV_VC + (compact ? PV_VS16 : 0u) + PV_VG + (uint32_t)G * PV_S1);
-        bulk_load(st, p.v_codes + row * (DK_D / 2), PV_VC, bar);
-        if (compact) bulk_load(st + PV_VC, p.v_scales16 + row / 16 * DK_D, PV_VS16, bar);
-        bulk_load(st + PV_VC + PV_VS16, p.v_g + (int64_t)b * p.Tmax + (int64_t)split * DK_KEYS, PV_VG, bar);
-        for (int g = 0; g < G; ++g)
-          bulk_load(st + PV_VC + PV_VS16 + PV_VG + g * PV_S1,
-                    p.S + ((int64_t)b * p.Hq + hk * G + g) * ks + (int64_t)split * DK_KEYS, PV_S1, bar);
-      });
-    return;
+  // B rows of heads >= G and rows >= 2 MG stay zero
+  for (uint32_t i = threadIdx.x; i < 2 * C::PB / 16; i += THREADS)
+    reinterpret_cast<uint4*>(sm + C::OFF_PB)[i] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (warp == 1) {
+    tmem_alloc(&tslot, 512);
+    tmem_relinquish();
   }
-  const float log2e = 1.4426950408889634f, r6 = __frcp_rn(6.0f);
-  // phase e: this lane's key (lane group lg takes heads lg, lg + LG, ...) and its MMA k position
-  const int lg = lane / KPW;
-  const int key = KPW * warp + lane % KPW;
-  const int kr = key & 15;
-  const int kpos = (key & ~15) + (kr & 8) + 2 * (kr & 3) + ((kr >> 2) & 1);
-  int cur = -1;
-  float m[MG];
-#pragma unroll
-  for (int g = 0; g < MG; ++g) m[g] = 0.0f;
-  for (int it = 0; it < i1 - i0; ++it) {
-    const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
-    const int b = bk / p.Hkv, hk = bk % p.Hkv;
-    const int64_t bh0 = (int64_t)b * p.Hq + hk * G;
-    if (bk != cur) {
-      cur = bk;
-#pragma unroll
-      for (int g = 0; g < MG; ++g)
-        if (g < G) m[g] = __uint_as_float(p.mrow[bh0 + g]);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmVs);
+      produce<NS>(full, empty, sm, C::STAGE, i0, i1, 0x411, [&](int item, uint8_t* st, uint64_t* bar) {
+        const int bk = item / p.nsplit, split = item % p.nsplit, b = bk / p.Hkv, hk = bk % p.Hkv;
+        const int64_t ks = (int64_t)p.nsplit * DK_KEYS;
+        const bool compact = split < p.nsplit16;
+        mbar_arrive_expect_tx(bar, VC + (compact ? VS16 : 0u) + VG + (uint32_t)G * S1);
+        tma_load_2d(st, &tmV, bar, split * (DK_KEYS / 2), bk * DK_D);
+        if (compact) tma_load_2d(st + VC, &tmVs, bar, split * (DK_KEYS / 16), bk * DK_D);
+        bulk_load(st + VC + VS16, p.v_g + (int64_t)b * p.Tmax + (int64_t)split * DK_KEYS, VG, bar);
+        for (int g = 0; g < G; ++g)
+          bulk_load(st + VC + VS16 + VG + g * S1,
+                    p.S + ((int64_t)b * p.Hq + hk * G + g) * ks + (int64_t)split * DK_KEYS, S1, bar);
+      });
     }
-    const int s = it % C::STAGES;
-    // a failed wait reads stale shared memory below; all consumers then leave together at consumers_all
-    const bool landed = mbar_wait(&full[s], (it / C::STAGES) & 1, 0x412);
-    uint8_t* st = ring + (size_t)s * C::STAGE;
-    const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
-    const bool live = key < nlive;
-    // chunks inside the group-scale prefix hold every key live
-    const bool compact = split < p.nsplit16;
-    const int64_t vrow = (int64_t)bk * p.Tmax + (int64_t)split * DK_KEYS;  // first cache row of the chunk
-    if (!live && lg == 0) {
-      // the key is past len: whatever the cache holds there becomes V = 0 (its scales read as 0
-      // below; P-hat is 0 there too)
-      uint4* vc = reinterpret_cast<uint4*>(st + key * (DK_D / 2));
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, C::NP);
+      for (int it = 0; it < n_items; ++it) {
+        const int a = it & 1;
+        if (!mbar_wait(&a_full[a], (it >> 1) & 1, 0x412)) break;
+        if (!mbar_wait(&b_full[a], (it >> 1) & 1, 0x413)) break;
+        if (it >= 2 && !mbar_wait(&acc_free[a], ((it - 2) >> 1) & 1, 0x414)) break;
+        tc_fence_after();
+        const uint32_t pb = smem_u32(sm + C::OFF_PB + a * C::PB);
 #pragma unroll
-      for (int i = 0; i < DK_D / 2 / 16; ++i) vc[i] = make_uint4(0u, 0u, 0u, 0u);
+        for (int ks = 0; ks < DK_KEYS / 16; ++ks)
+          mma_f16_ts(tmem + T_ACC + 32 * a, tmem + T_A + 128 * a + 8 * ks,
+                     smem_desc(pb + (ks >> 2) * C::KBLK + (ks & 3) * 32, 16, 1024, kSwizzle128B), idesc,
+                     ks > 0 ? 1u : 0u);
+        tc_commit(&a_free[a]);
+        tc_commit(&b_free[a]);
+        tc_commit(&acc_full[a]);
+      }
+      tc_commit(&drained);  // every MMA issued completes before TMEM is released
+      mbar_drain(&drained, 0);
     }
-    const float gv = live ? reinterpret_cast<const float*>(st + PV_VC + PV_VS16)[key] : 0.0f;
-    float gmax = gv;
+  } else if (warp < PW0) {
+    // ---------------------------------------------------------------- V-hat into TMEM
+    const int quarter = warp & 3, half = (warp - CW0) >> 2;
+    const int d = quarter * 32 + lane;  // channel == TMEM lane
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    for (int it = 0; it < n_items; ++it) {
+      const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
+      const int s = it % NS, a = it & 1;
+      if (!mbar_wait(&full[s], (it / NS) & 1, 0x415)) break;
+      if (it >= 2 && !mbar_wait(&a_free[a], ((it - 2) >> 1) & 1, 0x416)) break;
+      tc_fence_after();
+      const uint8_t* st = sm + (size_t)s * C::STAGE;
+      uint4 cw[4];  // this half's 64 code bytes: logical 16-byte chunks 4 half .. 4 half + 3 of the row
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
-    // 2^E with P-hat * g_v * 2^E < 2^15 (P-hat <= 1.03125 < 2, g_v < 2^(e+1))
-    int E = 0;
-    if (gmax > 0.0f) E = max(-100, min(100, 13 - (((__float_as_int(gmax) >> 23) & 0xFF) - 127)));
-    const float up = __int_as_float((E + 127) << 23), down = __int_as_float((127 - E) << 23);
-    {
-      const float* Ss = reinterpret_cast<const float*>(st + PV_VC + PV_VS16 + PV_VG);
+      for (int c = 0; c < 4; ++c)
+        cw[c] = *reinterpret_cast<const uint4*>(st + d * 128 + (((4 * half + c) ^ (d & 7)) << 4));
+      const uint32_t acol = tmem + lane_base + T_A + 128 * a + 64 * half;
+      if (split < p.nsplit16) {
+        // every key of the chunk is live; groups 8 half .. 8 half + 7 of the channel
+        const uint2 g8 = *reinterpret_cast<const uint2*>(st + VC + d * 16 + 8 * half);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
 #pragma unroll
-      for (int gi = 0; gi < (MG + LG - 1) / LG; ++gi) {
-        const int g = lg + gi * LG;
-        if (gi * LG >= G) break;  // uniform over the warp
-        const bool on = g < G;
-        float mg = m[gi * LG];  // m[g] with compile-time indices (lg is 0 or 1)
-        if constexpr (LG > 1) {
-          if (gi * LG + 1 < MG && lg == 1) mg = m[gi * LG + 1];
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t gw = c < 2 ? g8.x : g8.y;
+          const uint32_t b0 = (gw >> (16 * (c & 1))) & 0xFFu, b1 = (gw >> (16 * (c & 1) + 8)) & 0xFFu;
+          const uint32_t s0 = cvt_e4m3x2_f16x2(b0 * 0x101u), s1 = cvt_e4m3x2_f16x2(b1 * 0x101u);
+          const uint32_t w[4] = {cw[c].x, cw[c].y, cw[c].z, cw[c].w};
+          uint32_t o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            o[j] = hmul2u(cvt_e2m1x2_f16x2((w[j >> 2] >> (8 * (j & 3))) & 0xFFu), j < 8 ? s0 : s1);
+          tmem_st16(acol + 16 * c, o);
         }
-        const float e = live && on ? exp2f(__fmul_rn(Ss[min(g, G - 1) * DK_KEYS + key] - mg, log2e)) : 0.0f;
-        float am = e;  // block of 16 keys = 16 consecutive lanes
+      } else {
+        // per-element scales from the cache (L2); keys past len read scale 0, so V-hat is 0 there
+        const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
+        const uint8_t* vs = p.v_scales + ((int64_t)bk * DK_D + d) * p.Tmax + (int64_t)split * DK_KEYS + 128 * half;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        for (int c = 0; c < 4; ++c) {
+          uint4 sc[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int n = nlive - (128 * half + 32 * c + 16 * i);  // live keys of these 16
+            sc[i] = n > 0 ? __ldg(reinterpret_cast<const uint4*>(vs + 32 * c + 16 * i)) : make_uint4(0u, 0u, 0u, 0u);
+            if (n < 16) {
+              uint32_t* e = reinterpret_cast<uint32_t*>(&sc[i]);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int m = n - 4 * q;  // live bytes of word q
+                e[q] = m >= 4 ? e[q] : m <= 0 ? 0u : e[q] & (0xFFFFFFFFu >> (32 - 8 * m));
+              }
+            }
+          }
+          const uint32_t w[4] = {cw[c].x, cw[c].y, cw[c].z, cw[c].w};
+          const uint32_t sw[8] = {sc[0].x, sc[0].y, sc[0].z, sc[0].w, sc[1].x, sc[1].y, sc[1].z, sc[1].w};
+          uint32_t o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            o[j] = hmul2u(cvt_e2m1x2_f16x2((w[j >> 2] >> (8 * (j & 3))) & 0xFFu),
+                          cvt_e4m3x2_f16x2((sw[j >> 1] >> (16 * (j & 1))) & 0xFFFFu));
+          tmem_st16(acol + 16 * c, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[a]);
+    }
+  } else {
+    // ---------------------------------------------------------------- P-hat, l, partials
+    const int pt = threadIdx.x - PW0 * 32;
+    const int pw = pt >> 5, hs = pt >> 7, pair = pt & 127, k0 = 2 * pair;
+    const bool epi = warp < PW0 + 4;
+    const int quarter = warp & 3;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const float log2e = 1.4426950408889634f, r6 = __frcp_rn(6.0f);
+    // B word of keys (k0, k0 + 1): 64-key block, byte (k0 & 63) * 2 of the 128-byte row, chunk swizzled by row & 7
+    const uint32_t kb_off = (uint32_t)(k0 >> 6) * C::KBLK, wb = (uint32_t)(k0 & 63) * 2;
+    auto bword = [&](int row) { return kb_off + row * 128 + ((((wb >> 4) ^ (row & 7)) << 4) | (wb & 15)); };
+    float m[NH];
+#pragma unroll
+    for (int j = 0; j < NH; ++j) m[j] = 0.0f;
+    int cur = -1;
+    int64_t prev_bh0 = 0;
+    int prev_split = 0;
+    float prev_down = 1.0f;
+    auto epilogue = [&](int i) {
+      const int a = i & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a], (i >> 1) & 1, 0x417));
+      tc_fence_after();
+      if (ok) {
+        uint32_t r[32];
+        if constexpr (C::NP == 16) {
+          uint32_t r16[16];
+          tmem_ld16(tmem + lane_base + T_ACC + 32 * a, r16);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) r[c] = r16[c];
+        } else {
+          tmem_ld32(tmem + lane_base + T_ACC + 32 * a, r);
+          tmem_ld_wait();
+        }
+        const int d = quarter * 32 + lane;
+#pragma unroll
+        for (int h = 0; h < MG; ++h)
+          if (h < G)
+            p.opart[((prev_bh0 + h) * p.nsplit + prev_split) * DK_D + d] =
+                (__uint_as_float(r[h]) + __uint_as_float(r[MG + h])) * prev_down;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[a]);
+    };
+    int it = 0;
+    for (; it < n_items; ++it) {
+      const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
+      const int b = bk / p.Hkv, hk = bk % p.Hkv;
+      const int64_t bh0 = (int64_t)b * p.Hq + hk * G;
+      if (bk != cur) {
+        cur = bk;
+#pragma unroll
+        for (int j = 0; j < NH; ++j)
+          if (hs + 2 * j < G) m[j] = __uint_as_float(p.mrow[bh0 + hs + 2 * j]);
+      }
+      const int s = it % NS, par = it & 1;
+      // a failed wait reads stale shared memory below; the P warps then leave together at consumers_all
+      bool ok = mbar_wait(&full[s], (it / NS) & 1, 0x418);
+      const uint8_t* st = sm + (size_t)s * C::STAGE;
+      const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
+      const bool live0 = k0 < nlive, live1 = k0 + 1 < nlive;
+      const float2 gv2 = *reinterpret_cast<const float2*>(st + VC + VS16 + 8 * pair);
+      const float gv0 = live0 ? gv2.x : 0.0f, gv1 = live1 ? gv2.y : 0.0f;
+      const float* Ss = reinterpret_cast<const float*>(st + VC + VS16 + VG);
+      float e0[NH], e1[NH];
+#pragma unroll
+      for (int j = 0; j < NH; ++j) {
+        const int h = hs + 2 * j;
+        e0[j] = e1[j] = 0.0f;
+        if (h < G) {  // uniform over the warp
+          const float2 s2 = *reinterpret_cast<const float2*>(Ss + h * DK_KEYS + k0);
+          if (live0) e0[j] = exp2f(__fmul_rn(s2.x - m[j], log2e));
+          if (live1) e1[j] = exp2f(__fmul_rn(s2.y - m[j], log2e));
+          float l = e0[j] + e1[j];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+          if (lane == 0) lred[par][pw][j] = l;
+        }
+      }
+      float gmax = fmaxf(gv0, gv1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
+      if (lane == 0) gmx[par][pw] = gmax;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // S and g_v are in registers
+      if (!consumers_all<NPW>(ok)) break;     // also publishes lred and gmx
+      float gall = gmx[par][0];
+#pragma unroll
+      for (int w = 1; w < NPW; ++w) gall = fmaxf(gall, gmx[par][w]);
+      // 2^E with P-hat * g_v * 2^E < 2^15 (P-hat <= 1.03125 < 2, g_v < 2^(e+1))
+      int E = 0;
+      if (gall > 0.0f) E = max(-100, min(100, 13 - (((__float_as_int(gall) >> 23) & 0xFF) - 127)));
+      const float up = __int_as_float((E + 127) << 23), down = __int_as_float((127 - E) << 23);
+      if (pt < G) {
+        // l of head pt: the four warps of its head parity, slot pt / 2
+        const int w0 = (pt & 1) * 4, j = pt >> 1;
+        p.lpart[(bh0 + pt) * p.nsplit + split] =
+            (lred[par][w0][j] + lred[par][w0 + 1][j]) + (lred[par][w0 + 2][j] + lred[par][w0 + 3][j]);
+      }
+      // the B buffer is free once the MMAs of item it - 2 have read it (a failed wait is caught at the
+      // next consumers_all; every later wait then fails fast)
+      if (it >= 2) mbar_wait(&b_free[par], ((it - 2) >> 1) & 1, 0x419);
+      uint8_t* pb = sm + C::OFF_PB + par * C::PB;
+#pragma unroll
+      for (int j = 0; j < NH; ++j) {
+        const int h = hs + 2 * j;
+        if (h >= G) continue;  // uniform over the warp
+        float am = fmaxf(e0[j], e1[j]);  // block of 16 keys = 8 consecutive lanes
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
         const uint8_t sb = e4m3_satfinite(__fmul_rn(am, r6));  // e >= 0: sb < 0x80
         const float sf = e4m3_to_f32(sb);
         const float rs = rcp_tab[sb & 0x7F];
-        const uint32_t byte = e2m1x2(__fmaf_rn(e, rs, 0.0f), 0.0f);
-        const float code = __half2float(__ushort_as_half((unsigned short)(cvt_e2m1x2_f16x2(byte) & 0xFFFFu)));
-        const float x = live ? __fmul_rn(__fmul_rn(__fmul_rn(code, sf), gv), up) : 0.0f;
-        const __half hi = __float2half_rn(x);
-        if (on) {
-          ph[g][kpos] = hi;
-          ph[MG + g][kpos] = __float2half_rn(x - __half2float(hi));
-        }
-        float l = e;
-#pragma unroll
-        for (int o = KPW / 2; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (on && lane % KPW == 0) lred[warp][g] = l;
+        const uint32_t c2 = cvt_e2m1x2_f16x2(e2m1x2(__fmaf_rn(e0[j], rs, 0.0f), __fmaf_rn(e1[j], rs, 0.0f)));
+        const float2 cf = __half22float2(*reinterpret_cast<const __half2*>(&c2));
+        const float x0 = live0 ? __fmul_rn(__fmul_rn(__fmul_rn(cf.x, sf), gv0), up) : 0.0f;
+        const float x1 = live1 ? __fmul_rn(__fmul_rn(__fmul_rn(cf.y, sf), gv1), up) : 0.0f;
+        const __half2 hi = __floats2half2_rn(x0, x1);
+        const float2 hf = __half22float2(hi);
+        *reinterpret_cast<__half2*>(pb + bword(h)) = hi;
+        *reinterpret_cast<__half2*>(pb + bword(MG + h)) = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b_full[par]);
+      // the previous item's partial, while this item's V-hat and MMAs proceed
+      if (epi && it >= 1) epilogue(it - 1);
+      prev_bh0 = bh0, prev_split = split, prev_down = down;
     }
-    __syncwarp();
-    float acc[NT][8][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[nt][mt][i] = 0.0f;
-#pragma unroll
-    for (int kstep = 0; kstep < C::KSTEPS; ++kstep) {
-      const int kb = KPW * warp + 16 * kstep;
-      uint2 cw[4];
-      uint4 sw[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int kk = kb + t4 + 4 * i;
-        cw[i] = *reinterpret_cast<const uint2*>(st + kk * (DK_D / 2) + 8 * g8);
-      }
-      if (compact) {
-        // the four keys of this lane lie in one 16-token group: one row of group scales
-        const uint4 s16 = *reinterpret_cast<const uint4*>(st + PV_VC + (kb >> 4) * DK_D + 16 * g8);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sw[i] = s16;
-      } else {
-        // per-element scales straight from the cache (L2): only the chunks past the prefix
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int kk = kb + t4 + 4 * i;
-          sw[i] = kk < nlive ? __ldg(reinterpret_cast<const uint4*>(p.v_scales + (vrow + kk) * DK_D + 16 * g8))
-                             : make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
-      uint32_t bhi[NT][2], blo[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int h = 8 * nt + g8;
-        const bool on = h < G;
-        bhi[nt][0] = on ? *reinterpret_cast<const uint32_t*>(&ph[h][kb + 2 * t4]) : 0u;
-        bhi[nt][1] = on ? *reinterpret_cast<const uint32_t*>(&ph[h][kb + 2 * t4 + 8]) : 0u;
-        blo[nt][0] = on ? *reinterpret_cast<const uint32_t*>(&ph[MG + h][kb + 2 * t4]) : 0u;
-        blo[nt][1] = on ? *reinterpret_cast<const uint32_t*>(&ph[MG + h][kb + 2 * t4 + 8]) : 0u;
-      }
-      // code bytes of key pairs (t, t+4) and (t+8, t+12): even dims in E, odd dims in O,
-      // the first key of the pair in the low nibble
-      uint32_t ev[2][2], od[2][2];
-#pragma unroll
-      for (int pr = 0; pr < 2; ++pr)
-#pragma unroll
-        for (int wd = 0; wd < 2; ++wd) {
-          const uint32_t x = wd ? cw[2 * pr].y : cw[2 * pr].x, y = wd ? cw[2 * pr + 1].y : cw[2 * pr + 1].x;
-          ev[pr][wd] = (x & 0x0F0F0F0Fu) | ((y << 4) & 0xF0F0F0F0u);
-          od[pr][wd] = ((x >> 4) & 0x0F0F0F0Fu) | (y & 0xF0F0F0F0u);
-        }
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int wd = mt >> 2, sh = 8 * (mt & 3);
-        const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
-        uint32_t a[4];
-#pragma unroll
-        for (int pr = 0; pr < 2; ++pr) {
-          const uint32_t sx = (mt >> 1) == 0 ? sw[2 * pr].x : (mt >> 1) == 1 ? sw[2 * pr].y
-                            : (mt >> 1) == 2 ? sw[2 * pr].z : sw[2 * pr].w;
-          const uint32_t sy = (mt >> 1) == 0 ? sw[2 * pr + 1].x : (mt >> 1) == 1 ? sw[2 * pr + 1].y
-                            : (mt >> 1) == 2 ? sw[2 * pr + 1].z : sw[2 * pr + 1].w;
-          const uint32_t sc = prmt(sx, sy, sel);  // {s_x, s_y} of dim 2mt (low half), of dim 2mt+1 (high half)
-          a[2 * pr] = hmul2u(cvt_e2m1x2_f16x2((ev[pr][wd] >> sh) & 0xFFu), cvt_e4m3x2_f16x2(sc & 0xFFFFu));
-          a[2 * pr + 1] = hmul2u(cvt_e2m1x2_f16x2((od[pr][wd] >> sh) & 0xFFu), cvt_e4m3x2_f16x2(sc >> 16));
-        }
-        // fragment order: a0 rows g / k 0-7, a1 rows g+8 / k 0-7, a2 rows g / k 8-15, a3 rows g+8 / k 8-15
-        const uint32_t fr[4] = {a[0], a[1], a[2], a[3]};
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          mma16816(acc[nt][mt], fr, bhi[nt][0], bhi[nt][1]);
-          mma16816(acc[nt][mt], fr, blo[nt][0], blo[nt][1]);
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);  // this warp's V rows and scores are no longer read
-    // acc[nt][mt]: (dim 16g+2mt, head 8nt+2t), (dim, head+1), (dim+1, head), (dim+1, head+1)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int h = 8 * nt + 2 * t4, c = 2 * mt;
-        if (h < G) {
-          part[warp][h][c * 8 + g8] = acc[nt][mt][0] * down;
-          part[warp][h][(c + 1) * 8 + g8] = acc[nt][mt][2] * down;
-        }
-        if (h + 1 < G) {
-          part[warp][h + 1][c * 8 + g8] = acc[nt][mt][1] * down;
-          part[warp][h + 1][(c + 1) * 8 + g8] = acc[nt][mt][3] * down;
-        }
-      }
-    if (!consumers_all<NW>(landed)) break;  // part and lred are complete
-    if (t < G) {
-      float l = 0.0f;
-      for (int w = 0; w < NW; ++w) l += lred[w][t];
-      p.lpart[(bh0 + t) * p.nsplit + split] = l;
-    }
-    for (int i = t; i < G * DK_D; i += NW * 32) {
-      // consecutive threads read consecutive positions (no bank conflicts); pos c*8 + g holds dim 16g + c
-      const int g = i / DK_D, pos = i % DK_D, d = 16 * (pos & 7) + (pos >> 3);
-      float v[NW];
-#pragma unroll
-      for (int w = 0; w < NW; ++w) v[w] = part[w][g][pos];
-      // pairwise sums in a fixed order: ((w0 + w1) + (w2 + w3)) + ...
-#pragma unroll
-      for (int sp = 1; sp < NW; sp *= 2)
-#pragma unroll
-        for (int w = 0; w < NW; w += 2 * sp) v[w] += v[w + sp];
-      p.opart[((bh0 + g) * p.nsplit + split) * DK_D + d] = v[0];
-    }
-    consumers_sync<NW>();  // part and lred are rewritten by the next item
+    if (epi && it >= 1) epilogue(it - 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -610,12 +667,26 @@ int persistent_grid(const void* fn, uint32_t smem, int items, int threads = DK_T
   return std::min(items, sms * per_sm);
 }
 
-template <int MG, int NW>
+template <int MG>
 int launch_pv(const DecodeArgs& a, int items, cudaStream_t st) {
-  using C = PvCfg<MG, NW>;
-  if (int e = set_smem_attr((const void*)decode_pv_kernel<MG, NW>, (int)C::SMEM)) return e;
-  const int grid = persistent_grid((const void*)decode_pv_kernel<MG, NW>, C::SMEM, items, C::THREADS);
-  decode_pv_kernel<MG, NW><<<grid, C::THREADS, C::SMEM, st>>>(a);
+  using C = dpv::Cfg<MG>;
+  // codes: [B*Hkv*D rows][Tmax/2 bytes], tiles of 128 channels x 256 keys; group scales: [rows][Tmax/16]
+  const uint64_t rows = (uint64_t)a.B * a.Hkv * DK_D;
+  CUtensorMap mv, ms;
+  if (int e = encode_tiled_2d(&mv, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.v_codes, (uint64_t)a.Tmax / 2, rows,
+                              (uint64_t)a.Tmax / 2, DK_KEYS / 2, DK_D, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  // without a group-scale prefix the map is never read; it then describes the per-element scales
+  const uint8_t* s16 = a.v_scales16 ? a.v_scales16 : a.v_scales;
+  if (int e = encode_tiled_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT8, s16, (uint64_t)a.Tmax / 16, rows,
+                              (uint64_t)a.Tmax / 16, DK_KEYS / 16, DK_D, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return e;
+  if (int e = set_smem_attr((const void*)decode_pv_kernel<MG>, (int)C::SMEM)) return e;
+  // one CTA per SM: each holds all 512 TMEM columns
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  decode_pv_kernel<MG><<<std::min(items, sms), dpv::THREADS, C::SMEM, st>>>(mv, ms, a);
   return check_launch("decode_pv_kernel");
 }
 
@@ -673,10 +744,7 @@ extern "C" int fp4attn_decode_ex(const uint8_t* q_codes, const uint8_t* q_scales
                          st>>>(a);
   if (int e = check_launch("decode_scores_kernel")) return e;
   const int G = Hq / Hkv;
-  // eight consumer warps for every group size (sixteen, with the heads split between half-warps in
-  // phase e, measured 199 us against 175 us at B 8 / 32768 keys / 4 heads per KV head)
-  const int e = G <= 4 ? launch_pv<4, 8>(a, items, st)
-                : G <= 8 ? launch_pv<8, 8>(a, items, st) : launch_pv<16, 8>(a, items, st);
+  const int e = G <= 4 ? launch_pv<4>(a, items, st) : G <= 8 ? launch_pv<8>(a, items, st) : launch_pv<16>(a, items, st);
   if (e) return e;
   decode_combine_kernel<<<(unsigned)bh, CB_GROUPS * 32, 0, st>>>(a);
   return check_launch("decode_combine_kernel");

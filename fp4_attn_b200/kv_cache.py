@@ -15,13 +15,18 @@ decode kernels stream whole chunks of 256 keys):
   k_codes  uint8 [B, Hkv, Tmax, D/2]   E2M1 pairs, element 2k in the low nibble
   k_scales uint8 [B, Hkv, Tmax, D/16]  E4M3 block scales along head_dim
   k_g      fp32  [B, Tmax]             per-token global scale (row max)
-  v_codes  uint8 [B, Hkv, Tmax, D/2]
-  v_scales uint8 [B, Hkv, Tmax, D]     one E4M3 scale per element: a V block of
-                                       16 runs along the tokens of the call
-                                       that appended it
+  v_codes  uint8 [B, Hkv, D, Tmax/2]   V stored dim-major: byte j of channel d
+                                       holds tokens 2j (low nibble) and 2j+1
+  v_scales uint8 [B, Hkv, D, Tmax]     one E4M3 scale per element: a V block of
+                                       16 runs along the tokens of the call that
+                                       appended it
   v_g      fp32  [B, Tmax]             per-token global scale (column max / 1536)
-  v_scales16 uint8 [B, Hkv, Tmax/16, D] the same V scales once per 16-token group,
+  v_scales16 uint8 [B, Hkv, D, Tmax/16] the same V scales once per 16-token group,
                                        valid for the first len16 tokens
+
+V is dim-major because the decode kernel contracts over the keys: a channel's
+run of tokens is one row of the tensor-core operand (E2M1 pairs convert to
+fp16 pairs in place, one group scale multiplies 16 tokens).
 
 A call's V blocks coincide with whole 16-token groups of the cache when the
 call starts on a group boundary and each sequence's tokens fill whole blocks
@@ -51,10 +56,10 @@ class NVFP4KVCache:
         self.k_codes = torch.zeros(B, Hkv, Tmax, D // 2, dtype=u8, device=device)
         self.k_scales = torch.zeros(B, Hkv, Tmax, D // 16, dtype=u8, device=device)
         self.k_g = torch.zeros(B, Tmax, dtype=torch.float32, device=device)
-        self.v_codes = torch.zeros(B, Hkv, Tmax, D // 2, dtype=u8, device=device)
-        self.v_scales = torch.zeros(B, Hkv, Tmax, D, dtype=u8, device=device)
+        self.v_codes = torch.zeros(B, Hkv, D, Tmax // 2, dtype=u8, device=device)
+        self.v_scales = torch.zeros(B, Hkv, D, Tmax, dtype=u8, device=device)
         self.v_g = torch.zeros(B, Tmax, dtype=torch.float32, device=device)
-        self.v_scales16 = torch.zeros(B, Hkv, Tmax // 16, D, dtype=u8, device=device)
+        self.v_scales16 = torch.zeros(B, Hkv, D, Tmax // 16, dtype=u8, device=device)
         self.len = 0
         self.len16 = 0
 
@@ -64,15 +69,17 @@ class NVFP4KVCache:
             return
         Tmax = (capacity + 255) // 256 * 256
         L = self.len
-        for name in ("k_codes", "k_scales", "v_codes", "v_scales"):  # [B, Hkv, Tmax, x]
+        for name in ("k_codes", "k_scales"):  # [B, Hkv, Tmax, x]
             old = getattr(self, name)
             new = torch.zeros(self.B, self.Hkv, Tmax, old.shape[-1], dtype=old.dtype, device=old.device)
             new[:, :, :L] = old[:, :, :L]
             setattr(self, name, new)
-        old = self.v_scales16  # [B, Hkv, Tmax/16, D]
-        new = torch.zeros(self.B, self.Hkv, Tmax // 16, self.D, dtype=old.dtype, device=old.device)
-        new[:, :, :(L + 15) // 16] = old[:, :, :(L + 15) // 16]
-        self.v_scales16 = new
+        for name, per, keep in (("v_codes", 2, (L + 1) // 2), ("v_scales", 1, L),
+                                ("v_scales16", 16, (L + 15) // 16)):  # [B, Hkv, D, Tmax / per]
+            old = getattr(self, name)
+            new = torch.zeros(self.B, self.Hkv, self.D, Tmax // per, dtype=old.dtype, device=old.device)
+            new[..., :keep] = old[..., :keep]
+            setattr(self, name, new)
         for name in ("k_g", "v_g"):  # [B, Tmax]
             old = getattr(self, name)
             new = torch.zeros(self.B, Tmax, dtype=old.dtype, device=old.device)
@@ -103,18 +110,26 @@ class NVFP4KVCache:
         lo, hi = pv.codes & 15, pv.codes >> 4
         nib = torch.stack((lo, hi), dim=-1).reshape(H * D, npad)[:, :n]  # [H*D, B*q]
         sc = pv.scales.repeat_interleave(16, dim=1)[:, :n]  # [H*D, B*q]
-        nib = nib.view(H, D, B, q).permute(2, 0, 3, 1)  # [B, H, q, D]
-        sc = sc.view(H, D, B, q).permute(2, 0, 3, 1)
-        packed = (nib[..., 0::2] | (nib[..., 1::2] << 4)).to(torch.uint8)
-        self.v_codes[:, :, t0:t1] = packed
-        self.v_scales[:, :, t0:t1] = sc
+        nib = nib.view(H, D, B, q).permute(2, 0, 1, 3)  # [B, H, D, q]
+        sc = sc.view(H, D, B, q).permute(2, 0, 1, 3)
+        self.v_scales[..., t0:t1] = sc
         self.v_g[:, t0:t1] = pv.g[:n].view(B, q)
+        t = t0
+        if t % 2:  # the first token completes a byte whose low nibble an earlier call wrote
+            j = t // 2
+            self.v_codes[..., j] = (self.v_codes[..., j] & 0x0F) | (nib[..., 0].to(torch.uint8) << 4)
+            nib, t = nib[..., 1:], t + 1
+        if nib.shape[-1]:
+            if nib.shape[-1] % 2:  # the high nibble of the last byte waits for the next call's first token
+                nib = torch.cat((nib, torch.zeros_like(nib[..., :1])), dim=-1)
+            packed = (nib[..., 0::2] | (nib[..., 1::2] << 4)).to(torch.uint8)
+            self.v_codes[..., t // 2:t // 2 + packed.shape[-1]] = packed
         if self.len16 == t0 and t0 % 16 == 0 and (q % 16 == 0 or B == 1):
             # the call's blocks are the cache's groups t0/16 ... (the last one partial when q % 16 != 0,
             # its scale padded like the reference's block; the next call then starts mid-group)
             ng = (q + 15) // 16
-            s16 = pv.scales[:, :B * ng].view(H, D, B, ng).permute(2, 0, 3, 1)  # [B, H, groups, D]
-            self.v_scales16[:, :, t0 // 16:t0 // 16 + ng] = s16
+            s16 = pv.scales[:, :B * ng].view(H, D, B, ng).permute(2, 0, 1, 3)  # [B, H, D, groups]
+            self.v_scales16[..., t0 // 16:t0 // 16 + ng] = s16
             self.len16 = t0 + (q // 16) * 16 if q % 16 else t1
         self.len = t1
 

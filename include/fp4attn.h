@@ -293,7 +293,8 @@ int fp4qkv_rope_quant(const void* x, const void* w, const void* cos, const void*
  * of those values (fp4_attn_b200.kv_cache.NVFP4KVCache):
  *   k_codes [B][Hkv][Tmax][D/2], k_scales E4M3 [B][Hkv][Tmax][D/16],
  *   k_g [B][Tmax] (per-token row-mode global scale);
- *   v_codes [B][Hkv][Tmax][D/2], v_scales E4M3 [B][Hkv][Tmax][D] (one per
+ *   V dim-major: v_codes [B][Hkv][D][Tmax/2] (byte j of a channel holds
+ *   tokens 2j, low nibble, and 2j+1), v_scales E4M3 [B][Hkv][D][Tmax] (one per
  *   element: V's blocks run along the tokens of the call that appended them),
  *   v_g [B][Tmax].
  * The query is packed the same way, row mode on its [B, Hq*D] view:
@@ -309,7 +310,7 @@ int fp4attn_decode(const uint8_t* q_codes, const uint8_t* q_scales, const float*
                    const float* v_g, int B, int Hq, int Hkv, int D, int len, int Tmax, float scaling, float* out,
                    void* workspace, int64_t workspace_bytes, void* stream);
 /* fp4attn_decode with V's scales also stored once per 16-token group for a
- * prefix of the cache: v_scales16 E4M3 [B][Hkv][Tmax/16][D], valid for the
+ * prefix of the cache: v_scales16 E4M3 [B][Hkv][D][Tmax/16], valid for the
  * first len16 tokens (a multiple of 16, <= len; 0 and NULL = none), whose
  * groups each came from one quantization block (a call that started on a group
  * boundary with whole blocks per sequence).  Chunks of 256 keys inside the

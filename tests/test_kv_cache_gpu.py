@@ -31,9 +31,10 @@ def _e4m3(b):
 def _dequant_cache(c):
     L = c.len
     kc, ks, kg = c.k_codes[:, :, :L].cpu(), c.k_scales[:, :, :L].cpu(), c.k_g[:, :L].cpu()
-    vc, vs, vg = c.v_codes[:, :, :L].cpu(), c.v_scales[:, :, :L].cpu(), c.v_g[:, :L].cpu()
+    vs, vg = c.v_scales[..., :L].cpu(), c.v_g[:, :L].cpu()
+    vc = _unpack(c.v_codes.cpu())[..., :L]  # V is dim-major: [B, Hkv, D, tokens]
     k = (_unpack(kc) * _e4m3(ks).repeat_interleave(16, dim=-1)) * kg[:, None, :, None]
-    v = (_unpack(vc) * _e4m3(vs)) * vg[:, None, :, None]
+    v = ((vc * _e4m3(vs)) * vg[:, None, None, :]).transpose(-1, -2)
     return k, v
 
 
@@ -42,8 +43,8 @@ def _check_group_scales(c, expect_len16):
     L16 = c.len16
     assert L16 == expect_len16
     if L16:
-        rep = c.v_scales16[:, :, :L16 // 16].repeat_interleave(16, dim=2)
-        assert torch.equal(rep.cpu(), c.v_scales[:, :, :L16].cpu())
+        rep = c.v_scales16[..., :L16 // 16].repeat_interleave(16, dim=-1)
+        assert torch.equal(rep.cpu(), c.v_scales[..., :L16].cpu())
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,T0,len16", [(2, 8, 2, 300, 0), (3, 4, 4, 300, 0), (1, 16, 2, 520, 512),

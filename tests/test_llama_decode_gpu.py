@@ -32,7 +32,8 @@ def _dequant(c):
     e4 = lambda b: b.view(torch.float8_e4m3fn).float()  # noqa: E731
     k = (unpack(c.k_codes[:, :, :L].cpu()) * e4(c.k_scales[:, :, :L].cpu()).repeat_interleave(16, dim=-1)) \
         * c.k_g[:, :L].cpu()[:, None, :, None]
-    v = (unpack(c.v_codes[:, :, :L].cpu()) * e4(c.v_scales[:, :, :L].cpu())) * c.v_g[:, :L].cpu()[:, None, :, None]
+    v = ((unpack(c.v_codes.cpu())[..., :L] * e4(c.v_scales[..., :L].cpu())) * c.v_g[:, :L].cpu()[:, None, None, :]) \
+        .transpose(-1, -2)  # V is dim-major in the cache
     return k, v
 
 

@@ -142,10 +142,13 @@ def test_kv_cache_grow_keeps_tokens():
     from fp4_attn_b200 import kv_cache
     c = kv_cache.NVFP4KVCache(2, 2, 10, 128, "cpu")
     c.k_codes[:, :, :5] = 7
-    c.v_scales[:, :, :5] = 3
+    c.v_scales[..., :5] = 3  # V is dim-major: tokens along the last axis
+    c.v_codes[..., :3] = 0x21
     c.k_g[:, :5] = 1.5
     c.len = 5
     c.grow(300)
     assert c.capacity == 300 and c.Tmax == 512 and c.k_codes.shape[2] == 512
     assert (c.k_codes[:, :, :5] == 7).all() and (c.k_codes[:, :, 5:] == 0).all()
-    assert (c.v_scales[:, :, :5] == 3).all() and (c.k_g[:, :5] == 1.5).all() and (c.k_g[:, 5:] == 0).all()
+    assert (c.v_scales[..., :5] == 3).all() and (c.v_scales[..., 5:] == 0).all() and c.v_scales.shape[-1] == 512
+    assert (c.v_codes[..., :3] == 0x21).all() and (c.v_codes[..., 3:] == 0).all() and c.v_codes.shape[-1] == 256
+    assert (c.k_g[:, :5] == 1.5).all() and (c.k_g[:, 5:] == 0).all()

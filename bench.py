@@ -705,7 +705,7 @@ class DecodeWorkload:
     name = "decode"
     metric = "NVFP4 KV-cache decode attention GB/s per B200 (cache bytes read per step)"
     unit = "GB/s"
-    dtype = "nvfp4 K/V cache, mma.sync fp16-exact QK^T, tcgen05 fp16 V-hat x (P-hat g_v as hi + lo)"
+    dtype = "nvfp4 K/V cache, tcgen05 mxf4nvf4 QK^T, tcgen05 fp16 V-hat x (P-hat g_v as hi + lo)"
     B, Hq, Hkv, T, D = 8, 32, 8, 32768, 128
     use_graph = True
 

@@ -21,12 +21,11 @@
 // codes [B][Hq*D/2], E4M3 scales [B][Hq*D/16], g_q [B].
 //
 // Work item = (chunk of 256 keys, b, KV head).  Three kernels, HBM-bound:
-//  * scores: persistent CTAs stream their items' K through a ring of shared
-//    memory stages (one producer warp, bulk copies, mbarriers); eight warps
-//    compute S = (code*scale)_q . (code*scale)_k * g_q * g_k * scaling on
-//    mma.sync m16n8k16 (fp16 products exact, fp32 accumulate; the query heads
-//    of the KV head are the MMA rows, 8 keys its columns), write S and fold
-//    each row's maximum into an order-free atomic maximum;
+//  * scores: persistent CTAs stream their items' K (TMA codes, scales) through
+//    a ring; S^T = K-hat Q-hat^T on tcgen05 kind::mxf4nvf4 straight from the
+//    cache's NVFP4 data (the query heads of the KV head are the MMA's N = 16
+//    columns), S = acc * g_q * g_k * scaling written per key, and each row's
+//    maximum folded into an order-free atomic maximum;
 //  * pv: a ring of V (a TMA tile of 128 channels x 256 keys), S and g_v;
 //    the exact row max, e = exp2((S - m) log2 e), the NVFP4 fake-quant of e
 //    per 16 keys (as the prefill kernel does), then O-partial^T =
@@ -53,15 +52,7 @@ namespace {
 constexpr int DK_KEYS = 256;  // keys per work item
 constexpr int DK_MAXG = 16;   // query heads per KV head
 constexpr int DK_D = 128;     // head dim
-constexpr int DK_WARPS = 8;   // consumer warps (plus one producer warp)
-constexpr int DK_THREADS = (DK_WARPS + 1) * 32;
 
-// scores stage: K codes | K scales | g_k
-constexpr uint32_t SC_KC = DK_KEYS * DK_D / 2;
-constexpr uint32_t SC_KS = DK_KEYS * DK_D / 16;
-constexpr uint32_t SC_KG = DK_KEYS * 4;
-constexpr uint32_t SC_STAGE = SC_KC + SC_KS + SC_KG;
-constexpr int SC_STAGES = 3;
 struct DecodeArgs {
   const uint8_t* q_codes;   // [B][Hq*D/2]
   const uint8_t* q_scales;  // [B][Hq*D/16]
@@ -97,23 +88,13 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 // order-preserving float maximum on the bit pattern (exact, order-free)
 __device__ __forceinline__ void atomic_max_f32(unsigned int* a, float v) {
   if (!(v < 0.0f)) atomicMax(reinterpret_cast<int*>(a), __float_as_int(v));
   else atomicMin(a, __float_as_uint(v));
 }
-// named barrier 1 over the NW consumer warps (the producer warp is not in it)
-template <int NW = DK_WARPS>
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"r"(NW * 32) : "memory"); }
-// consumers_sync that also ANDs a flag over the consumer threads (every warp sees the same answer)
-template <int NW = DK_WARPS>
+// Named barrier 1 over NW warps that also ANDs a flag over their threads (every warp sees the same answer)
+template <int NW>
 __device__ __forceinline__ bool consumers_all(bool ok) {
   uint32_t r;
   asm volatile(
@@ -155,113 +136,221 @@ __device__ __forceinline__ void produce(uint64_t* full, uint64_t* empty, uint8_t
 }
 
 // ---------------------------------------------------------------- scores
-// Lane (r, q) of a warp: key r of the warp's group of 8; the MMA's K index
-// is permuted so that lane q's B values for chunk c (k = 2q, 2q+1, 2q+8,
-// 2q+9) are dims 32q + 4c + 0..3: its code bytes of a key are one contiguous
-// run (bytes 16q..16q+15) and its scales two bytes (2q, 2q+1).  The A
-// fragment uses the same permutation, so the dot product is unchanged.
-__global__ void __launch_bounds__(DK_THREADS) decode_scores_kernel(DecodeArgs p) {
-  extern __shared__ __align__(128) uint8_t ring[];
-  __shared__ __align__(8) uint64_t full[SC_STAGES], empty[SC_STAGES];
+// S^T[key][head] = K-hat Q-hat^T on tcgen05 kind::mxf4nvf4 (E2M1 codes and
+// E4M3 block scales straight from the cache, fp32 accumulate in TMEM), one
+// 256-key item = two 128-key tiles per MMA pair:
+//  * warp 0 streams an item's K codes (TMA, 64-byte swizzle: the rows are
+//    the MMA's A operand as stored) and its E4M3 scales into a ring;
+//  * warp 1 writes the KV head's query rows (B operand, N = 16: heads >= G
+//    zero) and their scale atoms when the KV head changes, turns each item's
+//    scales into the tcgen05 atom layout (row r at (r % 32) * 16 +
+//    (r / 32) * 4), and one lane issues the copies and MMAs into one of four
+//    accumulators;
+//  * warps 2-5, a TMEM lane (key) per thread: S = acc * g_q * g_k * scaling
+//    (keys past len -inf), written with 32 consecutive keys per warp store,
+//    and each head's running maximum, folded into the order-free atomic row
+//    maximum when the KV head changes.
+namespace dsc {
+constexpr int NS = 4, NACC = 4;
+constexpr int THREADS = 6 * 32;
+constexpr uint32_t KC = DK_KEYS * DK_D / 2;   // codes: 256 rows x 64 B
+constexpr uint32_t KS = DK_KEYS * DK_D / 16;  // scales: 256 rows x 8 B
+constexpr uint32_t STAGE = KC + KS;
+constexpr uint32_t OFF_ATOM = NS * STAGE;           // [NACC][tile][kk] atoms of 512 B
+constexpr uint32_t OFF_Q = OFF_ATOM + NACC * 2048;  // 16 query rows x 64 B, 64-byte swizzle
+constexpr uint32_t OFF_QSF = OFF_Q + 1024;          // [kk] query scale atoms
+constexpr uint32_t SMEM = OFF_QSF + 1024 + 1024;    // + alignment slack
+constexpr uint32_t T_SFA = 32 * NACC, T_SFB = T_SFA + 16 * NACC, TMEM_COLS = 256;
+static_assert(STAGE % 1024 == 0 && T_SFB + 8 <= TMEM_COLS, "layout");
+}  // namespace dsc
+
+template <int MG>
+__global__ void __launch_bounds__(dsc::THREADS) decode_scores_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                     DecodeArgs p) {
+  using namespace dsc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[NS], empty[NS], acc_full[NACC], acc_free[NACC], qdrain, drained;
+  __shared__ uint32_t tslot;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int G = p.Hq / p.Hkv;
   int i0, i1;
   item_range(p.nsplit * p.B * p.Hkv, i0, i1);
+  const int n_items = i1 - i0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SC_STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], DK_WARPS);
+    for (int s = 0; s < NS; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 1);
+    for (int i = 0; i < NACC; ++i) mbar_init(&acc_full[i], 1), mbar_init(&acc_free[i], 4);
+    mbar_init(&qdrain, 1), mbar_init(&drained, 1);
     fence_barrier_init();
   }
+  if (warp == 1) {
+    tmem_alloc(&tslot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
-  if (warp == DK_WARPS) {
-    if (lane == 0)
-      produce<SC_STAGES>(full, empty, ring, SC_STAGE, i0, i1, 0x401, [&](int item, uint8_t* st, uint64_t* bar) {
-        const int bk = item / p.nsplit, split = item % p.nsplit, b = bk / p.Hkv;
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      produce<NS>(full, empty, sm, STAGE, i0, i1, 0x401, [&](int item, uint8_t* st, uint64_t* bar) {
+        const int bk = item / p.nsplit, split = item % p.nsplit;
         const int64_t row = (int64_t)bk * p.Tmax + (int64_t)split * DK_KEYS;
-        mbar_arrive_expect_tx(bar, SC_STAGE);
-        bulk_load(st, p.k_codes + row * (DK_D / 2), SC_KC, bar);
-        bulk_load(st + SC_KC, p.k_scales + row * (DK_D / 16), SC_KS, bar);
-        bulk_load(st + SC_KC + SC_KS, p.k_g + (int64_t)b * p.Tmax + (int64_t)split * DK_KEYS, SC_KG, bar);
+        mbar_arrive_expect_tx(bar, STAGE);
+        tma_load_2d(st, &tmK, bar, 0, (int)row);
+        bulk_load(st + KC, p.k_scales + row * (DK_D / 16), KS, bar);
       });
-    return;
-  }
-  const int G = p.Hq / p.Hkv;
-  const int r = lane / 4, q = lane % 4;
-  const int ks = p.nsplit * DK_KEYS;
-  int cur = -1;
-  uint32_t afr[DK_D / 16][4];
-  float gq = 0.0f;
-  float mx[2] = {-INFINITY, -INFINITY};  // rows r, r+8
-  auto flush = [&](int bk) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
     }
-    const int64_t bh0 = (int64_t)(bk / p.Hkv) * p.Hq + (bk % p.Hkv) * G;
-    if (q == 0) {
-      if (r < G) atomic_max_f32(&p.mrow[bh0 + r], mx[0]);
-      if (r + 8 < G) atomic_max_f32(&p.mrow[bh0 + r + 8], mx[1]);
-    }
-  };
-  for (int it = 0; it < i1 - i0; ++it) {
-    const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
-    const int b = bk / p.Hkv, hk = bk % p.Hkv;
-    if (bk != cur) {
-      if (cur >= 0) flush(cur);
-      cur = bk;
-      mx[0] = mx[1] = -INFINITY;
-      gq = p.q_g[b];
-      // A: rows r, r+8 (query heads); k = 2q,2q+1 -> dims 32q+4c+0,1; k = 2q+8,2q+9 -> dims 32q+4c+2,3
-      const int64_t qel = ((int64_t)b * p.Hq + hk * G) * DK_D;
-#pragma unroll
-      for (int c = 0; c < DK_D / 16; ++c)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = r + (i & 1) * 8, dim = 32 * q + 4 * c + 2 * (i >> 1);
-          uint32_t v = 0;
-          if (row < G) {
-            const int64_t el = qel + row * DK_D + dim;
-            const uint32_t sb = p.q_scales[el / 16];
-            v = hmul2u(cvt_e2m1x2_f16x2(p.q_codes[el / 2]), cvt_e4m3x2_f16x2(sb | (sb << 8)));
-          }
-          afr[c][i] = v;
+  } else if (warp == 1) {
+    const uint32_t idesc = idesc_nvf4(128, 16);
+    uint8_t* qs = sm + OFF_Q;
+    uint8_t* qsf = sm + OFF_QSF;
+    int cur = -1, nq = 0;
+    bool ok = true;
+    for (int it = 0; it < n_items && ok; ++it) {
+      const int item = i0 + it, bk = item / p.nsplit;
+      const int s = it % NS, ai = it % NACC;
+      if (bk != cur) {
+        // a new KV head: every MMA issued so far reads the old query rows; let them finish first
+        if (cur >= 0) {
+          if (lane == 0) tc_commit(&qdrain);
+          ok = __all_sync(0xffffffffu, mbar_wait(&qdrain, nq & 1, 0x402));
+          ++nq;
+          if (!ok) break;
         }
-    }
-    const int s = it % SC_STAGES;
-    if (!mbar_wait(&full[s], (it / SC_STAGES) & 1, 0x402)) break;
-    const uint8_t* st = ring + (size_t)s * SC_STAGE;
-    const int64_t srow = ((int64_t)b * p.Hq + hk * G) * ks;
+        cur = bk;
+        const int b = bk / p.Hkv, hk = bk % p.Hkv;
+        // query rows n < G (heads hk G + n), zero above; chunk c of row n at n * 64 + (c ^ (n / 2 % 4)) * 16
 #pragma unroll
-    for (int gi = 0; gi < DK_KEYS / 8 / DK_WARPS; ++gi) {
-      const int kl = (warp + gi * DK_WARPS) * 8;  // first key of the group (in the item)
-      const uint4 cw = *reinterpret_cast<const uint4*>(st + (kl + r) * (DK_D / 2) + 16 * q);
-      const uint32_t sw = *reinterpret_cast<const uint16_t*>(st + SC_KC + (kl + r) * (DK_D / 16) + 2 * q);
-      const float2 kg = *reinterpret_cast<const float2*>(st + SC_KC + SC_KS + (kl + 2 * q) * 4);
-      const uint32_t s0 = cvt_e4m3x2_f16x2((sw & 0xFFu) * 0x101u), s1 = cvt_e4m3x2_f16x2((sw >> 8) * 0x101u);
-      const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int i = 0; i < 2; ++i) {
+          const int n = (lane + 32 * i) >> 2, c = lane & 3;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (n < G)
+            v = __ldg(reinterpret_cast<const uint4*>(p.q_codes + ((int64_t)b * p.Hq + hk * G + n) * (DK_D / 2)) + c);
+          *reinterpret_cast<uint4*>(qs + n * 64 + ((c ^ ((n >> 1) & 3)) << 4)) = v;
+        }
+        // scale atoms of the query rows: row n, blocks 4 kk .. 4 kk + 3 at n * 16 in atom kk
 #pragma unroll
-      for (int c = 0; c < DK_D / 16; ++c) {
-        // dims 32q + 4c + 0..3 = bytes 2c, 2c+1 of the lane's run (block 2q + c/4)
-        const uint32_t w = words[c / 2] >> (16 * (c & 1));
-        const uint32_t sc = c < 4 ? s0 : s1;
-        mma16816(acc, afr[c], hmul2u(cvt_e2m1x2_f16x2(w & 0xFFu), sc),
-                 hmul2u(cvt_e2m1x2_f16x2((w >> 8) & 0xFFu), sc));
+        for (int i = 0; i < 2; ++i) reinterpret_cast<uint4*>(qsf)[lane + 32 * i] = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+        if (lane < G) {
+          const uint2 sc = __ldg(reinterpret_cast<const uint2*>(p.q_scales + ((int64_t)b * p.Hq + hk * G + lane) * (DK_D / 16)));
+          reinterpret_cast<uint32_t*>(qsf)[lane * 4] = sc.x;
+          reinterpret_cast<uint32_t*>(qsf + 512)[lane * 4] = sc.y;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          tc_fence_after();
+          tmem_cp_sf_atom(tmem + T_SFB, smem_desc(smem_u32(qsf), 16, 128, kSwizzleNone));
+          tmem_cp_sf_atom(tmem + T_SFB + 4, smem_desc(smem_u32(qsf + 512), 16, 128, kSwizzleNone));
+        }
       }
-      // acc: rows r (0,1) and r+8 (2,3); keys kl + 2q, +1
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / NS) & 1, 0x403));
+      if (ok && it >= NACC) ok = __all_sync(0xffffffffu, mbar_wait(&acc_free[ai], ((it - NACC) / NACC) & 1, 0x404));
+      if (!ok) break;
+      // the item's K scales into atoms: key r + 128 t, blocks 4 kk .. 4 kk + 3
+      const uint8_t* st = sm + (size_t)s * STAGE;
+      uint8_t* at = sm + OFF_ATOM + ai * 2048;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = r + (i >> 1) * 8, key = split * DK_KEYS + kl + 2 * q + (i & 1);
-        if (row >= G) continue;
-        float sv = -INFINITY;
-        if (key < p.len) sv = __fmul_rn(__fmul_rn(__fmul_rn(acc[i], gq), (i & 1) ? kg.y : kg.x), p.scaling);
-        p.S[srow + (int64_t)row * ks + key] = sv;
-        mx[i >> 1] = fmaxf(mx[i >> 1], sv);
+      for (int j = 0; j < 8; ++j) {
+        const int key = lane + 32 * j, t = key >> 7, r = key & 127;
+        const uint2 sc = *reinterpret_cast<const uint2*>(st + KC + key * 8);
+        const uint32_t off = (r & 31) * 16 + ((r >> 5) & 3) * 4;
+        *reinterpret_cast<uint32_t*>(at + t * 1024 + off) = sc.x;
+        *reinterpret_cast<uint32_t*>(at + t * 1024 + 512 + off) = sc.y;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        tc_fence_after();
+        const uint32_t sfa = tmem + T_SFA + 16 * ai;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tmem_cp_sf_atom(sfa + 4 * c, smem_desc(smem_u32(at + 512 * c), 16, 128, kSwizzleNone));
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk)
+            mma_nvf4(tmem + 32 * ai + 16 * t, smem_desc(smem_u32(st + t * 8192) + kk * 32, 16, 512, kSwizzle64B),
+                     smem_desc(smem_u32(qs) + kk * 32, 16, 512, kSwizzle64B), idesc, sfa + 8 * t + 4 * kk,
+                     tmem + T_SFB + 4 * kk, kk > 0 ? 1u : 0u);
+        tc_commit(&empty[s]);
+        tc_commit(&acc_full[ai]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      tc_commit(&drained);  // every copy and MMA issued completes before TMEM is released
+      mbar_drain(&drained, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ S, row maxima
+    const int quarter = warp & 3;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int64_t ks = (int64_t)p.nsplit * DK_KEYS;
+    int cur = -1;
+    int64_t bh0 = 0;
+    float gq = 0.0f;
+    float mx[MG];
+#pragma unroll
+    for (int h = 0; h < MG; ++h) mx[h] = -INFINITY;
+    auto flush = [&]() {
+#pragma unroll
+      for (int h = 0; h < MG; ++h) {
+        if (h >= G) break;
+        float v = mx[h];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) atomic_max_f32(&p.mrow[bh0 + h], v);
+        mx[h] = -INFINITY;
+      }
+    };
+    for (int it = 0; it < n_items; ++it) {
+      const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
+      const int b = bk / p.Hkv, hk = bk % p.Hkv, ai = it % NACC;
+      if (bk != cur) {
+        if (cur >= 0) flush();
+        cur = bk;
+        bh0 = (int64_t)b * p.Hq + hk * G;
+        gq = p.q_g[b];
+      }
+      const int k0 = split * DK_KEYS + quarter * 32 + lane;  // this lane's key of tile 0 (+128: tile 1)
+      const float gk0 = __ldg(p.k_g + (int64_t)b * p.Tmax + k0), gk1 = __ldg(p.k_g + (int64_t)b * p.Tmax + k0 + 128);
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[ai], (it / NACC) & 1, 0x405));
+      tc_fence_after();
+      if (!ok) break;
+      uint32_t r0[16], r1[16];
+      tmem_ld16(tmem + lane_base + 32 * ai, r0);
+      tmem_ld16(tmem + lane_base + 32 * ai + 16, r1);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[ai]);
+#pragma unroll
+      for (int h = 0; h < MG; ++h) {
+        if (h >= G) break;
+        float* srow = p.S + (bh0 + h) * ks;
+        const float s0 = k0 < p.len ? __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(r0[h]), gq), gk0), p.scaling)
+                                    : -INFINITY;
+        const float s1 = k0 + 128 < p.len
+                             ? __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(r1[h]), gq), gk1), p.scaling)
+                             : -INFINITY;
+        srow[k0] = s0;
+        srow[k0 + 128] = s1;
+        mx[h] = fmaxf(mx[h], fmaxf(s0, s1));
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (cur >= 0) flush();
   }
-  if (cur >= 0) flush(cur);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
 }
 
 // -------------------------------------------------------------------- pv
@@ -655,16 +744,20 @@ __global__ void __launch_bounds__(CB_GROUPS * 32) decode_combine_kernel(DecodeAr
   }
 }
 
-// Persistent grid: as many CTAs as are resident at once, at most one per item.
-int persistent_grid(const void* fn, uint32_t smem, int items, int threads = DK_THREADS) {
-  int dev = 0, sms = 148, per_sm = 1;
+template <int MG>
+int launch_scores(const DecodeArgs& a, int items, cudaStream_t st) {
+  // K codes: [B*Hkv*Tmax rows][64 B], boxes of 256 keys with the 64-byte swizzle of the MMA operand
+  CUtensorMap mk;
+  if (int e = encode_tiled_2d(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.k_codes, DK_D / 2,
+                              (uint64_t)a.B * a.Hkv * a.Tmax, DK_D / 2, DK_D / 2, DK_KEYS, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  if (int e = set_smem_attr((const void*)decode_scores_kernel<MG>, (int)dsc::SMEM)) return e;
+  // two CTAs per SM (shared memory allows no third), each holding 256 TMEM columns
+  int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
-  return std::min(items, sms * per_sm);
+  decode_scores_kernel<MG><<<std::min(items, 2 * sms), dsc::THREADS, dsc::SMEM, st>>>(mk, a);
+  return check_launch("decode_scores_kernel");
 }
 
 template <int MG>
@@ -738,12 +831,10 @@ extern "C" int fp4attn_decode_ex(const uint8_t* q_codes, const uint8_t* q_scales
   if (cudaMemsetAsync(mrow, 0xFF, bh * sizeof(unsigned int), st) != cudaSuccess)
     return set_error(FP4ATTN_ERR_CUDA, "memset: %s", cudaGetErrorString(cudaGetLastError()));
   const int items = nsplit * B * Hkv;
-  constexpr uint32_t sc_smem = SC_STAGES * SC_STAGE;
-  if (int e = set_smem_attr((const void*)decode_scores_kernel, (int)sc_smem)) return e;
-  decode_scores_kernel<<<persistent_grid((const void*)decode_scores_kernel, sc_smem, items), DK_THREADS, sc_smem,
-                         st>>>(a);
-  if (int e = check_launch("decode_scores_kernel")) return e;
   const int G = Hq / Hkv;
+  if (int e = G <= 4 ? launch_scores<4>(a, items, st) : G <= 8 ? launch_scores<8>(a, items, st)
+                                                          : launch_scores<16>(a, items, st))
+    return e;
   const int e = G <= 4 ? launch_pv<4>(a, items, st) : G <= 8 ? launch_pv<8>(a, items, st) : launch_pv<16>(a, items, st);
   if (e) return e;
   decode_combine_kernel<<<(unsigned)bh, CB_GROUPS * 32, 0, st>>>(a);

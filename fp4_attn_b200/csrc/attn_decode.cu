@@ -27,7 +27,7 @@
 //    columns), S = acc * g_q * g_k * scaling written per key, and each row's
 //    maximum folded into an order-free atomic maximum;
 //  * pv: a ring of V (a TMA tile of 128 channels x 256 keys), S and g_v;
-//    the exact row max, e = exp2((S - m) log2 e), the NVFP4 fake-quant of e
+//    the exact row max, e = exp2(S log2 e - m log2 e), the NVFP4 fake-quant of e
 //    per 16 keys (as the prefill kernel does), then O-partial^T =
 //    (code*scale)_v^T (P-hat * g_v)^T on tcgen05 kind::f16 with V-hat in
 //    TMEM (exact in fp16) and P-hat * g_v as fp16 hi + lo rows in shared
@@ -37,6 +37,7 @@
 
 #include <algorithm>
 
+#include "attn_softmax.cuh"
 #include "common.cuh"
 #include "fp4attn.h"
 #include "sm100.cuh"
@@ -73,15 +74,18 @@ struct DecodeArgs {
   float* out;          // [B][Hq][D]
 };
 
-__device__ __forceinline__ uint32_t cvt_e2m1x2_f16x2(uint32_t byte) {
-  uint32_t r;
-  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(r) : "r"(byte));
-  return r;
-}
 __device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint32_t two_bytes) {
   uint32_t r;
   asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(two_bytes));
   return r;
+}
+// Four E2M1 code pairs (the bytes of w, lowest first) as fp16 pairs.
+__device__ __forceinline__ void cvt4_e2m1x2_f16x2(uint32_t w, uint32_t* o) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w));
 }
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -370,9 +374,10 @@ __global__ void __launch_bounds__(dsc::THREADS) decode_scores_kernel(const __gri
 //    cannot be factored out, and hi + lo keep 22 significant bits; 2^E, one
 //    power of two per item, puts the largest value just below 2^15 and is
 //    taken back out of the partial exactly.  Eight P warps: a thread takes a
-//    key pair and every other query head; e = exp2((S - m) log2 e) and the
-//    NVFP4 fake-quant of e per 16 keys (block maximum over eight lanes), as
-//    the prefill kernel quantizes P.
+//    key pair and every other query head; e = exp2(S log2 e - m log2 e) and
+//    the NVFP4 fake-quant of e per 16 keys (block maximum over eight lanes),
+//    with the prefill kernel's arithmetic (packed fp32 pairs, ex2, the block
+//    scale's reciprocal by rcp).
 //  * one thread issues an item's 16 MMAs (M = 128 channels, N = 2 MG rounded
 //    up to 16, K = 16 keys) into one of two accumulators; the first four P
 //    warps write an item's partial, (hi + lo) 2^-E, while the next item's
@@ -415,7 +420,6 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
   __shared__ uint32_t tslot;
   __shared__ float lred[2][NPW][NH];
   __shared__ float gmx[2][NPW];
-  __shared__ float rcp_tab[128];  // correctly rounded 1/s of every non-negative E4M3 scale byte (0 -> 0)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int G = p.Hq / p.Hkv;
   int i0, i1;
@@ -430,10 +434,6 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
     }
     mbar_init(&drained, 1);
     fence_barrier_init();
-  }
-  if (threadIdx.x < 128) {
-    const float sv = e4m3_to_f32((uint8_t)threadIdx.x);
-    rcp_tab[threadIdx.x] = sv == 0.0f ? 0.0f : __frcp_rn(sv);
   }
   // B rows of heads >= G and rows >= 2 MG stay zero
   for (uint32_t i = threadIdx.x; i < 2 * C::PB / 16; i += THREADS)
@@ -519,8 +519,9 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
           const uint32_t w[4] = {cw[c].x, cw[c].y, cw[c].z, cw[c].w};
           uint32_t o[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            o[j] = hmul2u(cvt_e2m1x2_f16x2((w[j >> 2] >> (8 * (j & 3))) & 0xFFu), j < 8 ? s0 : s1);
+          for (int q = 0; q < 4; ++q) cvt4_e2m1x2_f16x2(w[q], o + 4 * q);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = hmul2u(o[j], j < 8 ? s0 : s1);
           tmem_st16(acol + 16 * c, o);
         }
       } else {
@@ -549,9 +550,9 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
           const uint32_t sw[8] = {sc[0].x, sc[0].y, sc[0].z, sc[0].w, sc[1].x, sc[1].y, sc[1].z, sc[1].w};
           uint32_t o[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            o[j] = hmul2u(cvt_e2m1x2_f16x2((w[j >> 2] >> (8 * (j & 3))) & 0xFFu),
-                          cvt_e4m3x2_f16x2((sw[j >> 1] >> (16 * (j & 1))) & 0xFFFFu));
+          for (int q = 0; q < 4; ++q) cvt4_e2m1x2_f16x2(w[q], o + 4 * q);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = hmul2u(o[j], cvt_e4m3x2_f16x2((sw[j >> 1] >> (16 * (j & 1))) & 0xFFFFu));
           tmem_st16(acol + 16 * c, o);
         }
       }
@@ -568,12 +569,13 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
     const int quarter = warp & 3;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float log2e = 1.4426950408889634f, r6 = __frcp_rn(6.0f);
+    const uint64_t l2e2 = pk2(log2e, log2e);
     // B word of keys (k0, k0 + 1): 64-key block, byte (k0 & 63) * 2 of the 128-byte row, chunk swizzled by row & 7
     const uint32_t kb_off = (uint32_t)(k0 >> 6) * C::KBLK, wb = (uint32_t)(k0 & 63) * 2;
     auto bword = [&](int row) { return kb_off + row * 128 + ((((wb >> 4) ^ (row & 7)) << 4) | (wb & 15)); };
-    float m[NH];
+    uint64_t nml2[NH];  // -m log2 e of the thread's heads, as pairs
 #pragma unroll
-    for (int j = 0; j < NH; ++j) m[j] = 0.0f;
+    for (int j = 0; j < NH; ++j) nml2[j] = pk2(0.0f, 0.0f);
     int cur = -1;
     int64_t prev_bh0 = 0;
     int prev_split = 0;
@@ -614,7 +616,10 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
         cur = bk;
 #pragma unroll
         for (int j = 0; j < NH; ++j)
-          if (hs + 2 * j < G) m[j] = __uint_as_float(p.mrow[bh0 + hs + 2 * j]);
+          if (hs + 2 * j < G) {
+            const float nm = -__fmul_rn(__uint_as_float(p.mrow[bh0 + hs + 2 * j]), log2e);
+            nml2[j] = pk2(nm, nm);
+          }
       }
       const int s = it % NS, par = it & 1;
       // a failed wait reads stale shared memory below; the P warps then leave together at consumers_all
@@ -625,16 +630,19 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
       const float2 gv2 = *reinterpret_cast<const float2*>(st + VC + VS16 + 8 * pair);
       const float gv0 = live0 ? gv2.x : 0.0f, gv1 = live1 ? gv2.y : 0.0f;
       const float* Ss = reinterpret_cast<const float*>(st + VC + VS16 + VG);
-      float e0[NH], e1[NH];
+      uint64_t ee[NH];  // (e of key k0, e of key k0 + 1) per head
 #pragma unroll
       for (int j = 0; j < NH; ++j) {
         const int h = hs + 2 * j;
-        e0[j] = e1[j] = 0.0f;
+        ee[j] = pk2(0.0f, 0.0f);
         if (h < G) {  // uniform over the warp
+          // e = exp2(S log2 e - m log2 e), as the prefill kernel computes it
           const float2 s2 = *reinterpret_cast<const float2*>(Ss + h * DK_KEYS + k0);
-          if (live0) e0[j] = exp2f(__fmul_rn(s2.x - m[j], log2e));
-          if (live1) e1[j] = exp2f(__fmul_rn(s2.y - m[j], log2e));
-          float l = e0[j] + e1[j];
+          float t0, t1;
+          upk2(fma2(pk2(s2.x, s2.y), l2e2, nml2[j]), t0, t1);
+          const float e0 = live0 ? ex2(t0) : 0.0f, e1 = live1 ? ex2(t1) : 0.0f;
+          ee[j] = pk2(e0, e1);
+          float l = e0 + e1;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
           if (lane == 0) lred[par][pw][j] = l;
@@ -664,20 +672,27 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
       // next consumers_all; every later wait then fails fast)
       if (it >= 2) mbar_wait(&b_free[par], ((it - 2) >> 1) & 1, 0x419);
       uint8_t* pb = sm + C::OFF_PB + par * C::PB;
+      // g_v 2^E of the two keys (exact: 2^E is a power of two); 0 past len
+      const uint64_t gu2 = pk2(__fmul_rn(gv0, up), __fmul_rn(gv1, up));
 #pragma unroll
       for (int j = 0; j < NH; ++j) {
         const int h = hs + 2 * j;
         if (h >= G) continue;  // uniform over the warp
-        float am = fmaxf(e0[j], e1[j]);  // block of 16 keys = 8 consecutive lanes
+        float e0, e1;
+        upk2(ee[j], e0, e1);
+        float am = fmaxf(e0, e1);  // block of 16 keys = 8 consecutive lanes
 #pragma unroll
         for (int o = 4; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-        const uint8_t sb = e4m3_satfinite(__fmul_rn(am, r6));  // e >= 0: sb < 0x80
-        const float sf = e4m3_to_f32(sb);
-        const float rs = rcp_tab[sb & 0x7F];
-        const uint32_t c2 = cvt_e2m1x2_f16x2(e2m1x2(__fmaf_rn(e0[j], rs, 0.0f), __fmaf_rn(e1[j], rs, 0.0f)));
-        const float2 cf = __half22float2(*reinterpret_cast<const __half2*>(&c2));
-        const float x0 = live0 ? __fmul_rn(__fmul_rn(__fmul_rn(cf.x, sf), gv0), up) : 0.0f;
-        const float x1 = live1 ? __fmul_rn(__fmul_rn(__fmul_rn(cf.y, sf), gv1), up) : 0.0f;
+        // the block's E4M3 scale (fp16 pair, exact) and its reciprocal by rcp, as the prefill kernel
+        const uint32_t s2 = e4m3_f16x2(e4m3_satfinite(__fmul_rn(am, r6)) & 127);
+        const float sv = __half2float(__ushort_as_half((unsigned short)(s2 & 0xFFFFu)));
+        float rs;
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rs) : "f"(sv));
+        rs = sv == 0.0f ? 0.0f : rs;
+        float x0, x1;
+        upk2(mul2(ee[j], pk2(rs, rs)), x0, x1);
+        const float2 ph = f16x2_to_f32(quant_pair_cvt(x0, x1, s2));  // P-hat = code * scale, exact
+        upk2(mul2(pk2(ph.x, ph.y), gu2), x0, x1);
         const __half2 hi = __floats2half2_rn(x0, x1);
         const float2 hf = __half22float2(hi);
         *reinterpret_cast<__half2*>(pb + bword(h)) = hi;

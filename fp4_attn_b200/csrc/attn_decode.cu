@@ -69,10 +69,25 @@ struct DecodeArgs {
   float scaling;
   float* S;            // [B*Hq][nsplit*DK_KEYS]
   float* opart;        // [B*Hq][nsplit][D]
-  float* lpart;        // [B*Hq][nsplit]
+  float* lpart;        // [B*Hq][nsplit][4]: l of a chunk in four parts
   unsigned int* mrow;  // [B*Hq] row maximum of S (float bits, atomic; 0xFFFFFFFF = none yet)
   float* out;          // [B][Hq][D]
 };
+
+// Position of a work item (chunk `split` of KV head hk of sequence b, bk = b * Hkv + hk), advanced
+// item by item without the integer divisions of recomputing it.
+struct ItemPos {
+  int bk, split, b, hk;
+  __device__ __forceinline__ ItemPos(int item, const DecodeArgs& p)
+      : bk(item / p.nsplit), split(item % p.nsplit), b(bk / p.Hkv), hk(bk % p.Hkv) {}
+  __device__ __forceinline__ void next(const DecodeArgs& p) {
+    if (++split == p.nsplit) {
+      split = 0, ++bk;
+      if (++hk == p.Hkv) hk = 0, ++b;
+    }
+  }
+};
+
 
 __device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint32_t two_bytes) {
   uint32_t r;
@@ -213,8 +228,9 @@ __global__ void __launch_bounds__(dsc::THREADS) decode_scores_kernel(const __gri
     uint8_t* qsf = sm + OFF_QSF;
     int cur = -1, nq = 0;
     bool ok = true;
-    for (int it = 0; it < n_items && ok; ++it) {
-      const int item = i0 + it, bk = item / p.nsplit;
+    ItemPos pos(i0, p);
+    for (int it = 0; it < n_items && ok; ++it, pos.next(p)) {
+      const int bk = pos.bk;
       const int s = it % NS, ai = it % NACC;
       if (bk != cur) {
         // a new KV head: every MMA issued so far reads the old query rows; let them finish first
@@ -225,7 +241,7 @@ __global__ void __launch_bounds__(dsc::THREADS) decode_scores_kernel(const __gri
           if (!ok) break;
         }
         cur = bk;
-        const int b = bk / p.Hkv, hk = bk % p.Hkv;
+        const int b = pos.b, hk = pos.hk;
         // query rows n < G (heads hk G + n), zero above; chunk c of row n at n * 64 + (c ^ (n / 2 % 4)) * 16
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -312,9 +328,9 @@ __global__ void __launch_bounds__(dsc::THREADS) decode_scores_kernel(const __gri
         mx[h] = -INFINITY;
       }
     };
-    for (int it = 0; it < n_items; ++it) {
-      const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
-      const int b = bk / p.Hkv, hk = bk % p.Hkv, ai = it % NACC;
+    ItemPos pos(i0, p);
+    for (int it = 0; it < n_items; ++it, pos.next(p)) {
+      const int bk = pos.bk, split = pos.split, b = pos.b, hk = pos.hk, ai = it % NACC;
       if (bk != cur) {
         if (cur >= 0) flush();
         cur = bk;
@@ -377,15 +393,16 @@ __global__ void __launch_bounds__(dsc::THREADS) decode_scores_kernel(const __gri
 //    key pair and every other query head; e = exp2(S log2 e - m log2 e) and
 //    the NVFP4 fake-quant of e per 16 keys (block maximum over eight lanes),
 //    with the prefill kernel's arithmetic (packed fp32 pairs, ex2, the block
-//    scale's reciprocal by rcp).
+//    scale's reciprocal by rcp).  Each P warp writes its own quarter of l
+//    (64 keys); no warp waits for another's bookkeeping.
 //  * one thread issues an item's 16 MMAs (M = 128 channels, N = 2 MG rounded
-//    up to 16, K = 16 keys) into one of two accumulators; the first four P
-//    warps write an item's partial, (hi + lo) 2^-E, while the next item's
-//    MMAs run.
+//    up to 16, K = 16 keys) into one of two accumulators; the first four
+//    converter warps write an item's partial, (hi + lo) 2^-E, after handing
+//    over the next item's V-hat.
 namespace dpv {
 constexpr int NS = 4;               // ring stages
-constexpr int CW0 = 2, NCW = 8;     // converter warps 2 .. 9
-constexpr int PW0 = 10, NPW = 8;    // P warps 10 .. 17 (10 .. 13 also write the partials)
+constexpr int CW0 = 2, NCW = 8;     // converter warps 2 .. 9 (2 .. 5 also write the partials)
+constexpr int PW0 = 10, NPW = 8;    // P warps 10 .. 17
 constexpr int THREADS = (PW0 + NPW) * 32;
 constexpr uint32_t VC = DK_KEYS * DK_D / 2;       // codes [128 channels][128 B]
 constexpr uint32_t VS16 = DK_D * (DK_KEYS / 16);  // group scales [128 channels][16]
@@ -418,8 +435,6 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
   __shared__ __align__(8) uint64_t full[NS], empty[NS], a_full[2], a_free[2], b_full[2], b_free[2], acc_full[2],
       acc_free[2], drained;
   __shared__ uint32_t tslot;
-  __shared__ float lred[2][NPW][NH];
-  __shared__ float gmx[2][NPW];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int G = p.Hq / p.Hkv;
   int i0, i1;
@@ -447,6 +462,21 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tslot;
+  // 2^E of an item: the largest g_v of its live keys, read by every warp that needs it (no cross-warp
+  // exchange); P-hat * g_v * 2^E < 2^15 (P-hat <= 1.03125 < 2, g_v < 2^(e+1))
+  auto item_exp = [&](const uint8_t* st, int nlive, float& up, float& down) {
+    const float4* gv = reinterpret_cast<const float4*>(st + VC + VS16) + 2 * lane;  // keys 8 lane .. 8 lane + 7
+    const float4 a = gv[0], b = gv[1];
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float g = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) g = 8 * lane + i < nlive ? fmaxf(g, v[i]) : g;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) g = fmaxf(g, __shfl_xor_sync(0xffffffffu, g, o));
+    int E = 0;
+    if (g > 0.0f) E = max(-100, min(100, 13 - (((__float_as_int(g) >> 23) & 0xFF) - 127)));
+    up = __int_as_float((E + 127) << 23), down = __int_as_float((127 - E) << 23);
+  };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
@@ -490,17 +520,53 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
       mbar_drain(&drained, 0);
     }
   } else if (warp < PW0) {
-    // ---------------------------------------------------------------- V-hat into TMEM
+    // ------------------------------------------------ V-hat into TMEM; partials (warps 2-5)
     const int quarter = warp & 3, half = (warp - CW0) >> 2;
+    const bool epi = half == 0;
     const int d = quarter * 32 + lane;  // channel == TMEM lane
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    for (int it = 0; it < n_items; ++it) {
-      const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
+    float prev_down = 1.0f;
+    // the partial of item i: (hi + lo) 2^-E of this lane's channel, while item i + 1's MMAs wait for their
+    // operands
+    auto epilogue = [&](int i, const ItemPos& q) {
+      const int a = i & 1, split = q.split;
+      const int64_t bh0 = (int64_t)q.b * p.Hq + q.hk * G;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a], (i >> 1) & 1, 0x417));
+      tc_fence_after();
+      if (ok) {
+        uint32_t r[32];
+        if constexpr (C::NP == 16) {
+          uint32_t r16[16];
+          tmem_ld16(tmem + lane_base + T_ACC + 32 * a, r16);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) r[c] = r16[c];
+        } else {
+          tmem_ld32(tmem + lane_base + T_ACC + 32 * a, r);
+          tmem_ld_wait();
+        }
+#pragma unroll
+        for (int h = 0; h < MG; ++h)
+          if (h < G)
+            p.opart[((bh0 + h) * p.nsplit + split) * DK_D + d] =
+                (__uint_as_float(r[h]) + __uint_as_float(r[MG + h])) * prev_down;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[a]);
+    };
+    ItemPos pos(i0, p), prev = pos;
+    int it = 0;
+    for (; it < n_items; ++it, prev = pos, pos.next(p)) {
+      const int bk = pos.bk, split = pos.split;
       const int s = it % NS, a = it & 1;
       if (!mbar_wait(&full[s], (it / NS) & 1, 0x415)) break;
       if (it >= 2 && !mbar_wait(&a_free[a], ((it - 2) >> 1) & 1, 0x416)) break;
       tc_fence_after();
       const uint8_t* st = sm + (size_t)s * C::STAGE;
+      const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
+      float up, down;
+      if (epi) item_exp(st, nlive, up, down);
       uint4 cw[4];  // this half's 64 code bytes: logical 16-byte chunks 4 half .. 4 half + 3 of the row
 #pragma unroll
       for (int c = 0; c < 4; ++c)
@@ -526,7 +592,6 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
         }
       } else {
         // per-element scales from the cache (L2); keys past len read scale 0, so V-hat is 0 there
-        const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
         const uint8_t* vs = p.v_scales + ((int64_t)bk * DK_D + d) * p.Tmax + (int64_t)split * DK_KEYS + 128 * half;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -560,14 +625,16 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[a]);
+      if (epi) {
+        if (it >= 1) epilogue(it - 1, prev);
+        prev_down = down;
+      }
     }
+    if (epi && it >= 1) epilogue(it - 1, prev);
   } else {
-    // ---------------------------------------------------------------- P-hat, l, partials
+    // ---------------------------------------------------------------- P-hat and l
     const int pt = threadIdx.x - PW0 * 32;
-    const int pw = pt >> 5, hs = pt >> 7, pair = pt & 127, k0 = 2 * pair;
-    const bool epi = warp < PW0 + 4;
-    const int quarter = warp & 3;
-    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int hs = pt >> 7, pair = pt & 127, k0 = 2 * pair;
     const float log2e = 1.4426950408889634f, r6 = __frcp_rn(6.0f);
     const uint64_t l2e2 = pk2(log2e, log2e);
     // B word of keys (k0, k0 + 1): 64-key block, byte (k0 & 63) * 2 of the 128-byte row, chunk swizzled by row & 7
@@ -577,40 +644,9 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
 #pragma unroll
     for (int j = 0; j < NH; ++j) nml2[j] = pk2(0.0f, 0.0f);
     int cur = -1;
-    int64_t prev_bh0 = 0;
-    int prev_split = 0;
-    float prev_down = 1.0f;
-    auto epilogue = [&](int i) {
-      const int a = i & 1;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a], (i >> 1) & 1, 0x417));
-      tc_fence_after();
-      if (ok) {
-        uint32_t r[32];
-        if constexpr (C::NP == 16) {
-          uint32_t r16[16];
-          tmem_ld16(tmem + lane_base + T_ACC + 32 * a, r16);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) r[c] = r16[c];
-        } else {
-          tmem_ld32(tmem + lane_base + T_ACC + 32 * a, r);
-          tmem_ld_wait();
-        }
-        const int d = quarter * 32 + lane;
-#pragma unroll
-        for (int h = 0; h < MG; ++h)
-          if (h < G)
-            p.opart[((prev_bh0 + h) * p.nsplit + prev_split) * DK_D + d] =
-                (__uint_as_float(r[h]) + __uint_as_float(r[MG + h])) * prev_down;
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_free[a]);
-    };
-    int it = 0;
-    for (; it < n_items; ++it) {
-      const int item = i0 + it, bk = item / p.nsplit, split = item % p.nsplit;
-      const int b = bk / p.Hkv, hk = bk % p.Hkv;
+    ItemPos pos(i0, p);
+    for (int it = 0; it < n_items; ++it, pos.next(p)) {
+      const int bk = pos.bk, split = pos.split, b = pos.b, hk = pos.hk;
       const int64_t bh0 = (int64_t)b * p.Hq + hk * G;
       if (bk != cur) {
         cur = bk;
@@ -622,13 +658,15 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
           }
       }
       const int s = it % NS, par = it & 1;
-      // a failed wait reads stale shared memory below; the P warps then leave together at consumers_all
-      bool ok = mbar_wait(&full[s], (it / NS) & 1, 0x418);
+      if (!mbar_wait(&full[s], (it / NS) & 1, 0x418)) break;
       const uint8_t* st = sm + (size_t)s * C::STAGE;
       const int nlive = min(DK_KEYS, p.len - split * DK_KEYS);
       const bool live0 = k0 < nlive, live1 = k0 + 1 < nlive;
+      float up, down;
+      item_exp(st, nlive, up, down);
       const float2 gv2 = *reinterpret_cast<const float2*>(st + VC + VS16 + 8 * pair);
-      const float gv0 = live0 ? gv2.x : 0.0f, gv1 = live1 ? gv2.y : 0.0f;
+      // g_v 2^E of the two keys (exact: 2^E is a power of two); 0 past len
+      const uint64_t gu2 = pk2(live0 ? __fmul_rn(gv2.x, up) : 0.0f, live1 ? __fmul_rn(gv2.y, up) : 0.0f);
       const float* Ss = reinterpret_cast<const float*>(st + VC + VS16 + VG);
       uint64_t ee[NH];  // (e of key k0, e of key k0 + 1) per head
 #pragma unroll
@@ -642,38 +680,18 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
           upk2(fma2(pk2(s2.x, s2.y), l2e2, nml2[j]), t0, t1);
           const float e0 = live0 ? ex2(t0) : 0.0f, e1 = live1 ? ex2(t1) : 0.0f;
           ee[j] = pk2(e0, e1);
+          // this warp's share of l (its 64 keys), one of four per head and chunk
           float l = e0 + e1;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-          if (lane == 0) lred[par][pw][j] = l;
+          if (lane == 0) p.lpart[((bh0 + h) * p.nsplit + split) * 4 + (pair >> 5)] = l;
         }
       }
-      float gmax = fmaxf(gv0, gv1);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, o));
-      if (lane == 0) gmx[par][pw] = gmax;
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // S and g_v are in registers
-      if (!consumers_all<NPW>(ok)) break;     // also publishes lred and gmx
-      float gall = gmx[par][0];
-#pragma unroll
-      for (int w = 1; w < NPW; ++w) gall = fmaxf(gall, gmx[par][w]);
-      // 2^E with P-hat * g_v * 2^E < 2^15 (P-hat <= 1.03125 < 2, g_v < 2^(e+1))
-      int E = 0;
-      if (gall > 0.0f) E = max(-100, min(100, 13 - (((__float_as_int(gall) >> 23) & 0xFF) - 127)));
-      const float up = __int_as_float((E + 127) << 23), down = __int_as_float((127 - E) << 23);
-      if (pt < G) {
-        // l of head pt: the four warps of its head parity, slot pt / 2
-        const int w0 = (pt & 1) * 4, j = pt >> 1;
-        p.lpart[(bh0 + pt) * p.nsplit + split] =
-            (lred[par][w0][j] + lred[par][w0 + 1][j]) + (lred[par][w0 + 2][j] + lred[par][w0 + 3][j]);
-      }
-      // the B buffer is free once the MMAs of item it - 2 have read it (a failed wait is caught at the
-      // next consumers_all; every later wait then fails fast)
-      if (it >= 2) mbar_wait(&b_free[par], ((it - 2) >> 1) & 1, 0x419);
+      // the B buffer is free once the MMAs of item it - 2 have read it
+      if (it >= 2 && !mbar_wait(&b_free[par], ((it - 2) >> 1) & 1, 0x419)) break;
       uint8_t* pb = sm + C::OFF_PB + par * C::PB;
-      // g_v 2^E of the two keys (exact: 2^E is a power of two); 0 past len
-      const uint64_t gu2 = pk2(__fmul_rn(gv0, up), __fmul_rn(gv1, up));
 #pragma unroll
       for (int j = 0; j < NH; ++j) {
         const int h = hs + 2 * j;
@@ -701,11 +719,7 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&b_full[par]);
-      // the previous item's partial, while this item's V-hat and MMAs proceed
-      if (epi && it >= 1) epilogue(it - 1);
-      prev_bh0 = bh0, prev_split = split, prev_down = down;
     }
-    if (epi && it >= 1) epilogue(it - 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -725,7 +739,7 @@ __global__ void __launch_bounds__(CB_GROUPS * 32) decode_combine_kernel(DecodeAr
   __shared__ float lsum[CB_GROUPS];
   const int bh = blockIdx.x, r = threadIdx.x / 32, lane = threadIdx.x % 32;
   const float4* op = reinterpret_cast<const float4*>(p.opart + (int64_t)bh * p.nsplit * DK_D) + lane;
-  const float* lp = p.lpart + (int64_t)bh * p.nsplit;
+  const float4* lp = reinterpret_cast<const float4*>(p.lpart) + (int64_t)bh * p.nsplit;  // four parts per chunk
   float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   float l = 0.0f;
   int s = r;
@@ -736,13 +750,19 @@ __global__ void __launch_bounds__(CB_GROUPS * 32) decode_combine_kernel(DecodeAr
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       o.x += v[u].x, o.y += v[u].y, o.z += v[u].z, o.w += v[u].w;
-      if (lane == 0) l += lp[s + u * CB_GROUPS];
+      if (lane == 0) {
+        const float4 q = lp[s + u * CB_GROUPS];
+        l += (q.x + q.y) + (q.z + q.w);
+      }
     }
   }
   for (; s < p.nsplit; s += CB_GROUPS) {
     const float4 v = op[(int64_t)s * (DK_D / 4)];
     o.x += v.x, o.y += v.y, o.z += v.z, o.w += v.w;
-    if (lane == 0) l += lp[s];
+    if (lane == 0) {
+      const float4 q = lp[s];
+      l += (q.x + q.y) + (q.z + q.w);
+    }
   }
   osum[r][lane] = o;
   if (lane == 0) lsum[r] = l;
@@ -807,7 +827,7 @@ extern "C" int64_t fp4attn_decode_workspace_size(int B, int Hq, int len) {
   if (B <= 0 || Hq <= 0 || len <= 0) return -1;
   const int64_t nsplit = (len + DK_KEYS - 1) / DK_KEYS;
   const int64_t bh = (int64_t)B * Hq;
-  return (bh * nsplit * DK_KEYS + bh * nsplit * (DK_D + 1) + bh) * (int64_t)sizeof(float);
+  return (bh * nsplit * DK_KEYS + bh * nsplit * (DK_D + 4) + bh) * (int64_t)sizeof(float);
 }
 
 extern "C" int fp4attn_decode_ex(const uint8_t* q_codes, const uint8_t* q_scales, const float* q_g,
@@ -838,7 +858,7 @@ extern "C" int fp4attn_decode_ex(const uint8_t* q_codes, const uint8_t* q_scales
   float* S = static_cast<float*>(workspace);
   float* opart = S + bh * nsplit * DK_KEYS;
   float* lpart = opart + bh * nsplit * DK_D;
-  unsigned int* mrow = reinterpret_cast<unsigned int*>(lpart + bh * nsplit);
+  unsigned int* mrow = reinterpret_cast<unsigned int*>(lpart + bh * nsplit * 4);
   DecodeArgs a{q_codes, q_scales, q_g,    k_codes, k_scales, k_g,  v_codes, v_scales,
                v_g,     v_scales16, B,   Hq,      Hkv,      len,  Tmax,    nsplit,
                len16 / DK_KEYS, scaling, S, opart, lpart, mrow, out};

@@ -100,7 +100,7 @@ def test_decode_argument_errors():
     B, Hq, Hkv, D, len_ = 2, 32, 8, 128, 300
     need = L.fp4attn_decode_workspace_size(B, Hq, len_)
     nsplit = (len_ + 255) // 256
-    assert need == (B * Hq * nsplit * 256 + B * Hq * nsplit * (D + 1) + B * Hq) * 4
+    assert need == (B * Hq * nsplit * 256 + B * Hq * nsplit * (D + 4) + B * Hq) * 4
     p = ctypes.c_void_p(256)
 
     def call(ptr=p, Hq=Hq, Hkv=Hkv, D=D, len_=len_, Tmax=512, ws_bytes=need, ws=p):

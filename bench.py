@@ -90,6 +90,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=10,
                     help="weights workload: layers per rank (10 = the 80-layer stack at 8 ranks)")
+    ap.add_argument("--decode-batch", type=int, default=8,
+                    help="decode workload: sequences per rank (8 = the headline case; profiles capture 4)")
     return ap.parse_args()
 
 
@@ -713,12 +715,12 @@ class DecodeWorkload:
         # per (token, KV head): K codes 64 B + K scales 8 B + V codes 64 B + V scales 8 B (one per
         # 16-token group: the appends are whole groups); per token: g_k, g_v
         self.cache_bytes = self.B * self.Hkv * self.T * (64 + 8 + 64 + 8) + 2 * self.B * self.T * 4
-        self.config = {"workload": "NVFP4 KV-cache decode: B=8, Hq=32, Hkv=8, D=128, 32768 cached tokens "
+        self.config = {"workload": f"NVFP4 KV-cache decode: B={self.B}, Hq=32, Hkv=8, D=128, 32768 cached tokens "
                                    "(appended in calls of 4096, so V scales are read per 16-token group), "
                                    "one new query token per sequence",
                        "cache_bytes": self.cache_bytes, "global_batch": world * self.B,
-                       "shard": "batch rows 8r..8r+7 on rank r (own cache, seed 2 + r)",
-                       "l2": "cache bytes read 304 MB > L2"}
+                       "shard": f"batch rows {self.B}r..{self.B}r+{self.B - 1} on rank r (own cache, seed 2 + r)",
+                       "l2": f"cache bytes read {self.cache_bytes / 1e6:.0f} MB > L2"}
         if cpu_only:
             return
         from fp4_attn_b200 import _lib
@@ -1423,6 +1425,7 @@ def make_workload(name, dev, cpu_only=False, rank=0, world=1, layers=10):
 
 def main():
     args = parse()
+    DecodeWorkload.B = args.decode_batch
     if args.impl == "reference":
         # CPU only: rank 0 runs and prints, other ranks exit without work.
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -730,10 +730,10 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
 }
 
 // O = sum over chunks of O-partial / sum of l.  One CTA per (b, query head):
-// group r of 32 threads sums chunks r, r + 8, r + 16, ... (4 dims per thread,
+// group r of 32 threads sums chunks r, r + 16, r + 32, ... (4 dims per thread,
 // 16-byte loads, every load of the group issued before the adds), then the
-// eight group sums are added in a fixed order.
-constexpr int CB_GROUPS = 8;
+// sixteen group sums are added in a fixed order.
+constexpr int CB_GROUPS = 16;
 __global__ void __launch_bounds__(CB_GROUPS * 32) decode_combine_kernel(DecodeArgs p) {
   __shared__ float4 osum[CB_GROUPS][DK_D / 4];
   __shared__ float lsum[CB_GROUPS];
@@ -773,8 +773,15 @@ __global__ void __launch_bounds__(CB_GROUPS * 32) decode_combine_kernel(DecodeAr
     float v[CB_GROUPS];
 #pragma unroll
     for (int g = 0; g < CB_GROUPS; ++g) v[g] = os[g * DK_D + d];
-    const float on = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-    const float ln = ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3])) + ((lsum[4] + lsum[5]) + (lsum[6] + lsum[7]));
+    float l[CB_GROUPS];
+#pragma unroll
+    for (int g = 0; g < CB_GROUPS; ++g) l[g] = lsum[g];
+    // pairwise, in a fixed order
+#pragma unroll
+    for (int sp = 1; sp < CB_GROUPS; sp *= 2)
+#pragma unroll
+      for (int g = 0; g < CB_GROUPS; g += 2 * sp) v[g] += v[g + sp], l[g] += l[g + sp];
+    const float on = v[0], ln = l[0];
     p.out[(int64_t)bh * DK_D + d] = on / ln;
   }
 }

@@ -468,9 +468,13 @@ __global__ void __launch_bounds__(dpv::THREADS, 1)
     const float4* gv = reinterpret_cast<const float4*>(st + VC + VS16) + 2 * lane;  // keys 8 lane .. 8 lane + 7
     const float4 a = gv[0], b = gv[1];
     const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    float g = 0.0f;
+    float g = 0.0f;  // g_v >= 0
+    if (nlive >= DK_KEYS) {
+      g = fmaxf(max3f(v[0], v[1], v[2]), max3f(v[3], v[4], max3f(v[5], v[6], v[7])));
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) g = 8 * lane + i < nlive ? fmaxf(g, v[i]) : g;
+      for (int i = 0; i < 8; ++i) g = 8 * lane + i < nlive ? fmaxf(g, v[i]) : g;
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) g = fmaxf(g, __shfl_xor_sync(0xffffffffu, g, o));
     int E = 0;
